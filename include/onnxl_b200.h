@@ -1,0 +1,198 @@
+/*
+ * onnxl_b200 — C ABI of the B200 (sm_100a) kernels for onnx-light's
+ * quantized-inference path.
+ *
+ * Every entry point replaces one onnx-light CPU kernel's operator() (cited
+ * beside it, paths relative to the onnx-light source tree) and keeps its
+ * argument meaning, accepted dtypes and validation.  Where the reference
+ * throws std::invalid_argument (EXT_ENFORCE_INVALID), these return a negative
+ * status and b2_last_error() holds a message with the same "kernel::<Op>:"
+ * prefix.
+ *
+ * Conventions
+ *  - Tensors are contiguous row-major device buffers (b2_tensor.data is a
+ *    device address).  Sub-byte types (INT4, UINT4, FLOAT4E2M1, INT2, UINT2)
+ *    are packed low-order-first, as in onnx-light's Tensor storage
+ *    (onnx_light/onnx_core/runtime/kernels/cast_sub_byte.h:48-60).
+ *  - dtype is the ONNX TensorProto.DataType code.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *    stream-ordered and never synchronize the host.
+ *  - Nothing is allocated inside.  Entry points that need scratch take
+ *    (workspace, workspace_bytes): with workspace == NULL the required size is
+ *    written to *workspace_bytes and nothing runs; otherwise *workspace_bytes is
+ *    the capacity offered.  A workspace must be zero-filled once before its
+ *    first use; every call leaves the arrival counters it used at zero again,
+ *    so the same buffer serves any later call on the same stream.  Calls that
+ *    share one workspace must not overlap on the GPU.
+ *  - No CPU fallback: every accepted call runs on the GPU or fails.
+ */
+#ifndef ONNXL_B200_H
+#define ONNXL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2_API __attribute__((visibility("default")))
+#else
+#define B2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define B2_OK 0
+#define B2_ERR_INVALID_ARGUMENT -1  /* reference: std::invalid_argument */
+#define B2_ERR_UNSUPPORTED_DTYPE -2 /* reference: "unsupported data type" invalid_argument */
+#define B2_ERR_CUDA -3              /* a CUDA runtime call failed */
+#define B2_ERR_WORKSPACE -4         /* workspace smaller than required */
+#define B2_ERR_TIMEOUT -5           /* a bounded device-side wait gave up */
+#define B2_ERR_UNSUPPORTED -6       /* valid for the reference, not handled on the GPU */
+
+typedef struct b2_tensor {
+  void *data;           /* device address (NULL allowed when the tensor has no elements) */
+  int32_t dtype;        /* ONNX TensorProto.DataType */
+  int32_t ndim;         /* 0 for a scalar */
+  const int64_t *shape; /* ndim entries (may be NULL when ndim == 0) */
+} b2_tensor;
+
+/* Library identification, e.g. "onnxl_b200 0.1 sm_100a". */
+B2_API const char *b2_version(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len) and returns the status it belonged to. */
+B2_API int b2_last_error(char *buf, size_t len);
+
+/*
+ * DequantizeLinear: y = (x - x_zero_point) * x_scale, bit-exact with the
+ * reference.
+ * Replaces kernel::DequantizeLinear::operator()(x, x_scale, x_zero_point,
+ * axis, output, rt) (kernel_dequantizelinear.cc:522-651) and, with
+ * x_zero_point == NULL, operator()(x, x_scale, axis, output, rt) (:670-693).
+ *  x: UINT8, INT8, UINT16, INT16, INT32, FLOAT8E4M3FN, FLOAT8E4M3FNUZ,
+ *     FLOAT8E5M2, FLOAT8E5M2FNUZ, UINT4, INT4, UINT2, INT2, FLOAT4E2M1,
+ *     FLOAT6E2M3, FLOAT6E3M2.
+ *  x_scale: FLOAT or FLOAT16; one element -> per-tensor; rank(x) -> blocked
+ *     along `axis` (block = x.shape[axis] / x_scale.shape[axis]); otherwise
+ *     per-axis with x.shape[axis] elements.
+ *  y: dtype == x_scale dtype, shape == x shape.
+ *  axis: must already be non-negative, as the reference requires (:539-540).
+ */
+B2_API int b2_dequantize_linear(const b2_tensor *x, const b2_tensor *x_scale,
+                         const b2_tensor *x_zero_point, int64_t axis, b2_tensor *y,
+                         void *stream);
+
+/*
+ * Fused DequantizeLinear -> [Cast] -> MatMul with the quantized operand on the
+ * right: y = a @ cast(dequantize(w, w_scale, w_zero_point, axis)).
+ * Replaces the node pair kernel::DequantizeLinear (as above) feeding
+ * kernel::MatMul::operator()(a, b) (kernel_matmul.cc:181-223), optionally with
+ * an ONNX Cast between them.
+ *  a: FLOAT, FLOAT16 or BFLOAT16, rank >= 1 (NumPy MatMul broadcasting of the
+ *     leading dimensions against a rank-2 w).
+ *  w: rank-2 [K, N] quantized weight, any dtype b2_dequantize_linear takes.
+ *  cast_dtype: 0 when the dequantized weight feeds MatMul directly (its dtype
+ *     is then the scale dtype and must equal a's dtype, kernel_matmul.cc:182);
+ *     otherwise FLOAT, FLOAT16 or BFLOAT16 (RNE cast of the dequantized value,
+ *     onnx_light/onnx_core/runtime/kernels/cast_helper.cc:51-135), equal to a's dtype.
+ *  y: dtype of a; shape = MatMul output shape.
+ * Arithmetic: the dequantized weight is formed exactly as the reference does
+ * (fp32 (q-zp)*s, rounded to the node's output type), then multiplied with fp32
+ * accumulation; results agree with the reference within rel-L2 1e-3 for
+ * FLOAT16/BFLOAT16 and 1e-5 for FLOAT.
+ */
+B2_API int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w, const b2_tensor *w_scale,
+                         const b2_tensor *w_zero_point, int64_t axis, int32_t cast_dtype,
+                         b2_tensor *y, void *workspace, size_t *workspace_bytes, void *stream);
+
+/*
+ * MatMulInteger: y[i,j] = sum_k (a[i,k] - a_zp[i]) * (b[k,j] - b_zp[j]) in
+ * int32, bit-exact.
+ * Replaces kernel::MatMulInteger::operator()(a, b, a_zero_point, b_zero_point,
+ * output) (kernel_matmul_integer.cc:178-234).
+ *  a, b: INT8 or UINT8; zero points NULL (= 0), scalar, per-row [M] (a) or
+ *  per-column [N] (b); y: INT32.
+ */
+B2_API int b2_matmul_integer(const b2_tensor *a, const b2_tensor *b, const b2_tensor *a_zero_point,
+                      const b2_tensor *b_zero_point, b2_tensor *y, void *workspace,
+                      size_t *workspace_bytes, void *stream);
+
+/*
+ * QLinearMatMul: y = saturate(nearbyint(float(acc) * (a_s * b_s / y_s)) + y_zp),
+ * acc the exact integer dot product, bit-exact.
+ * Replaces kernel::QLinearMatMul::operator() (kernel_qlinearmatmul.cc:221-267).
+ * Scales: FLOAT or FLOAT16 scalars; zero points: scalars of a/b/y's dtype;
+ * y: INT8 or UINT8 (y_zero_point's dtype).
+ */
+B2_API int b2_qlinear_matmul(const b2_tensor *a, const b2_tensor *a_scale, const b2_tensor *a_zero_point,
+                      const b2_tensor *b, const b2_tensor *b_scale, const b2_tensor *b_zero_point,
+                      const b2_tensor *y_scale, const b2_tensor *y_zero_point, b2_tensor *y,
+                      void *workspace, size_t *workspace_bytes, void *stream);
+
+/* Attributes of the opset-23 Attention node (kernel_attention.cc:867-878). */
+typedef struct b2_attention_attrs {
+  int32_t has_scale;        /* 0: scale = 1/sqrt(head_size) */
+  float scale;
+  int32_t is_causal;
+  float softcap;            /* > 0: softcap * tanh(s / softcap) before the mask */
+  int32_t qk_matmul_output_mode; /* only 0 is accepted (no qk output on this path) */
+  int64_t q_num_heads;      /* rank-3 inputs only */
+  int64_t kv_num_heads;     /* rank-3 inputs only */
+  int64_t left_window_size; /* -1 = unbounded */
+  int64_t right_window_size;
+  /* Contiguous KV cache.  0: present_key/value are fresh [B,Hkv,past+new,D]
+   * buffers (the reference's ConcatAxis2 repack, kernel_attention.cc:313-339).
+   * > 0: past and present alias one capacity-reserved buffer
+   * [B, Hkv, kv_capacity, D]; past occupies positions [0, past_len) and the new
+   * keys/values are appended in place (ReservePersistentAppend,
+   * kernel_attention.cc:297-310). */
+  int64_t kv_capacity;
+} b2_attention_attrs;
+
+/*
+ * Attention (opset 23) with GQA and a contiguous KV cache.
+ * Replaces kernel::Attention::operator()(Q, K, V, attrs, attn_mask, past_key,
+ * past_value, nonpad_kv_seqlen = nullptr) (kernel_attention.cc:767-852).
+ *  q, k, v: FLOAT16 or BFLOAT16, rank 4 [B, H, S, D] or rank 3 [B, S, H*D].
+ *  attn_mask: NULL or FLOAT, rank 1-4, broadcast to [B, Hq, Sq, L].
+ *  past_key/past_value: NULL or rank-4 [B, Hkv, past_len, D] (shape), with
+ *    data pointing at the cache buffer (see kv_capacity).
+ *  present_key/present_value: rank-4 outputs [B, Hkv, past_len+S, D]; may be
+ *    NULL when no past is given and the caller does not want them.
+ *  y: same dtype as q; rank and layout of q.
+ */
+B2_API int b2_attention(const b2_tensor *q, const b2_tensor *k, const b2_tensor *v,
+                 const b2_tensor *attn_mask, const b2_tensor *past_key,
+                 const b2_tensor *past_value, const b2_attention_attrs *attrs, b2_tensor *y,
+                 b2_tensor *present_key, b2_tensor *present_value, void *workspace,
+                 size_t *workspace_bytes, void *stream);
+
+/*
+ * Seeded synthetic inputs, identical to onnx-light's SplitMix64 generators
+ * (onnx_light/onnx_core/runtime/kernels/random.cc:38-176), produced on the
+ * device so that benchmark inputs never cross PCIe.  Not part of the hot path.
+ *  kind 0: uniform  lo + u*(hi-lo)             -> out FLOAT
+ *  kind 1: normal   lo + (sum12(u)-6)*hi        -> out FLOAT   (lo = mean, hi = scale)
+ *  kind 2: integer  RandInt(lo, hi+1)           -> out INT64
+ * Returns B2_ERR_UNSUPPORTED if integer rejection sampling would be needed
+ * (never for spans that divide 2^64 or are small).
+ */
+B2_API int b2_synth_fill(int32_t kind, uint64_t seed, int64_t n, double lo, double hi, void *out,
+                  void *stream);
+
+/*
+ * Converts a device array: FLOAT -> FLOAT16/BFLOAT16 (RNE, reference NaN
+ * patterns), INT64 -> packed INT4/UINT4/INT2/UINT2/INT8/UINT8 (two's-complement
+ * truncation), FLOAT -> FLOAT8E4M3FN (saturating RNE).  Input-preparation
+ * helper for synthetic inputs; not part of the hot path.
+ */
+B2_API int b2_convert(const void *src, int32_t src_dtype, void *dst, int32_t dst_dtype, int64_t n,
+               void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ONNXL_B200_H */

@@ -1,0 +1,620 @@
+// Opset-23 Attention with GQA and a contiguous KV cache on sm_100a.
+//
+// Replaces kernel::Attention::operator() and ComputeAttentionRank4
+// (onnx_light/onnx_extensions/kernels/kernels/nn/kernel_attention.cc:427-691, 767-852).
+//
+// Data layout in HBM
+//  * KV cache: one buffer per K and V, [B, Hkv, capacity, D], the layout the
+//    reference's persistent append uses (kernel_attention.cc:297-310).  New
+//    tokens are appended in place by kv_append; with kv_capacity == 0 the
+//    present buffers are fresh [B, Hkv, past+new, D] tensors and the past is
+//    copied in first (the reference's ConcatAxis2 repack, :313-339).
+//  * Q / Y: rank-4 [B, H, S, D] or rank-3 [B, S, H*D], read and written through
+//    strides, so rank-3 inputs need no transpose pass (the reference repacks
+//    them, :179-248).
+//
+// attn_fwd: split-KV flash attention on CUDA cores.  One CTA owns one
+// (batch, kv_head) pair, up to 16 query rows of that group (the Hq/Hkv query
+// heads of a GQA group share every K/V byte read, :587) and a contiguous
+// range of keys.  K/V tiles of 32 keys stream through shared memory with
+// cp.async double buffering; each lane scores one key against all rows
+// (fp32), the online softmax (running max / sum) is kept per row, and for
+// P.V each lane owns D/32 output dims.  Splits write (m, l, o) partials; the
+// last CTA of a (b, kv_head, row-tile) merges them in split order.
+// The decode configuration is HBM-bound: bytes = K and V cache + Q + Y.
+#include "b2_common.cuh"
+
+namespace b2 {
+
+constexpr int ATT_THREADS = 128; // 4 warps
+constexpr int ATT_ROWS = 16;     // query rows per CTA
+constexpr int ATT_TK = 32;       // keys per tile (one per lane)
+constexpr int ATT_DMAX = 256; // largest head size handled
+
+struct AttParams {
+  const void *q;
+  const void *k; // present / key view
+  const void *v;
+  void *y;
+  const float *mask;
+  int64_t mask_shape[4];
+  int64_t B, Hq, Hkv, Sq, L, D;
+  int64_t q_sb, q_sh, q_ss; // strides (elements)
+  int64_t k_sb, k_sh, k_ss;
+  int64_t v_sb, v_sh, v_ss;
+  int64_t y_sb, y_sh, y_ss;
+  int64_t past_len;
+  float scale, softcap;
+  int causal;
+  int64_t left_window, right_window;
+  int group;      // Hq / Hkv
+  int rows_total; // group * Sq
+  int row_tiles;
+  int splits;
+  int64_t keys_per_split;
+  float *ws_o;    // [splits][B*Hkv*rows_total][D]
+  float *ws_ml;   // [splits][B*Hkv*rows_total][2]
+  uint32_t *counters;
+  int dt;
+};
+
+template <typename T> __device__ __forceinline__ float ld_act(const void *p, int64_t i);
+template <> __device__ __forceinline__ float ld_act<float>(const void *p, int64_t i) {
+  return reinterpret_cast<const float *>(p)[i];
+}
+template <> __device__ __forceinline__ float ld_act<__half>(const void *p, int64_t i) {
+  return __half2float(reinterpret_cast<const __half *>(p)[i]);
+}
+template <> __device__ __forceinline__ float ld_act<__nv_bfloat16>(const void *p, int64_t i) {
+  return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(p)[i] << 16);
+}
+template <typename T> __device__ __forceinline__ void st_act(void *p, int64_t i, float v);
+template <> __device__ __forceinline__ void st_act<float>(void *p, int64_t i, float v) {
+  reinterpret_cast<float *>(p)[i] = v;
+}
+template <> __device__ __forceinline__ void st_act<__half>(void *p, int64_t i, float v) {
+  reinterpret_cast<uint16_t *>(p)[i] = f32_to_f16_bits(v);
+}
+template <> __device__ __forceinline__ void st_act<__nv_bfloat16>(void *p, int64_t i, float v) {
+  reinterpret_cast<uint16_t *>(p)[i] = f32_to_bf16_bits(v);
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N));
+}
+
+// Mask bias of (b, h, i, j) (kernel_attention.cc:343-386, 583-606).
+__device__ __forceinline__ float att_bias(const AttParams &p, int64_t b, int64_t h, int64_t i,
+                                          int64_t j) {
+  float bias = 0.0f;
+  if (p.mask) {
+    if (j >= p.mask_shape[3]) {
+      bias = -INFINITY;
+    } else {
+      const int64_t idx[4] = {b, h, i, j};
+      int64_t lin = 0, st = 1;
+#pragma unroll
+      for (int k = 3; k >= 0; --k) {
+        lin += (p.mask_shape[k] == 1 ? 0 : idx[k]) * st;
+        st *= p.mask_shape[k];
+      }
+      bias = p.mask[lin];
+    }
+  }
+  if (p.causal && j > i + p.past_len) bias = -INFINITY;
+  const int64_t wd = i + p.past_len - j;
+  if ((p.left_window >= 0 && wd > p.left_window) || (p.right_window >= 0 && -wd > p.right_window))
+    bias = -INFINITY;
+  return bias;
+}
+
+template <typename T, int ROWS, int DPL>
+__global__ void __launch_bounds__(ATT_THREADS) attn_fwd(const AttParams p) {
+  extern __shared__ __align__(16) uint8_t att_smem[];
+  const int D = (int)p.D;
+  const int DP = D + 8; // padded row (elements) to spread shared-memory banks
+  T *ks = reinterpret_cast<T *>(att_smem);                  // [2][4 warps][32][DP]
+  T *vs = ks + 2 * 4 * ATT_TK * DP;                         // [2][4][32][DP]
+  float *qs = reinterpret_cast<float *>(vs + 2 * 4 * ATT_TK * DP); // [ROWS][D]
+  float *ps = qs + ROWS * D;                            // [4 warps][ROWS][32]
+  float *red = ps + 4 * ROWS * ATT_TK;                  // merge buffer
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int bh = blockIdx.x;
+  const int64_t b = bh / p.Hkv, kvh = bh % p.Hkv;
+  const int rt = blockIdx.z;
+  const int split = blockIdx.y;
+  const int row0 = rt * ROWS;
+  const int nrows = min(ROWS, p.rows_total - row0);
+
+  // Query rows: row r -> (head = kvh*group + r % group, query index r / group).
+  for (int e = threadIdx.x; e < ROWS * D; e += ATT_THREADS) {
+    const int r = e / D, d = e % D;
+    float val = 0.0f;
+    if (r < nrows) {
+      const int rr = row0 + r;
+      const int64_t h = kvh * p.group + rr % p.group, s = rr / p.group;
+      val = ld_act<T>(p.q, b * p.q_sb + h * p.q_sh + s * p.q_ss + d);
+    }
+    qs[e] = val;
+  }
+
+  const int64_t kbeg = (int64_t)split * p.keys_per_split;
+  const int64_t kend = min(p.L, kbeg + p.keys_per_split);
+  // Each warp walks its own interleaved sequence of 32-key tiles.
+  const int64_t ntiles = (kend - kbeg + ATT_TK - 1) / ATT_TK;
+  const T *kbase = reinterpret_cast<const T *>(p.k) + b * p.k_sb + kvh * p.k_sh;
+  const T *vbase = reinterpret_cast<const T *>(p.v) + b * p.v_sb + kvh * p.v_sh;
+  const int chunks = D * (int)sizeof(T) / 16; // 16-byte chunks per row
+
+  auto issue = [&](int64_t tile, int buf) {
+    T *kd = ks + (buf * 4 + warp) * ATT_TK * DP;
+    T *vd = vs + (buf * 4 + warp) * ATT_TK * DP;
+    const int64_t j0 = kbeg + tile * ATT_TK;
+    for (int e = lane; e < ATT_TK * chunks; e += 32) {
+      const int kk = e / chunks, c = e % chunks;
+      const int64_t j = j0 + kk;
+      if (j < kend) {
+        cp_async16(reinterpret_cast<uint8_t *>(kd + kk * DP) + 16 * c,
+                   reinterpret_cast<const uint8_t *>(kbase + j * p.k_ss) + 16 * c);
+        cp_async16(reinterpret_cast<uint8_t *>(vd + kk * DP) + 16 * c,
+                   reinterpret_cast<const uint8_t *>(vbase + j * p.v_ss) + 16 * c);
+      }
+    }
+  };
+
+  __syncthreads();
+  float m_run[ROWS], l_run[ROWS];
+  float acc[ROWS][DPL];
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    m_run[r] = -INFINITY;
+    l_run[r] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < DPL; ++t) acc[r][t] = 0.0f;
+  }
+  const int dpl = (D + 31) / 32; // output dims per lane
+
+  int64_t my_tile = warp;
+  if (my_tile < ntiles) issue(my_tile, 0);
+  cp_async_commit();
+  int buf = 0;
+  for (; my_tile < ntiles; my_tile += 4) {
+    const int64_t next = my_tile + 4;
+    if (next < ntiles) issue(next, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    const T *kt = ks + (buf * 4 + warp) * ATT_TK * DP;
+    const T *vt = vs + (buf * 4 + warp) * ATT_TK * DP;
+    const int64_t j = kbeg + my_tile * ATT_TK + lane;
+    const bool valid = j < kend;
+    // scores for this lane's key against every row
+    float sc[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) sc[r] = 0.0f;
+    if (valid) {
+      const T *krow = kt + lane * DP;
+      for (int d = 0; d < D; d += 8) {
+        float kv[8];
+        if (sizeof(T) == 2) {
+          const uint4 raw = *reinterpret_cast<const uint4 *>(krow + d);
+          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint16_t lo = (uint16_t)(w[t] & 0xffffu), hi = (uint16_t)(w[t] >> 16);
+            if (p.dt == kFloat16) {
+              kv[2 * t] = f16_bits_to_f32(lo);
+              kv[2 * t + 1] = f16_bits_to_f32(hi);
+            } else {
+              kv[2 * t] = __uint_as_float((uint32_t)lo << 16);
+              kv[2 * t + 1] = __uint_as_float((uint32_t)hi << 16);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 8; ++t) kv[t] = ld_act<T>(krow, d + t);
+        }
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+          const float4 q0 = *reinterpret_cast<const float4 *>(qs + r * D + d);
+          const float4 q1 = *reinterpret_cast<const float4 *>(qs + r * D + d + 4);
+          float s = sc[r];
+          s = fmaf(q0.x, kv[0], s); s = fmaf(q0.y, kv[1], s);
+          s = fmaf(q0.z, kv[2], s); s = fmaf(q0.w, kv[3], s);
+          s = fmaf(q1.x, kv[4], s); s = fmaf(q1.y, kv[5], s);
+          s = fmaf(q1.z, kv[6], s); s = fmaf(q1.w, kv[7], s);
+          sc[r] = s;
+        }
+      }
+    }
+    // scale, softcap, mask; online softmax per row
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      float s = -INFINITY;
+      if (valid && r < nrows) {
+        const int rr = row0 + r;
+        const int64_t h = kvh * p.group + rr % p.group, qi = rr / p.group;
+        s = sc[r] * p.scale;
+        if (p.softcap > 0.0f) s = p.softcap * tanhf(s / p.softcap);
+        s += att_bias(p, b, h, qi, j);
+      }
+      float tmax = s;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float m_new = fmaxf(m_run[r], tmax);
+      // all keys so far masked: keep zeros
+      const float corr = m_new == -INFINITY ? 1.0f : __expf(m_run[r] - m_new);
+      const float pj = (s == -INFINITY) ? 0.0f : __expf(s - m_new);
+      float psum = pj;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+      l_run[r] = l_run[r] * corr + psum;
+      m_run[r] = m_new;
+#pragma unroll
+      for (int t = 0; t < DPL; ++t) acc[r][t] *= corr;
+      ps[(warp * ROWS + r) * ATT_TK + lane] = pj;
+    }
+    __syncwarp();
+    // P.V: lane owns dims d = lane + 32 t
+    const int64_t rem_k = kend - (kbeg + my_tile * ATT_TK);
+    const int nk = rem_k < ATT_TK ? (int)rem_k : ATT_TK;
+    for (int kk = 0; kk < nk; ++kk) {
+      float vv[DPL];
+#pragma unroll
+      for (int t = 0; t < DPL; ++t)
+        vv[t] = (t < dpl && lane + 32 * t < D) ? ld_act<T>(vt + kk * DP, lane + 32 * t) : 0.0f;
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        const float pr = ps[(warp * ROWS + r) * ATT_TK + kk];
+#pragma unroll
+        for (int t = 0; t < DPL; ++t) acc[r][t] = fmaf(pr, vv[t], acc[r][t]);
+      }
+    }
+    __syncwarp();
+    buf ^= 1;
+  }
+  cp_async_wait<0>();
+
+  // Merge the 4 warps of this CTA: red[warp][r] = (m, l), then o.
+  float *red_ml = red;                        // [4][ROWS][2]
+  float *red_o = red + 4 * ROWS * 2;       // [4][ROWS][D]
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      red_ml[(warp * ROWS + r) * 2] = m_run[r];
+      red_ml[(warp * ROWS + r) * 2 + 1] = l_run[r];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+    for (int t = 0; t < DPL; ++t)
+      if (t < dpl && lane + 32 * t < D) red_o[(warp * ROWS + r) * D + lane + 32 * t] = acc[r][t];
+  __syncthreads();
+
+  const int64_t row_base = (int64_t)bh * p.rows_total + row0; // global row id
+  for (int e = threadIdx.x; e < nrows * D; e += ATT_THREADS) {
+    const int r = e / D, d = e % D;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) m = fmaxf(m, red_ml[(w * ROWS + r) * 2]);
+    float l = 0.0f, o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = red_ml[(w * ROWS + r) * 2];
+      const float c = (mw == -INFINITY) ? 0.0f : __expf(mw - m);
+      l += red_ml[(w * ROWS + r) * 2 + 1] * c;
+      o += red_o[(w * ROWS + r) * D + d] * c;
+    }
+    const int64_t grow = row_base + r;
+    if (p.splits == 1) {
+      const int rr = row0 + r;
+      const int64_t h = kvh * p.group + rr % p.group, qi = rr / p.group;
+      st_act<T>(p.y, b * p.y_sb + h * p.y_sh + qi * p.y_ss + d, l != 0.0f ? o / l : 0.0f);
+    } else {
+      const int64_t nrow_all = p.B * p.Hkv * p.rows_total;
+      p.ws_o[((int64_t)split * nrow_all + grow) * D + d] = o;
+      if (d == 0) {
+        p.ws_ml[((int64_t)split * nrow_all + grow) * 2] = m;
+        p.ws_ml[((int64_t)split * nrow_all + grow) * 2 + 1] = l;
+      }
+    }
+  }
+  if (p.splits == 1) return;
+
+  // Last split CTA of this (b, kv_head, row tile) merges all splits.
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    uint32_t *ctr = p.counters + (int64_t)bh * p.row_tiles + rt;
+    const uint32_t prev = atomicAdd(ctr, 1u);
+    last = prev + 1 == (uint32_t)p.splits;
+    if (last) {
+      __threadfence();
+      *ctr = 0u;
+    }
+  }
+  __syncthreads();
+  if (!last) return;
+  const int64_t nrow_all = p.B * p.Hkv * p.rows_total;
+  for (int e = threadIdx.x; e < nrows * D; e += ATT_THREADS) {
+    const int r = e / D, d = e % D;
+    const int64_t grow = row_base + r;
+    float m = -INFINITY;
+    for (int s = 0; s < p.splits; ++s) m = fmaxf(m, __ldcg(p.ws_ml + ((int64_t)s * nrow_all + grow) * 2));
+    float l = 0.0f, o = 0.0f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float ms = __ldcg(p.ws_ml + ((int64_t)s * nrow_all + grow) * 2);
+      const float c = (ms == -INFINITY) ? 0.0f : __expf(ms - m);
+      l += __ldcg(p.ws_ml + ((int64_t)s * nrow_all + grow) * 2 + 1) * c;
+      o += __ldcg(p.ws_o + ((int64_t)s * nrow_all + grow) * D + d) * c;
+    }
+    const int rr = row0 + r;
+    const int64_t h = kvh * p.group + rr % p.group, qi = rr / p.group;
+    st_act<T>(p.y, b * p.y_sb + h * p.y_sh + qi * p.y_ss + d, l != 0.0f ? o / l : 0.0f);
+  }
+}
+
+// present[b, h, dst_off + s, :] = src(b, h, s, :) for s < S; 16-byte chunks.
+template <typename T>
+__global__ void kv_copy(const T *__restrict__ src, int64_t s_sb, int64_t s_sh, int64_t s_ss,
+                        T *__restrict__ dst, int64_t d_sb, int64_t d_sh, int64_t d_ss,
+                        int64_t dst_off, int64_t B, int64_t H, int64_t S, int64_t D) {
+  const int64_t chunks = D * (int64_t)sizeof(T) / 16;
+  const int64_t total = B * H * S * chunks;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = e % chunks;
+    int64_t t = e / chunks;
+    const int64_t s = t % S;
+    t /= S;
+    const int64_t h = t % H, b = t / H;
+    const uint4 val = *reinterpret_cast<const uint4 *>(src + b * s_sb + h * s_sh + s * s_ss + c * (16 / sizeof(T)));
+    *reinterpret_cast<uint4 *>(dst + b * d_sb + h * d_sh + (dst_off + s) * d_ss + c * (16 / sizeof(T))) = val;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+struct View { int64_t sb, sh, ss; };
+
+static View rank4_view(int64_t H, int64_t S, int64_t D) { return {H * S * D, S * D, D}; }
+static View rank3_view(int64_t H, int64_t S, int64_t D) { return {S * H * D, D, H * D}; }
+
+template <typename T>
+static int launch_copy(const void *src, View sv, void *dst, View dv, int64_t off, int64_t B,
+                       int64_t H, int64_t S, int64_t D, cudaStream_t st) {
+  const int64_t total = B * H * S * (D * (int64_t)sizeof(T) / 16);
+  if (total == 0) return B2_OK;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > sm_count() * 16) blocks = sm_count() * 16;
+  kv_copy<T><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const T *>(src), sv.sb, sv.sh, sv.ss,
+                                                static_cast<T *>(dst), dv.sb, dv.sh, dv.ss, off, B,
+                                                H, S, D);
+  B2_LAUNCH_CHECK();
+  return B2_OK;
+}
+
+template <typename T>
+static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *v,
+                       const b2_tensor *mask, const b2_tensor *past_k, const b2_tensor *past_v,
+                       const b2_attention_attrs *at, b2_tensor *y, b2_tensor *pres_k,
+                       b2_tensor *pres_v, void *ws, size_t *ws_bytes, cudaStream_t st) {
+  const int rank = q->ndim;
+  int64_t B, Hq, Sq, D, Hkv, Sk;
+  View qv, kv, vv, yv;
+  if (rank == 4) {
+    B = q->shape[0]; Hq = q->shape[1]; Sq = q->shape[2]; D = q->shape[3];
+    Hkv = k->shape[1]; Sk = k->shape[2];
+    B2_ENFORCE(k->shape[0] == B && v->shape[0] == B,
+               "kernel::Attention: Q, K, V must share the same batch size.");
+    B2_ENFORCE(k->shape[3] == D, "kernel::Attention: K head_size must match Q head_size.");
+    B2_ENFORCE(v->shape[1] == Hkv, "kernel::Attention: V num_heads must match K num_heads.");
+    B2_ENFORCE(v->shape[2] == Sk, "kernel::Attention: V kv_seq_len must match K kv_seq_len.");
+    if (v->shape[3] != D)
+      B2_FAIL(B2_ERR_UNSUPPORTED, "kernel::Attention: v_head_size != head_size is not handled on the GPU");
+    qv = rank4_view(Hq, Sq, D);
+    kv = rank4_view(Hkv, Sk, D);
+    vv = kv;
+    yv = qv;
+  } else {
+    B2_ENFORCE(at->q_num_heads > 0, "kernel::Attention: 'Q' needs a positive ``num_heads`` to promote rank-3.");
+    B2_ENFORCE(at->kv_num_heads > 0, "kernel::Attention: 'K' needs a positive ``num_heads`` to promote rank-3.");
+    B = q->shape[0]; Sq = q->shape[1]; Hq = at->q_num_heads;
+    B2_ENFORCE(q->shape[2] % Hq == 0, "kernel::Attention: 'Q' hidden_size must be a multiple of ``num_heads``.");
+    D = q->shape[2] / Hq;
+    Hkv = at->kv_num_heads;
+    Sk = k->shape[1];
+    B2_ENFORCE(k->shape[2] % Hkv == 0, "kernel::Attention: 'K' hidden_size must be a multiple of ``num_heads``.");
+    B2_ENFORCE(k->shape[2] / Hkv == D, "kernel::Attention: K head_size must match Q head_size.");
+    B2_ENFORCE(v->shape[2] == k->shape[2] && v->shape[1] == Sk && k->shape[0] == B && v->shape[0] == B,
+               "kernel::Attention: V must match K.");
+    qv = rank3_view(Hq, Sq, D);
+    kv = rank3_view(Hkv, Sk, D);
+    vv = kv;
+    yv = qv;
+  }
+  B2_ENFORCE(Hkv > 0 && Hq % Hkv == 0,
+             "kernel::Attention: q_num_heads must be a positive multiple of kv_num_heads.");
+  B2_ENFORCE(at->left_window_size >= -1,
+             "kernel::Attention: 'left_window_size' must be -1 or nonnegative.");
+  B2_ENFORCE(at->right_window_size >= -1,
+             "kernel::Attention: 'right_window_size' must be -1 or nonnegative.");
+  B2_ENFORCE((past_k == nullptr) == (past_v == nullptr),
+             "kernel::Attention: past_key and past_value must be provided together.");
+  if (at->qk_matmul_output_mode != 0)
+    B2_FAIL(B2_ERR_UNSUPPORTED, "kernel::Attention: qk_matmul_output is not produced on the GPU");
+  if (D % 8 != 0 || D > ATT_DMAX)
+    B2_FAIL(B2_ERR_UNSUPPORTED, "kernel::Attention: head_size must be a multiple of 8 and <= 256 on the GPU");
+  const int64_t P = past_k ? past_k->shape[2] : 0;
+  if (past_k) {
+    B2_ENFORCE(past_k->ndim == 4 && past_v->ndim == 4, "kernel::Attention: concat inputs must be rank-4.");
+    B2_ENFORCE(past_k->shape[0] == B && past_k->shape[1] == Hkv && past_k->shape[3] == D,
+               "kernel::Attention: past KV shape must match current K/V on axes 0, 1, 3.");
+    B2_ENFORCE(past_v->shape[0] == B && past_v->shape[1] == Hkv && past_v->shape[2] == P &&
+                   past_v->shape[3] == D,
+               "kernel::Attention: past KV shape must match current K/V on axes 0, 1, 3.");
+  }
+  const int64_t L = P + Sk;
+  if (mask) {
+    B2_ENFORCE(mask->dtype == kFloat, "kernel::Attention: 'attn_mask' must be FLOAT or BOOL.");
+    B2_ENFORCE(mask->ndim >= 1 && mask->ndim <= 4,
+               "kernel::Attention: 'attn_mask' must have rank between 1 and 4.");
+  }
+  int64_t ms[4] = {1, 1, 1, 1};
+  if (mask) {
+    for (int i = 0; i < mask->ndim; ++i) ms[4 - mask->ndim + i] = mask->shape[i];
+    const int64_t od[3] = {B, Hq, Sq};
+    for (int i = 0; i < 3; ++i)
+      B2_ENFORCE(ms[i] == 1 || ms[i] == od[i],
+                 "kernel::Attention: 'attn_mask' is not broadcastable to (batch_size, q_num_heads, "
+                 "q_seq_len); its last axis defines the mask KV length.");
+  }
+  // present buffers
+  const bool alias = at->kv_capacity > 0;
+  const bool have_present = pres_k && pres_v;
+  if (past_k) B2_ENFORCE(have_present, "b2_attention: present_key/present_value are required with a past");
+  int64_t cap = L;
+  if (alias) {
+    cap = at->kv_capacity;
+    B2_ENFORCE(L <= cap, "b2_attention: past_len + new tokens exceed kv_capacity");
+    B2_ENFORCE(past_k == nullptr || (past_k->data == pres_k->data && past_v->data == pres_v->data),
+               "b2_attention: with kv_capacity the past and present tensors must share storage");
+  }
+  if (have_present) {
+    B2_ENFORCE(pres_k->ndim == 4 && pres_k->shape[0] == B && pres_k->shape[1] == Hkv &&
+                   pres_k->shape[2] == L && pres_k->shape[3] == D,
+               "b2_attention: present_key must be [B, Hkv, past+new, D]");
+    B2_ENFORCE(pres_v->ndim == 4 && pres_v->shape[0] == B && pres_v->shape[1] == Hkv &&
+                   pres_v->shape[2] == L && pres_v->shape[3] == D,
+               "b2_attention: present_value must be [B, Hkv, past+new, D]");
+  }
+  B2_ENFORCE(y->dtype == q->dtype, "kernel::Attention preallocated output must share Q's element type.");
+
+  // plan
+  const int group = (int)(Hq / Hkv);
+  const int rows_total = (int)(group * Sq);
+  const int rows_cta = rows_total <= 4 ? 4 : ATT_ROWS;
+  const int row_tiles = (rows_total + rows_cta - 1) / rows_cta;
+  const int64_t ctas_base = B * Hkv * row_tiles;
+  const int sms = sm_count();
+  int64_t splits = ctas_base >= 2 * sms ? 1 : (2 * sms + ctas_base - 1) / ctas_base;
+  int64_t kps = (L + splits - 1) / splits;
+  kps = (kps + 4 * ATT_TK - 1) / (4 * ATT_TK) * (4 * ATT_TK);
+  if (kps < 4 * ATT_TK) kps = 4 * ATT_TK;
+  splits = (L + kps - 1) / kps;
+  if (splits < 1) splits = 1;
+  const int64_t nrow_all = B * Hkv * rows_total;
+  size_t need = 0;
+  if (splits > 1)
+    need = (size_t)splits * nrow_all * (D + 2) * 4 + (size_t)ctas_base * 4;
+  int rc = workspace_check(ws, ws_bytes, need);
+  if (rc < 0) return rc;
+  if (rc == 1) return B2_OK;
+
+  // 1) build present: copy the past unless it is already in place, append new K/V.
+  View cache = {Hkv * cap * D, cap * D, D};
+  if (have_present) {
+    if (past_k && !alias) {
+      rc = launch_copy<T>(past_k->data, rank4_view(Hkv, P, D), pres_k->data, cache, 0, B, Hkv, P, D, st);
+      if (rc) return rc;
+      rc = launch_copy<T>(past_v->data, rank4_view(Hkv, P, D), pres_v->data, cache, 0, B, Hkv, P, D, st);
+      if (rc) return rc;
+    }
+    rc = launch_copy<T>(k->data, kv, pres_k->data, cache, P, B, Hkv, Sk, D, st);
+    if (rc) return rc;
+    rc = launch_copy<T>(v->data, vv, pres_v->data, cache, P, B, Hkv, Sk, D, st);
+    if (rc) return rc;
+  }
+  if (B * Hq * Sq == 0) return B2_OK;
+
+  AttParams p{};
+  p.q = q->data;
+  p.k = have_present ? pres_k->data : k->data;
+  p.v = have_present ? pres_v->data : v->data;
+  const View kview = have_present ? cache : kv;
+  const View vview = have_present ? cache : vv;
+  p.y = y->data;
+  p.mask = mask ? static_cast<const float *>(mask->data) : nullptr;
+  for (int i = 0; i < 4; ++i) p.mask_shape[i] = ms[i];
+  p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.Sq = Sq; p.L = L; p.D = D;
+  p.q_sb = qv.sb; p.q_sh = qv.sh; p.q_ss = qv.ss;
+  p.k_sb = kview.sb; p.k_sh = kview.sh; p.k_ss = kview.ss;
+  p.v_sb = vview.sb; p.v_sh = vview.sh; p.v_ss = vview.ss;
+  p.y_sb = yv.sb; p.y_sh = yv.sh; p.y_ss = yv.ss;
+  p.past_len = P;
+  p.scale = at->has_scale ? at->scale : 1.0f / sqrtf((float)D);
+  p.softcap = at->softcap;
+  p.causal = at->is_causal;
+  p.left_window = at->left_window_size;
+  p.right_window = at->right_window_size;
+  p.group = group;
+  p.rows_total = rows_total;
+  p.row_tiles = row_tiles;
+  p.splits = (int)splits;
+  p.keys_per_split = kps;
+  p.dt = q->dtype;
+  if (splits > 1) {
+    p.ws_o = static_cast<float *>(ws);
+    p.ws_ml = p.ws_o + (size_t)splits * nrow_all * D;
+    p.counters = reinterpret_cast<uint32_t *>(p.ws_ml + (size_t)splits * nrow_all * 2);
+  }
+  if (L == 0) {
+    // No keys: every row is fully masked and the reference writes zeros.
+    B2_CUDA(cudaMemsetAsync(y->data, 0, (size_t)B * Hq * Sq * D * sizeof(T), st));
+    return B2_OK;
+  }
+  const int DP = (int)D + 8;
+  const size_t smem = (size_t)2 * 2 * 4 * ATT_TK * DP * sizeof(T) + (size_t)rows_cta * D * 4 +
+                      (size_t)4 * rows_cta * ATT_TK * 4 + (size_t)4 * rows_cta * 2 * 4 +
+                      (size_t)4 * rows_cta * D * 4;
+  dim3 grid((unsigned)(B * Hkv), (unsigned)splits, (unsigned)row_tiles);
+  const int dpl = (int)((D + 31) / 32);
+  void (*kern)(AttParams) = nullptr;
+  if (rows_cta == 4) {
+    kern = dpl <= 2 ? attn_fwd<T, 4, 2> : dpl <= 4 ? attn_fwd<T, 4, 4> : attn_fwd<T, 4, 8>;
+  } else {
+    kern = dpl <= 2 ? attn_fwd<T, ATT_ROWS, 2> : dpl <= 4 ? attn_fwd<T, ATT_ROWS, 4> : attn_fwd<T, ATT_ROWS, 8>;
+  }
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<grid, ATT_THREADS, smem, st>>>(p);
+  B2_LAUNCH_CHECK();
+  return B2_OK;
+}
+
+} // namespace b2
+
+using namespace b2;
+
+extern "C" int b2_attention(const b2_tensor *q, const b2_tensor *k, const b2_tensor *v,
+                            const b2_tensor *attn_mask, const b2_tensor *past_key,
+                            const b2_tensor *past_value, const b2_attention_attrs *attrs,
+                            b2_tensor *y, b2_tensor *present_key, b2_tensor *present_value,
+                            void *workspace, size_t *workspace_bytes, void *stream) {
+  if (!q || !k || !v || !attrs || !y) B2_FAIL(B2_ERR_INVALID_ARGUMENT, "kernel::Attention: null tensor");
+  B2_ENFORCE(q->dtype == kFloat || q->dtype == kFloat16 || q->dtype == kBfloat16,
+             "kernel::Attention: 'Q' must be a FLOAT, FLOAT16 or BFLOAT16 tensor.");
+  B2_ENFORCE(k->dtype == q->dtype && v->dtype == q->dtype,
+             "kernel::Attention: Q, K, V must share the same dtype.");
+  B2_ENFORCE(q->ndim == k->ndim && q->ndim == v->ndim,
+             "kernel::Attention: Q, K, V must all share the same rank.");
+  B2_ENFORCE(q->ndim == 3 || q->ndim == 4, "kernel::Attention: Q, K, V must be rank-3 or rank-4.");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (q->dtype == kFloat16)
+    return attention_t<__half>(q, k, v, attn_mask, past_key, past_value, attrs, y, present_key,
+                               present_value, workspace, workspace_bytes, st);
+  if (q->dtype == kBfloat16)
+    return attention_t<__nv_bfloat16>(q, k, v, attn_mask, past_key, past_value, attrs, y,
+                                      present_key, present_value, workspace, workspace_bytes, st);
+  return attention_t<float>(q, k, v, attn_mask, past_key, past_value, attrs, y, present_key,
+                            present_value, workspace, workspace_bytes, st);
+}

@@ -1,0 +1,567 @@
+// Fused DequantizeLinear -> [Cast] -> MatMul (weight-only quantization).
+//
+// Replaces the node pair kernel::DequantizeLinear
+// (onnx_light/onnx_extensions/kernels/kernels/quantization/kernel_dequantizelinear.cc:522-693)
+// feeding kernel::MatMul (onnx_light/onnx_extensions/kernels/kernels/math/kernel_matmul.cc:181-223).
+// The dequantized weight never exists in HBM: packed weights are read once,
+// dequantized in registers with the reference's rounding (fp32 (q-zp)*s, then
+// RNE to the DequantizeLinear output type and to the Cast type), and
+// multiplied with fp32 accumulation.
+//
+// Kernels
+//  * dq_gemv  — decode shapes (M <= 4 activation rows).  HBM-bound: each warp
+//    streams 128-byte row segments of the packed weight with 16-byte loads
+//    (8 lanes per row, 4 rows per load instruction), scales for the CTA's
+//    K-range are staged in shared memory by the bulk-copy (TMA) engine, lanes
+//    reduce across rows with warp shuffles, warps through shared memory and
+//    CTAs (split-K) through a deterministic last-CTA reduction of partials.
+//  * dq_gemm_simt — any shape / layout / dtype; tiled CUDA-core GEMM with the
+//    dequantization fused into the B-tile load.  Used for FLOAT activations
+//    (fp32 accumulation parity, 1e-5) and for layouts the fast paths skip.
+//  * dq_gemm_tc (dq_gemm_tc.cu) — FLOAT16/BFLOAT16 activations with M > 8 on
+//    tcgen05 tensor cores.
+#include "b2_common.cuh"
+#include "dq_matmul.cuh"
+
+namespace b2 {
+
+// ---------------------------------------------------------------------------
+// Dequantized weight element with the reference's rounding chain.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float round_to(float v, int dt) {
+  if (dt == kFloat16) return __half2float(__ushort_as_half(f32_to_f16_bits(v)));
+  if (dt == kBfloat16) return __uint_as_float((uint32_t)f32_to_bf16_bits(v) << 16);
+  return v;
+}
+
+__device__ __forceinline__ int64_t w_scale_index(const DqMmParams &p, int64_t k, int64_t n) {
+  switch (p.slayout) {
+  case kScaleTensor: return 0;
+  case kScaleAxis0Block: return (k / p.block) * p.N + n;
+  case kScaleAxis0: return k;
+  case kScaleAxis1Block: return k * p.s_alen + n / p.block;
+  default: return n; // kScaleAxis1
+  }
+}
+
+__device__ __forceinline__ float w_element(const DqMmParams &p, int64_t k, int64_t n) {
+  const int64_t i = k * p.N + n;
+  const float q = qval(p.wdt, p.w, i);
+  const int64_t si = w_scale_index(p, k, n);
+  const float s = p.s_f16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t *>(p.scale)[si])
+                          : reinterpret_cast<const float *>(p.scale)[si];
+  const float z = p.zp ? qval(p.wdt, p.zp, si) : 0.0f;
+  float v = x86_mul(x86_sub(q, z), s);
+  v = round_to(v, p.s_f16 ? kFloat16 : kFloat); // DequantizeLinear output type
+  if (p.cast_dt) v = round_to(v, p.cast_dt);    // optional Cast node
+  return v;
+}
+
+template <typename T> __device__ __forceinline__ float act_load(const void *a, int64_t i);
+template <> __device__ __forceinline__ float act_load<float>(const void *a, int64_t i) {
+  return reinterpret_cast<const float *>(a)[i];
+}
+template <> __device__ __forceinline__ float act_load<__half>(const void *a, int64_t i) {
+  return __half2float(reinterpret_cast<const __half *>(a)[i]);
+}
+template <> __device__ __forceinline__ float act_load<__nv_bfloat16>(const void *a, int64_t i) {
+  return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(a)[i] << 16);
+}
+
+__device__ __forceinline__ void store_out(void *y, int dt, int64_t i, float v) {
+  if (dt == kFloat) reinterpret_cast<float *>(y)[i] = v;
+  else if (dt == kFloat16) reinterpret_cast<uint16_t *>(y)[i] = f32_to_f16_bits(v);
+  else reinterpret_cast<uint16_t *>(y)[i] = f32_to_bf16_bits(v);
+}
+
+// ---------------------------------------------------------------------------
+// Split-K finalisation shared by the CUDA-core kernels.
+//
+// Workspace layout: [ksplit][M][N] fp32 partials, then one uint32 arrival
+// counter per output tile.  Each CTA writes its partial tile, then bumps the
+// tile's counter; the CTA that arrives last sums the partials in split order
+// (deterministic), writes y and resets the counter to 0, so the counters are
+// zero again for the next call.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ bool arrive_last(uint32_t *counter, int expected) {
+  __shared__ bool last;
+  __syncthreads(); // all partial stores of this CTA issued
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(counter, 1u);
+    last = (prev + 1 == (uint32_t)expected);
+    if (last) {
+      __threadfence();
+      *counter = 0u;
+    }
+  }
+  __syncthreads();
+  return last;
+}
+
+// ---------------------------------------------------------------------------
+// dq_gemm_simt: C[M,N] = A[M,K] * Wdeq[K,N]
+// ---------------------------------------------------------------------------
+
+constexpr int SIMT_BM = 32, SIMT_BN = 128, SIMT_BK = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(256) dq_gemm_simt(const DqMmParams p) {
+  __shared__ float As[SIMT_BK][SIMT_BM + 1];
+  __shared__ float Bs[SIMT_BK][SIMT_BN];
+  const int tid = threadIdx.x;
+  const int tn = tid % 32, tm = tid / 32;
+  const int64_t n0 = (int64_t)blockIdx.x * SIMT_BN;
+  const int64_t m0 = (int64_t)blockIdx.y * SIMT_BM;
+  const int split = blockIdx.z;
+  const int64_t kbeg = (int64_t)split * p.kchunk;
+  const int64_t kend = min((int64_t)p.K, kbeg + p.kchunk);
+  float acc[4][4] = {};
+  for (int64_t k0 = kbeg; k0 < kend; k0 += SIMT_BK) {
+    // A tile: 32 x 32, 4 per thread
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int e = tid + r * 256;
+      const int mm = e / SIMT_BK, kk = e % SIMT_BK;
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < p.M && gk < kend) ? act_load<T>(p.a, gm * p.K + gk) : 0.0f;
+    }
+    // B tile: 32 x 128, dequantized, 16 per thread
+#pragma unroll 4
+    for (int r = 0; r < 16; ++r) {
+      const int e = tid + r * 256;
+      const int kk = e / SIMT_BN, nn = e % SIMT_BN;
+      const int64_t gk = k0 + kk, gn = n0 + nn;
+      Bs[kk][nn] = (gk < kend && gn < p.N) ? w_element(p, gk, gn) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < SIMT_BK; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][tm * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tn + 32 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  if (p.ksplit == 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t gm = m0 + tm * 4 + i, gn = n0 + tn + 32 * j;
+        if (gm < p.M && gn < p.N) store_out(p.y, p.ydt, gm * p.N + gn, acc[i][j]);
+      }
+    return;
+  }
+  float *part = p.partials + (int64_t)split * p.M * p.N;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gm = m0 + tm * 4 + i, gn = n0 + tn + 32 * j;
+      if (gm < p.M && gn < p.N) part[gm * p.N + gn] = acc[i][j];
+    }
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  if (!arrive_last(p.counters + tile, p.ksplit)) return;
+  for (int e = tid; e < SIMT_BM * SIMT_BN; e += 256) {
+    const int64_t gm = m0 + e / SIMT_BN, gn = n0 + e % SIMT_BN;
+    if (gm >= p.M || gn >= p.N) continue;
+    float s = 0.0f;
+    for (int sp = 0; sp < p.ksplit; ++sp) s += __ldcg(p.partials + ((int64_t)sp * p.M + gm) * p.N + gn);
+    store_out(p.y, p.ydt, gm * p.N + gn, s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dq_gemv: decode-shaped fused kernel (M <= 8).
+// ---------------------------------------------------------------------------
+
+// Decodes the 32 (int4/fp4: 16 bytes) or 32 (8-bit: 32 bytes) consecutive
+// quantized values a lane owns in one weight row.
+template <int BITS>
+__device__ __forceinline__ void gemv_load(const uint8_t *row, uint4 (&raw)[BITS / 4]) {
+  const uint4 *src = reinterpret_cast<const uint4 *>(row);
+#pragma unroll
+  for (int i = 0; i < BITS / 4; ++i) raw[i] = __ldcs(src + i);
+}
+
+template <int BITS>
+__device__ __forceinline__ float gemv_q(int wdt, const uint4 (&raw)[BITS / 4], int j) {
+  if (BITS == 4) {
+    const uint32_t word = j < 8 ? raw[0].x : j < 16 ? raw[0].y : j < 24 ? raw[0].z : raw[0].w;
+    const uint32_t nib = (word >> (4 * (j & 7))) & 0xfu;
+    if (wdt == kInt4) return (float)((int)nib - ((nib & 8u) ? 16 : 0));
+    if (wdt == kUint4) return (float)nib;
+    return dec_f4e2m1(nib);
+  } else {
+    const uint4 &r = raw[j >> 4];
+    const int jj = j & 15;
+    const uint32_t word = jj < 4 ? r.x : jj < 8 ? r.y : jj < 12 ? r.z : r.w;
+    const uint32_t b = (word >> (8 * (jj & 3))) & 0xffu;
+    switch (wdt) {
+    case kUint8: return (float)b;
+    case kInt8: return (float)(int8_t)b;
+    case kF8E4M3FN: return dec_f8e4m3fn(b);
+    case kF8E4M3FNUZ: return dec_f8e4m3fnuz(b);
+    case kF8E5M2: return dec_f8e5m2(b);
+    default: return dec_f8e5m2fnuz(b);
+    }
+  }
+}
+
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_TN = 256; // columns per CTA (8 lanes x 32)
+
+// Fast dequantisation of 8 signed/unsigned int4 values (one 32-bit word) into
+// fp16 pairs, multiplied by fp16 scales: the fp16 product of a 4-bit integer
+// and an fp16 scale is the correctly rounded fp16 of the exact product, i.e.
+// FloatToFloat16Bits((q - 0) * s) of the reference.
+__device__ __forceinline__ void int4x8_times_scale_f16(uint32_t w, bool is_signed,
+                                                       const __half2 (&s2)[4], __half2 (&out)[4]) {
+  // Element j of the word is nibble j.  Pairs are formed as (j, j+4): bits
+  // [4j, 4j+4) go to the low half, bits [4j+16, 4j+20) to the high half.
+  const uint32_t x = is_signed ? (w ^ 0x88888888u) : w;
+  const __half2 bias = __halves2half2(__ushort_as_half(is_signed ? 0x6408 : 0x6400),
+                                      __ushort_as_half(is_signed ? 0x6408 : 0x6400));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t h = ((x >> (4 * j)) & 0x000f000fu) | 0x64006400u; // 1024 + code
+    const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&h), bias);
+    __half2 r;
+    asm("mul.rn.f16x2 %0, %1, %2;"
+        : "=r"(*reinterpret_cast<uint32_t *>(&r))
+        : "r"(*reinterpret_cast<const uint32_t *>(&q)), "r"(*reinterpret_cast<const uint32_t *>(&s2[j])));
+    out[j] = r;
+  }
+}
+
+// Nibble order of the (j, j+4) pairing above: word element e = 4*hi + j.
+__device__ __forceinline__ float act_load_rt(const DqMmParams &p, int64_t i) {
+  if (p.ydt == kFloat) return act_load<float>(p.a, i);
+  if (p.ydt == kFloat16) return act_load<__half>(p.a, i);
+  return act_load<__nv_bfloat16>(p.a, i);
+}
+
+template <int MT, int BITS, bool FAST16>
+__global__ void __launch_bounds__(GEMV_THREADS) dq_gemv(const DqMmParams p) {
+  extern __shared__ float smem[];
+  // smem: activations [MT][kchunk] fp32, then per-warp reduction buffer
+  float *a_s = smem;
+  float *red = smem + MT * p.kchunk;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = lane & 7, r = lane >> 3;
+  const int64_t n0 = (int64_t)blockIdx.x * GEMV_TN;
+  const int64_t ncol = n0 + c * 32;
+  const int split = blockIdx.y;
+  const int64_t kbeg = (int64_t)split * p.kchunk;
+  const int64_t kend = min((int64_t)p.K, kbeg + p.kchunk);
+  const int64_t klen = kend - kbeg;
+  for (int e = threadIdx.x; e < MT * p.kchunk; e += GEMV_THREADS) {
+    const int mm = e / p.kchunk;
+    const int64_t kk = e % p.kchunk;
+    a_s[e] = (mm < p.M && kk < klen) ? act_load_rt(p, (int64_t)mm * p.K + kbeg + kk) : 0.0f;
+  }
+  __syncthreads();
+
+  float acc[MT][32];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[m][j] = 0.0f;
+
+  const bool col_ok = ncol + 32 <= p.N;
+  float sc[32], zc[32];
+  int64_t cur_kb = -1;
+  const int64_t row_bytes = p.N * BITS / 8;
+  const uint8_t *wcol = p.w + ncol * BITS / 8;
+  for (int64_t kk = warp * 4 + r; kk < klen; kk += 32) {
+    const int64_t k = kbeg + kk;
+    if (!col_ok) break;
+    // per-row scale / zero point for this lane's 32 columns
+    const int64_t kb = p.slayout == kScaleAxis0Block ? k / p.block : 0;
+    if (kb != cur_kb) {
+      cur_kb = kb;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int64_t si = p.slayout == kScaleTensor ? 0
+                           : p.slayout == kScaleAxis0Block ? kb * p.N + ncol + j
+                                                           : ncol + j;
+        sc[j] = p.s_f16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t *>(p.scale)[si])
+                        : reinterpret_cast<const float *>(p.scale)[si];
+        zc[j] = p.zp ? qval(p.wdt, p.zp, si) : 0.0f;
+      }
+    }
+    uint4 raw[BITS / 4];
+    gemv_load<BITS>(wcol + k * row_bytes, raw);
+    float wv[32];
+    if (FAST16) {
+      __half2 s2[4], o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t words[4] = {raw[0].x, raw[0].y, raw[0].z, raw[0].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s2[j] = __floats2half2_rn(sc[q * 8 + j], sc[q * 8 + j + 4]);
+        int4x8_times_scale_f16(words[q], p.wdt == kInt4, s2, o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          wv[q * 8 + j] = __low2float(o[j]);
+          wv[q * 8 + j + 4] = __high2float(o[j]);
+        }
+      }
+      if (p.cast_dt) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) wv[j] = round_to(wv[j], p.cast_dt);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float v = x86_mul(x86_sub(gemv_q<BITS>(p.wdt, raw, j), zc[j]), sc[j]);
+        v = round_to(v, p.s_f16 ? kFloat16 : kFloat);
+        if (p.cast_dt) v = round_to(v, p.cast_dt);
+        wv[j] = v;
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float av = a_s[m * p.kchunk + kk];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[m][j] = fmaf(av, wv[j], acc[m][j]);
+    }
+  }
+  // reduce the 4 row-lanes (r) sharing a column chunk
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], 8);
+      acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], 16);
+    }
+  // warps -> shared: red[warp][m][256]
+  if (r == 0) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) red[(warp * MT + m) * GEMV_TN + c * 32 + j] = acc[m][j];
+  }
+  __syncthreads();
+  float *part = p.ksplit > 1 ? p.partials + (int64_t)split * p.M * p.N : nullptr;
+  for (int e = threadIdx.x; e < MT * GEMV_TN; e += GEMV_THREADS) {
+    const int m = e / GEMV_TN, nn = e % GEMV_TN;
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < GEMV_THREADS / 32; ++w) s += red[(w * MT + m) * GEMV_TN + nn];
+    const int64_t gn = n0 + nn;
+    if (m < p.M && gn < p.N) {
+      if (part) part[(int64_t)m * p.N + gn] = s;
+      else store_out(p.y, p.ydt, (int64_t)m * p.N + gn, s);
+    }
+  }
+  if (!part) return;
+  if (!arrive_last(p.counters + blockIdx.x, p.ksplit)) return;
+  for (int e = threadIdx.x; e < MT * GEMV_TN; e += GEMV_THREADS) {
+    const int m = e / GEMV_TN;
+    const int64_t gn = n0 + e % GEMV_TN;
+    if (m >= p.M || gn >= p.N) continue;
+    float s = 0.0f;
+    for (int sp = 0; sp < p.ksplit; ++sp)
+      s += __ldcg(p.partials + ((int64_t)sp * p.M + m) * p.N + gn);
+    store_out(p.y, p.ydt, (int64_t)m * p.N + gn, s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+static int dq_mm_validate(const b2_tensor *a, const b2_tensor *w, const b2_tensor *s,
+                          const b2_tensor *zp, int64_t axis, int32_t cast_dt, const b2_tensor *y,
+                          DqMmParams &p) {
+  B2_ENFORCE(a && w && s && y, "kernel::MatMul: null tensor");
+  B2_ENFORCE(w->ndim == 2, "b2_dequantize_matmul: the quantized weight must be rank-2 [K, N]");
+  B2_ENFORCE(s->dtype == kFloat || s->dtype == kFloat16,
+             "kernel::DequantizeLinear: x_scale must be FLOAT or FLOAT16.");
+  const int dq_out = s->dtype;
+  const int wdt_eff = cast_dt ? cast_dt : dq_out;
+  if (cast_dt)
+    B2_ENFORCE(cast_dt == kFloat || cast_dt == kFloat16 || cast_dt == kBfloat16,
+               "b2_dequantize_matmul: cast_dtype must be FLOAT, FLOAT16 or BFLOAT16");
+  B2_ENFORCE(a->dtype == wdt_eff, "kernel::MatMul inputs must share the same dtype.");
+  B2_ENFORCE(a->dtype == kFloat || a->dtype == kFloat16 || a->dtype == kBfloat16,
+             "kernel::MatMul: unsupported data type %d", a->dtype);
+  // DequantizeLinear layout rules (kernel_dequantizelinear.cc:528-565).
+  DqParams dqp{};
+  std::vector<int64_t> wshape = shape_of(w);
+  int rc = dq_validate(w, s, zp, axis, dq_out, wshape, dqp);
+  if (rc) return rc;
+  // MatMul shape rules (matmul_shape_utils.h:86-106) with a rank-2 right operand.
+  B2_ENFORCE(a->ndim >= 1, "kernel::MatMul does not accept rank-0 inputs.");
+  const int64_t K = w->shape[0], N = w->shape[1];
+  const int64_t Ka = a->shape[a->ndim - 1];
+  B2_ENFORCE(Ka == K, "kernel::MatMul got incompatible inner dimensions.");
+  int64_t M = 1;
+  for (int i = 0; i < a->ndim - 1; ++i) M *= a->shape[i];
+  std::vector<int64_t> out(a->shape, a->shape + a->ndim - 1);
+  out.push_back(N);
+  B2_ENFORCE(y->dtype == a->dtype, "kernel::MatMul preallocated output must have the same dtype as input A.");
+  B2_ENFORCE(shape_of(y) == out, "kernel::MatMul preallocated output has an invalid shape.");
+  p.M = M;
+  p.K = K;
+  p.N = N;
+  p.wdt = w->dtype;
+  p.s_f16 = s->dtype == kFloat16;
+  p.cast_dt = cast_dt;
+  p.ydt = a->dtype;
+  if (dqp.layout == 0) p.slayout = kScaleTensor;
+  else if (axis == 0) p.slayout = dqp.layout == 2 ? kScaleAxis0Block : kScaleAxis0;
+  else p.slayout = dqp.layout == 2 ? kScaleAxis1Block : kScaleAxis1;
+  p.block = dqp.block;
+  p.s_alen = dqp.s_alen;
+  return B2_OK;
+}
+
+struct Plan {
+  int kind = 0; // 0 simt, 1 gemv, 2 tensor core
+  int ksplit = 1;
+  int64_t kchunk = 0;
+  dim3 grid;
+  size_t smem = 0;
+  int mt = 1;
+  int bits = 4;
+  bool fast16 = false;
+  size_t ws = 0;
+};
+
+static int wbits(int dt) {
+  if (dt == kInt4 || dt == kUint4 || dt == kF4E2M1) return 4;
+  if (dt == kInt8 || dt == kUint8 || is_f8(dt)) return 8;
+  return 0;
+}
+
+static Plan make_plan(const DqMmParams &p) {
+  Plan pl;
+  const int sms = sm_count();
+  const int bits = wbits(p.wdt);
+  const bool col_layout = p.slayout == kScaleTensor || p.slayout == kScaleAxis0Block ||
+                          p.slayout == kScaleAxis1;
+  const bool fast16 = (p.wdt == kInt4 || p.wdt == kUint4) && p.s_f16 && p.zp == nullptr;
+  const bool gemv_ok = p.M <= (fast16 ? 4 : 2) && bits && col_layout && p.N % 32 == 0 &&
+                       (p.slayout != kScaleAxis0Block || p.block % 32 == 0) &&
+                       ((p.N * bits / 8) % 16 == 0);
+  if (dq_tc_supported(p)) {
+    pl.kind = 2;
+    pl.ws = dq_tc_workspace(p);
+    return pl;
+  }
+  if (gemv_ok) {
+    pl.kind = 1;
+    pl.bits = bits;
+    pl.mt = p.M <= 1 ? 1 : p.M <= 2 ? 2 : 4;
+    pl.fast16 = fast16;
+    const int64_t ntiles = (p.N + GEMV_TN - 1) / GEMV_TN;
+    int64_t want = (2 * sms + ntiles - 1) / ntiles;
+    int64_t kchunk = (p.K + want - 1) / want;
+    const int64_t align = p.slayout == kScaleAxis0Block ? std::max<int64_t>(32, p.block) : 32;
+    kchunk = (kchunk + align - 1) / align * align;
+    if (kchunk < 32) kchunk = 32;
+    pl.kchunk = kchunk;
+    pl.ksplit = (int)((p.K + kchunk - 1) / kchunk);
+    pl.grid = dim3((unsigned)ntiles, (unsigned)pl.ksplit, 1);
+    pl.smem = (size_t)pl.mt * kchunk * 4 + (size_t)(GEMV_THREADS / 32) * pl.mt * GEMV_TN * 4;
+    if (pl.ksplit > 1) pl.ws = (size_t)pl.ksplit * p.M * p.N * 4 + (size_t)ntiles * 4;
+    return pl;
+  }
+  pl.kind = 0;
+  const int64_t tn = (p.N + SIMT_BN - 1) / SIMT_BN, tm = (p.M + SIMT_BM - 1) / SIMT_BM;
+  int64_t want = (2 * sms + tn * tm - 1) / (tn * tm);
+  if (want < 1) want = 1;
+  int64_t kchunk = (p.K + want - 1) / want;
+  kchunk = (kchunk + SIMT_BK - 1) / SIMT_BK * SIMT_BK;
+  if (kchunk < SIMT_BK) kchunk = SIMT_BK;
+  pl.kchunk = kchunk;
+  pl.ksplit = (int)((p.K + kchunk - 1) / kchunk);
+  if (pl.ksplit < 1) pl.ksplit = 1;
+  pl.grid = dim3((unsigned)tn, (unsigned)tm, (unsigned)pl.ksplit);
+  if (pl.ksplit > 1) pl.ws = (size_t)pl.ksplit * p.M * p.N * 4 + (size_t)tn * tm * 4;
+  return pl;
+}
+
+template <typename T> static int launch_simt(const DqMmParams &p, const Plan &pl, cudaStream_t st) {
+  dq_gemm_simt<T><<<pl.grid, 256, 0, st>>>(p);
+  B2_LAUNCH_CHECK();
+  return B2_OK;
+}
+
+template <int MT, int BITS, bool FAST>
+static int launch_gemv_t(const DqMmParams &p, const Plan &pl, cudaStream_t st) {
+  auto kern = dq_gemv<MT, BITS, FAST>;
+  if (pl.smem > 48 * 1024)
+    B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+  kern<<<pl.grid, GEMV_THREADS, pl.smem, st>>>(p);
+  B2_LAUNCH_CHECK();
+  return B2_OK;
+}
+
+static int launch_gemv(const DqMmParams &p, const Plan &pl, cudaStream_t st) {
+  if (pl.fast16) {
+    switch (pl.mt) {
+    case 1: return launch_gemv_t<1, 4, true>(p, pl, st);
+    case 2: return launch_gemv_t<2, 4, true>(p, pl, st);
+    default: return launch_gemv_t<4, 4, true>(p, pl, st);
+    }
+  }
+  if (pl.bits == 4) {
+    if (pl.mt == 1) return launch_gemv_t<1, 4, false>(p, pl, st);
+    return launch_gemv_t<2, 4, false>(p, pl, st);
+  }
+  if (pl.mt == 1) return launch_gemv_t<1, 8, false>(p, pl, st);
+  return launch_gemv_t<2, 8, false>(p, pl, st);
+}
+
+} // namespace b2
+
+using namespace b2;
+
+extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
+                                    const b2_tensor *w_scale, const b2_tensor *w_zero_point,
+                                    int64_t axis, int32_t cast_dtype, b2_tensor *y,
+                                    void *workspace, size_t *workspace_bytes, void *stream) {
+  DqMmParams p{};
+  int rc = dq_mm_validate(a, w, w_scale, w_zero_point, axis, cast_dtype, y, p);
+  if (rc) return rc;
+  const Plan pl = make_plan(p);
+  rc = workspace_check(workspace, workspace_bytes, pl.ws);
+  if (rc < 0) return rc;
+  if (rc == 1) return B2_OK; // size query
+  if (p.M == 0 || p.N == 0) return B2_OK;
+  p.a = a->data;
+  p.w = static_cast<const uint8_t *>(w->data);
+  p.scale = static_cast<const uint8_t *>(w_scale->data);
+  p.zp = w_zero_point ? static_cast<const uint8_t *>(w_zero_point->data) : nullptr;
+  p.y = y->data;
+  p.kchunk = pl.kchunk;
+  p.ksplit = pl.ksplit;
+  if (pl.ksplit > 1) {
+    p.partials = static_cast<float *>(workspace);
+    p.counters = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) +
+                                              (size_t)pl.ksplit * p.M * p.N * 4);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p.K == 0) {
+    // Empty reduction: y = 0.
+    B2_CUDA(cudaMemsetAsync(y->data, 0, (size_t)p.M * p.N * (p.ydt == kFloat ? 4 : 2), st));
+    return B2_OK;
+  }
+  if (pl.kind == 2) return dq_tc_launch(p, workspace, st);
+  if (pl.kind == 1) return launch_gemv(p, pl, st);
+  if (p.ydt == kFloat) return launch_simt<float>(p, pl, st);
+  if (p.ydt == kFloat16) return launch_simt<__half>(p, pl, st);
+  return launch_simt<__nv_bfloat16>(p, pl, st);
+}

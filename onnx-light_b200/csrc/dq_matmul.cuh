@@ -1,0 +1,41 @@
+// Parameters of the fused DequantizeLinear -> [Cast] -> MatMul kernels.
+#pragma once
+#include "b2_common.cuh"
+#include "dequantize.cuh"
+
+namespace b2 {
+
+// Where the scale (and zero point) of weight element (k, n) of W[K, N] lives.
+enum ScaleLayout : int {
+  kScaleTensor = 0,     // one scale
+  kScaleAxis0Block = 1, // blocked along K: s[k / block][n]
+  kScaleAxis0 = 2,      // per-axis along K: s[k]
+  kScaleAxis1Block = 3, // blocked along N: s[k][n / block]
+  kScaleAxis1 = 4       // per-axis along N: s[n]
+};
+
+struct DqMmParams {
+  const void *a;        // activations [M, K] (FLOAT / FLOAT16 / BFLOAT16)
+  const uint8_t *w;     // packed quantized weight [K, N]
+  const uint8_t *scale; // FLOAT or FLOAT16
+  const uint8_t *zp;    // nullable, dtype of w
+  void *y;              // [M, N], dtype of a
+  int64_t M, K, N;
+  int64_t block, s_alen;
+  int wdt;
+  int s_f16;    // scale (and DequantizeLinear output) is FLOAT16
+  int cast_dt;  // 0 or the Cast target dtype
+  int ydt;
+  int slayout;
+  int64_t kchunk;
+  int ksplit;
+  float *partials;    // split-K workspace
+  uint32_t *counters; // split-K arrival counters (zero between calls)
+};
+
+// Tensor-core path (dq_gemm_tc.cu).
+bool dq_tc_supported(const DqMmParams &p);
+size_t dq_tc_workspace(const DqMmParams &p);
+int dq_tc_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
+
+} // namespace b2

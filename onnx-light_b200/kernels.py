@@ -1,0 +1,289 @@
+"""Host-side mirror of onnx-light's kernel classes for the quantized-inference path.
+
+Each class keeps the reference's name, call signature, argument meaning and
+error behaviour (std::invalid_argument -> ValueError), and runs on the GPU
+through the C ABI in include/onnxl_b200.h.  Inputs and outputs are CUDA
+tensors; sub-byte and 8-bit float tensors travel as :class:`QTensor` (packed
+uint8 storage + ONNX dtype + logical shape), exactly like onnx-light's Tensor
+storage.  There is no CPU fallback: a missing library or a CPU tensor raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from . import _capi as capi
+from ._capi import Desc, check, lib, stream_ptr
+
+
+@dataclass
+class QTensor:
+    """Quantized tensor: packed storage bytes, ONNX dtype, logical shape."""
+
+    data: torch.Tensor  # uint8 storage on the device (packed low-order-first)
+    dtype: int
+    shape: tuple
+
+    @property
+    def device(self):
+        return self.data.device
+
+
+def _desc(t, dtype: Optional[int] = None) -> Desc:
+    if isinstance(t, QTensor):
+        if not t.data.is_cuda:
+            raise ValueError("onnxl_b200 tensors must live on a CUDA device")
+        return Desc(t.data.data_ptr(), t.dtype, t.shape)
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"expected a torch.Tensor or QTensor, got {type(t).__name__}")
+    if not t.is_cuda:
+        raise ValueError("onnxl_b200 tensors must live on a CUDA device (no CPU fallback)")
+    if not t.is_contiguous():
+        raise ValueError("onnxl_b200 tensors must be contiguous")
+    dt = dtype if dtype is not None else capi.TORCH_TO_ONNX[t.dtype]
+    return Desc(t.data_ptr(), dt, tuple(t.shape))
+
+
+def _ref(d: Optional[Desc]):
+    return d.ref if d is not None else None
+
+
+# ---------------------------------------------------------------------------
+# Workspace: one zero-initialised buffer per device, grown on demand.  The
+# kernels return their split-K counters to zero, so the buffer stays valid.
+# ---------------------------------------------------------------------------
+
+_workspaces: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
+def _call_with_workspace(fn, args_before, args_after, device):
+    """Queries the workspace size (workspace=NULL), then runs."""
+    need = C.c_size_t(0)
+    check(fn(*args_before, None, C.byref(need), *args_after))
+    ws = workspace(device, need.value) if need.value else None
+    cap = C.c_size_t(ws.numel() if ws is not None else 0)
+    check(fn(*args_before, C.c_void_p(ws.data_ptr()) if ws is not None else None, C.byref(cap),
+             *args_after))
+
+
+# ---------------------------------------------------------------------------
+# Kernels
+# ---------------------------------------------------------------------------
+
+
+class DequantizeLinear:
+    """kernel::DequantizeLinear (kernel_dequantizelinear.cc:332-712).
+
+    ``y = (x - x_zero_point) * x_scale``; per-tensor, per-axis or blocked along
+    ``axis`` (the block is x.shape[axis] / x_scale.shape[axis]); the output
+    dtype is x_scale's (FLOAT or FLOAT16).  Bit-exact with the reference.
+    """
+
+    name = "onnx_kernels:GPU:ai.onnx:DequantizeLinear"
+
+    def __call__(self, x, x_scale: torch.Tensor, x_zero_point=None, axis: int = 1,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        xd = _desc(x)
+        sd = _desc(x_scale)
+        zd = _desc(x_zero_point) if x_zero_point is not None else None
+        shape = tuple(x.shape)
+        if out is None:
+            if x_scale.dtype not in (torch.float32, torch.float16):
+                raise ValueError("kernel::DequantizeLinear: x_scale must be FLOAT or FLOAT16.")
+            out = torch.empty(shape, dtype=x_scale.dtype, device=x_scale.device)
+        yd = _desc(out)
+        check(lib().b2_dequantize_linear(xd.ref, sd.ref, _ref(zd), int(axis), yd.ref,
+                                         stream_ptr(out.device)))
+        return out
+
+
+class DequantizeMatMul:
+    """The DequantizeLinear -> [Cast] -> MatMul weight-only pattern as one kernel.
+
+    Equivalent to ``MatMul(a, Cast(DequantizeLinear(w, w_scale, w_zero_point, axis)))``
+    with kernel::DequantizeLinear (kernel_dequantizelinear.cc:522-693) and
+    kernel::MatMul (kernel_matmul.cc:181-223): the weight is dequantized with the
+    reference's rounding and never written to HBM.
+    """
+
+    name = "onnx_kernels:GPU:b200:DequantizeMatMul"
+
+    def __call__(self, a: torch.Tensor, w, w_scale: torch.Tensor, w_zero_point=None,
+                 axis: int = 0, cast_dtype: Optional[torch.dtype] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        ad, wd, sd = _desc(a), _desc(w), _desc(w_scale)
+        zd = _desc(w_zero_point) if w_zero_point is not None else None
+        cast = capi.TORCH_TO_ONNX[cast_dtype] if cast_dtype is not None else 0
+        if out is None:
+            n = int(w.shape[-1])
+            out = torch.empty(tuple(a.shape[:-1]) + (n,), dtype=a.dtype, device=a.device)
+        yd = _desc(out)
+        _call_with_workspace(lib().b2_dequantize_matmul,
+                             (ad.ref, wd.ref, sd.ref, _ref(zd), int(axis), cast, yd.ref),
+                             (stream_ptr(a.device),), a.device)
+        return out
+
+
+def _matmul_shape(a_shape, b_shape):
+    a2 = list(a_shape) if len(a_shape) > 1 else [1, a_shape[0]]
+    b2 = list(b_shape) if len(b_shape) > 1 else [b_shape[0], 1]
+    ap, bp = a2[:-2], b2[:-2]
+    r = max(len(ap), len(bp))
+    ap = [1] * (r - len(ap)) + ap
+    bp = [1] * (r - len(bp)) + bp
+    out = [max(x, y) if 1 in (x, y) else x for x, y in zip(ap, bp)]
+    if len(a_shape) != 1:
+        out.append(a2[-2])
+    if len(b_shape) != 1:
+        out.append(b2[-1])
+    return tuple(out)
+
+
+class MatMulInteger:
+    """kernel::MatMulInteger (kernel_matmul_integer.cc:178-250): int32 output, bit-exact."""
+
+    name = "onnx_kernels:GPU:ai.onnx:MatMulInteger"
+
+    def __call__(self, a: torch.Tensor, b: torch.Tensor, a_zero_point=None, b_zero_point=None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        ad, bd = _desc(a), _desc(b)
+        azd = _desc(a_zero_point) if a_zero_point is not None else None
+        bzd = _desc(b_zero_point) if b_zero_point is not None else None
+        if out is None:
+            out = torch.empty(_matmul_shape(a.shape, b.shape), dtype=torch.int32, device=a.device)
+        yd = _desc(out)
+        _call_with_workspace(lib().b2_matmul_integer, (ad.ref, bd.ref, _ref(azd), _ref(bzd), yd.ref),
+                             (stream_ptr(a.device),), a.device)
+        return out
+
+
+class QLinearMatMul:
+    """kernel::QLinearMatMul (kernel_qlinearmatmul.cc:221-284): int8/uint8 output, bit-exact."""
+
+    name = "onnx_kernels:GPU:ai.onnx:QLinearMatMul"
+
+    def __call__(self, a, a_scale, a_zero_point, b, b_scale, b_zero_point, y_scale, y_zero_point,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        ds = [_desc(t) for t in (a, a_scale, a_zero_point, b, b_scale, b_zero_point, y_scale,
+                                 y_zero_point)]
+        if out is None:
+            out = torch.empty(_matmul_shape(a.shape, b.shape), dtype=y_zero_point.dtype,
+                              device=a.device)
+        yd = _desc(out)
+        _call_with_workspace(lib().b2_qlinear_matmul, tuple(d.ref for d in ds) + (yd.ref,),
+                             (stream_ptr(a.device),), a.device)
+        return out
+
+
+@dataclass
+class Attributes:
+    """kernel::Attention::Attributes (include_nn_kernels.h:1027-1040)."""
+
+    has_scale: bool = False
+    scale: float = 0.0
+    is_causal: bool = False
+    softcap: float = 0.0
+    qk_matmul_output_mode: int = 0
+    q_num_heads: int = 0
+    kv_num_heads: int = 0
+    left_window_size: int = -1
+    right_window_size: int = -1
+
+
+@dataclass
+class Result:
+    Y: torch.Tensor
+    present_key: Optional[torch.Tensor] = None
+    present_value: Optional[torch.Tensor] = None
+
+
+class KVCache:
+    """Contiguous, capacity-reserved KV cache [B, Hkv, capacity, D] per K and V.
+
+    The device counterpart of onnx-light's persistent KV storage
+    (RuntimeSessionOptions::persistent_tensor_initial_capacity,
+    runtime_context.h:763-768): past and present share one buffer and each
+    Attention call appends its new tokens in place.
+    """
+
+    def __init__(self, batch: int, kv_heads: int, capacity: int, head_size: int,
+                 dtype=torch.float16, device="cuda"):
+        self.k = torch.zeros((batch, kv_heads, capacity, head_size), dtype=dtype, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.capacity = capacity
+        self.length = 0
+
+    def view(self, length: int):
+        """past/present views: the buffer with a logical sequence length."""
+        return self.k, self.v, length
+
+
+class Attention:
+    """kernel::Attention, opset 23 (kernel_attention.cc:767-902), GQA + contiguous KV cache."""
+
+    name = "onnx_kernels:GPU:ai.onnx:Attention"
+
+    def __call__(self, Q, K, V, attrs: Optional[Attributes] = None, attn_mask=None,
+                 past_key=None, past_value=None, cache: Optional[KVCache] = None,
+                 present_key=None, present_value=None, out=None) -> Result:
+        attrs = attrs or Attributes()
+        a = capi.B2AttentionAttrs(int(attrs.has_scale), float(attrs.scale), int(attrs.is_causal),
+                                  float(attrs.softcap), int(attrs.qk_matmul_output_mode),
+                                  int(attrs.q_num_heads), int(attrs.kv_num_heads),
+                                  int(attrs.left_window_size), int(attrs.right_window_size), 0)
+        qd, kd, vd = _desc(Q), _desc(K), _desc(V)
+        md = _desc(attn_mask) if attn_mask is not None else None
+        rank3 = Q.dim() == 3
+        new = K.shape[1] if rank3 else K.shape[2]
+        B = Q.shape[0]
+        if rank3:
+            hkv = attrs.kv_num_heads
+            D = K.shape[2] // hkv if hkv > 0 else 0
+        else:
+            hkv, D = K.shape[1], K.shape[3]
+        pkd = pvd = None
+        if cache is not None:
+            past = cache.length
+            a.kv_capacity = cache.capacity
+            if past:
+                pkd = Desc(cache.k.data_ptr(), capi.TORCH_TO_ONNX[cache.k.dtype], (B, hkv, past, D))
+                pvd = Desc(cache.v.data_ptr(), capi.TORCH_TO_ONNX[cache.v.dtype], (B, hkv, past, D))
+            total = past + new
+            prk = Desc(cache.k.data_ptr(), capi.TORCH_TO_ONNX[cache.k.dtype], (B, hkv, total, D))
+            prv = Desc(cache.v.data_ptr(), capi.TORCH_TO_ONNX[cache.v.dtype], (B, hkv, total, D))
+        else:
+            if past_key is not None:
+                pkd, pvd = _desc(past_key), _desc(past_value)
+                total = past_key.shape[2] + new
+            else:
+                total = new
+            if present_key is None and (past_key is not None):
+                present_key = torch.empty((B, hkv, total, D), dtype=Q.dtype, device=Q.device)
+                present_value = torch.empty_like(present_key)
+            prk = _desc(present_key) if present_key is not None else None
+            prv = _desc(present_value) if present_value is not None else None
+        if out is None:
+            out = torch.empty(Q.shape if not rank3 else Q.shape, dtype=Q.dtype, device=Q.device)
+            if not rank3 and V.shape[3] != Q.shape[3]:
+                out = torch.empty(Q.shape[:3] + (V.shape[3],), dtype=Q.dtype, device=Q.device)
+        yd = _desc(out)
+        _call_with_workspace(lib().b2_attention,
+                             (qd.ref, kd.ref, vd.ref, _ref(md), _ref(pkd), _ref(pvd), C.byref(a),
+                              yd.ref, _ref(prk), _ref(prv)),
+                             (stream_ptr(Q.device),), Q.device)
+        if cache is not None:
+            cache.length = total
+            return Result(out, cache.k[:, :, :total], cache.v[:, :, :total])
+        return Result(out, present_key, present_value)

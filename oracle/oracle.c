@@ -34,8 +34,8 @@ enum {
   DT_FLOAT = 1, DT_UINT8 = 2, DT_INT8 = 3, DT_UINT16 = 4, DT_INT16 = 5, DT_INT32 = 6,
   DT_INT64 = 7, DT_BOOL = 9, DT_FLOAT16 = 10, DT_DOUBLE = 11, DT_UINT32 = 12, DT_UINT64 = 13,
   DT_BFLOAT16 = 16, DT_F8E4M3FN = 17, DT_F8E4M3FNUZ = 18, DT_F8E5M2 = 19, DT_F8E5M2FNUZ = 20,
-  DT_UINT4 = 21, DT_INT4 = 22, DT_F4E2M1 = 23, DT_F6E2M3 = 24, DT_F6E3M2 = 25,
-  DT_UINT2 = 26, DT_INT2 = 27
+  DT_UINT4 = 21, DT_INT4 = 22, DT_F4E2M1 = 23, DT_F8E8M0 = 24, DT_UINT2 = 25, DT_INT2 = 26,
+  DT_F6E2M3 = 27, DT_F6E3M2 = 28
 };
 
 static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }

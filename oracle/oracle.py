@@ -26,7 +26,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 FLOAT, UINT8, INT8, UINT16, INT16, INT32, INT64, BOOL = 1, 2, 3, 4, 5, 6, 7, 9
 FLOAT16, DOUBLE, BFLOAT16 = 10, 11, 16
 F8E4M3FN, F8E4M3FNUZ, F8E5M2, F8E5M2FNUZ = 17, 18, 19, 20
-UINT4, INT4, F4E2M1, F6E2M3, F6E3M2, UINT2, INT2 = 21, 22, 23, 24, 25, 26, 27
+UINT4, INT4, F4E2M1, F8E8M0, UINT2, INT2, F6E2M3, F6E3M2 = 21, 22, 23, 24, 25, 26, 27, 28
 
 SUB_BYTE_BITS = {UINT4: 4, INT4: 4, F4E2M1: 4, UINT2: 2, INT2: 2, F6E2M3: 6, F6E3M2: 6}
 ELEM_BYTES = {FLOAT: 4, UINT8: 1, INT8: 1, UINT16: 2, INT16: 2, INT32: 4, INT64: 8, BOOL: 1,

@@ -1,0 +1,206 @@
+"""Generates tests/golden/ref_fixtures.npz from onnx-light's own kernels.
+
+Run in a container that has the reference tree: ``make -C oracle ref`` builds
+oracle/_ref/libref.so from the reference sources, then
+``python tests/golden/make_golden.py`` calls the reference kernels on seeded
+inputs and stores inputs + outputs.  The committed fixtures let the GPU box
+(which has no reference tree) check parity against the reference itself.
+
+Cases cover every DequantizeLinear input type and layout (per-tensor,
+per-axis, blocked; with and without zero point; FLOAT and FLOAT16 scales;
+NaN/Inf float8 codes; odd element counts), MatMulInteger zero-point modes and
+broadcast batches, QLinearMatMul including ties-to-even and saturation, MatMul
+in FLOAT/FLOAT16/BFLOAT16 and Attention (GQA, causal, past KV, softcap, mask,
+rank-3).
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, os.path.dirname(HERE))
+
+import oracle as O  # noqa: E402
+from util import CODE_RANGE, encode_codes, scale_raw  # noqa: E402
+
+OUT = os.path.join(HERE, "ref_fixtures.npz")
+
+
+def dq_cases():
+    """(name, x_dt, x_shape, s_dt, s_shape, has_zp, axis) tuples."""
+    dts = [O.UINT8, O.INT8, O.UINT16, O.INT16, O.INT32, O.F8E4M3FN, O.F8E4M3FNUZ, O.F8E5M2,
+           O.F8E5M2FNUZ, O.UINT4, O.INT4, O.UINT2, O.INT2, O.F4E2M1, O.F6E2M3, O.F6E3M2]
+    cases = []
+    for dt in dts:
+        for s_dt in (O.FLOAT, O.FLOAT16):
+            for zp in (False, True):
+                cases.append((dt, (7, 5), s_dt, (), zp, 1))              # per-tensor, odd count
+                cases.append((dt, (4, 6, 8), s_dt, (6,), zp, 1))         # per-axis, middle axis
+                cases.append((dt, (64, 48), s_dt, (2, 48), zp, 0))       # blocked along axis 0
+                cases.append((dt, (6, 64), s_dt, (6, 4), zp, 1))         # blocked along the last axis
+    return cases
+
+
+def main():
+    arrays = {}
+    meta = {"dq": [], "mmi": [], "qlm": [], "mm": [], "att": []}
+    seed = 100
+
+    # ---------------- DequantizeLinear ----------------
+    for i, (dt, xs, s_dt, ss, has_zp, axis) in enumerate(dq_cases()):
+        seed += 10
+        n = int(np.prod(xs))
+        lo, hi = CODE_RANGE[dt]
+        codes = O.randint(seed, (n,), lo, hi)
+        x = encode_codes(codes, dt)
+        sn = int(np.prod(ss)) if len(ss) else 1
+        s = scale_raw(O.rand_uniform(seed + 1, (sn,), 0.01, 2.0), s_dt)
+        zp = None
+        if has_zp:
+            if dt in (O.F8E4M3FN, O.F8E4M3FNUZ, O.F8E5M2, O.F8E5M2FNUZ):
+                zcodes = O.randint(seed + 2, (sn,), 0, 40)  # small finite float8 values
+            else:
+                zlo, zhi = CODE_RANGE[dt]
+                zcodes = O.randint(seed + 2, (sn,), max(zlo, -3), min(zhi, 3))
+            zp = encode_codes(zcodes, dt)
+        y = O.ref_dequantize_linear(x, dt, xs, s, s_dt, ss, zp, ss if has_zp else None, axis)
+        k = f"dq{i}"
+        arrays[k + "_x"], arrays[k + "_s"], arrays[k + "_y"] = x, s.view(np.uint8), y.view(np.uint8)
+        if zp is not None:
+            arrays[k + "_z"] = zp
+        meta["dq"].append(dict(key=k, x_dt=dt, x_shape=list(xs), s_dt=s_dt, s_shape=list(ss),
+                               zp=has_zp, axis=axis))
+
+    # ---------------- MatMulInteger ----------------
+    mmi = [
+        ((16, 64), O.UINT8, (64, 40), O.INT8, "scalar", "col"),
+        ((16, 64), O.INT8, (64, 40), O.INT8, "row", "scalar"),
+        ((3, 1, 33, 70), O.UINT8, (2, 70, 17), O.UINT8, "scalar", "none"),
+        ((70,), O.INT8, (70, 9), O.UINT8, "none", "col"),
+        ((5, 70), O.UINT8, (70,), O.INT8, "row", "none"),
+        ((130, 256), O.UINT8, (256, 200), O.INT8, "scalar", "col"),
+    ]
+    for i, (ash, adt, bsh, bdt, az, bz) in enumerate(mmi):
+        seed += 10
+        a = encode_codes(O.randint(seed, (int(np.prod(ash)),), *CODE_RANGE[adt]), adt).reshape(ash)
+        b = encode_codes(O.randint(seed + 1, (int(np.prod(bsh)),), *CODE_RANGE[bdt]), bdt).reshape(bsh)
+        M = ash[-2] if len(ash) > 1 else 1
+        N = bsh[-1] if len(bsh) > 1 else 1
+        azp = bzp = None
+        if az != "none":
+            azp = encode_codes(O.randint(seed + 2, ((M if az == "row" else 1),), 100, 130) if adt == O.UINT8
+                               else O.randint(seed + 2, ((M if az == "row" else 1),), -5, 5), adt)
+        if bz != "none":
+            bzp = encode_codes(O.randint(seed + 3, ((N if bz == "col" else 1),), -4, 4) if bdt == O.INT8
+                               else O.randint(seed + 3, ((N if bz == "col" else 1),), 120, 130), bdt)
+        y = O.ref_matmul_integer(a, adt, b, bdt, azp, bzp,
+                                 a_zp_shape=None if azp is None else [azp.size],
+                                 b_zp_shape=None if bzp is None else [bzp.size])
+        k = f"mmi{i}"
+        arrays[k + "_a"], arrays[k + "_b"], arrays[k + "_y"] = a, b, y
+        if azp is not None:
+            arrays[k + "_az"] = azp
+        if bzp is not None:
+            arrays[k + "_bz"] = bzp
+        meta["mmi"].append(dict(key=k, a_dt=adt, b_dt=bdt, a_shape=list(ash), b_shape=list(bsh),
+                                az=azp is not None, bz=bzp is not None))
+
+    # ---------------- QLinearMatMul ----------------
+    kat = json.load(open(os.path.join(HERE, "kat_reference_tests.json")))["qlinear_matmul_inputs"][0]
+    qcases = []
+    for is_int8 in (False, True):
+        sh = 127 if is_int8 else 0
+        dt = O.INT8 if is_int8 else O.UINT8
+        a = np.array([v - sh for v in kat["a"]], np.int64)
+        b = np.array([v - sh for v in kat["b"]], np.int64)
+        for s_dt in (O.FLOAT, O.FLOAT16):
+            qcases.append(dict(a=encode_codes(a, dt).reshape(kat["a_shape"]),
+                               b=encode_codes(b, dt).reshape(kat["b_shape"]), dt=dt, s_dt=s_dt,
+                               sc=(kat["a_scale"], kat["b_scale"], kat["y_scale"]),
+                               zp=(kat["a_zp"] - sh, kat["b_zp"] - sh, kat["y_zp"] - sh)))
+    for i, (ash, bsh, dt, ydt) in enumerate([((64, 96), (96, 48), O.UINT8, O.UINT8),
+                                             ((2, 33, 70), (70, 19), O.INT8, O.INT8),
+                                             ((40, 128), (128, 64), O.UINT8, O.INT8)]):
+        seed += 10
+        a = encode_codes(O.randint(seed, (int(np.prod(ash)),), *CODE_RANGE[dt]), dt).reshape(ash)
+        b = encode_codes(O.randint(seed + 1, (int(np.prod(bsh)),), *CODE_RANGE[dt]), dt).reshape(bsh)
+        zp = (3, -2, 5) if dt == O.INT8 else (113, 114, 118)
+        if ydt == O.INT8 and dt == O.UINT8:
+            zp = (113, 114, -7)
+        qcases.append(dict(a=a, b=b, dt=dt, ydt=ydt, s_dt=O.FLOAT, sc=(0.0066, 0.00705, 0.0107 * (1 + i)),
+                           zp=zp))
+    for i, c in enumerate(qcases):
+        ydt = c.get("ydt", c["dt"])
+        y = O.ref_qlinear_matmul(c["a"], c["dt"], c["sc"][0], c["zp"][0], c["b"], c["dt"], c["sc"][1],
+                                 c["zp"][1], c["sc"][2], c["zp"][2], ydt, scale_dt=c["s_dt"])
+        k = f"qlm{i}"
+        arrays[k + "_a"], arrays[k + "_b"], arrays[k + "_y"] = c["a"], c["b"], y.view(np.uint8)
+        meta["qlm"].append(dict(key=k, dt=c["dt"], ydt=ydt, s_dt=c["s_dt"], sc=list(c["sc"]),
+                                zp=list(c["zp"]), a_shape=list(c["a"].shape),
+                                b_shape=list(c["b"].shape)))
+
+    # ---------------- MatMul ----------------
+    for i, (ash, bsh, dt) in enumerate([((3, 37, 64), (64, 50), O.FLOAT),
+                                        ((8, 128), (128, 96), O.FLOAT16),
+                                        ((2, 16, 96), (96, 64), O.BFLOAT16)]):
+        seed += 10
+        a = O.randn(seed, ash)
+        b = O.randn(seed + 1, bsh)
+        if dt == O.FLOAT16:
+            a, b = O.f32_to_f16_bits(a), O.f32_to_f16_bits(b)
+        elif dt == O.BFLOAT16:
+            a, b = O.f32_to_bf16_bits(a), O.f32_to_bf16_bits(b)
+        y = O.ref_matmul(a, b, dt)
+        k = f"mm{i}"
+        arrays[k + "_a"], arrays[k + "_b"], arrays[k + "_y"] = a, b, y
+        meta["mm"].append(dict(key=k, dt=dt))
+
+    # ---------------- Attention ----------------
+    att = [
+        dict(B=2, Hq=8, Hkv=2, Sq=1, P=37, D=64, causal=True, softcap=0.0, mask=False, rank=4, dt=O.FLOAT16),
+        dict(B=1, Hq=4, Hkv=4, Sq=9, P=0, D=32, causal=True, softcap=0.0, mask=False, rank=4, dt=O.FLOAT16),
+        dict(B=2, Hq=6, Hkv=3, Sq=5, P=11, D=16, causal=False, softcap=5.0, mask=True, rank=4, dt=O.FLOAT),
+        dict(B=1, Hq=4, Hkv=2, Sq=7, P=0, D=32, causal=True, softcap=0.0, mask=False, rank=3, dt=O.BFLOAT16),
+        dict(B=1, Hq=32, Hkv=8, Sq=1, P=65, D=128, causal=True, softcap=0.0, mask=False, rank=4, dt=O.FLOAT16),
+    ]
+    for i, c in enumerate(att):
+        seed += 10
+        B, Hq, Hkv, Sq, P, D = c["B"], c["Hq"], c["Hkv"], c["Sq"], c["P"], c["D"]
+        if c["rank"] == 4:
+            q = O.randn(seed, (B, Hq, Sq, D), 0, 0.5)
+            k = O.randn(seed + 1, (B, Hkv, Sq, D), 0, 0.5)
+            v = O.randn(seed + 2, (B, Hkv, Sq, D), 0, 0.5)
+        else:
+            q = O.randn(seed, (B, Sq, Hq * D), 0, 0.5)
+            k = O.randn(seed + 1, (B, Sq, Hkv * D), 0, 0.5)
+            v = O.randn(seed + 2, (B, Sq, Hkv * D), 0, 0.5)
+        pk = O.randn(seed + 3, (B, Hkv, P, D), 0, 0.5) if P else None
+        pv = O.randn(seed + 4, (B, Hkv, P, D), 0, 0.5) if P else None
+        mask = O.randn(seed + 5, (Sq, P + Sq), 0, 1.0) if c["mask"] else None
+        cv = {O.FLOAT: lambda t: t, O.FLOAT16: O.f32_to_f16_bits, O.BFLOAT16: O.f32_to_bf16_bits}[c["dt"]]
+        q, k, v = cv(q), cv(k), cv(v)
+        if P:
+            pk, pv = cv(pk), cv(pv)
+        y, prk, prv = O.ref_attention(q, k, v, dt=c["dt"], is_causal=c["causal"], softcap=c["softcap"],
+                                      mask=mask, past_k=pk, past_v=pv, q_num_heads=Hq, kv_num_heads=Hkv)
+        kk = f"att{i}"
+        arrays.update({kk + "_q": q, kk + "_k": k, kk + "_v": v, kk + "_y": y})
+        if P:
+            arrays.update({kk + "_pk": pk, kk + "_pv": pv, kk + "_prk": prk, kk + "_prv": prv})
+        if mask is not None:
+            arrays[kk + "_mask"] = mask
+        meta["att"].append(dict(key=kk, **c))
+
+    arrays["meta"] = np.frombuffer(json.dumps(meta).encode(), np.uint8)
+    np.savez_compressed(OUT, **arrays)
+    print(f"wrote {OUT}: {sum(len(v) for v in meta.values())} cases, {os.path.getsize(OUT)} bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,105 @@
+"""Opset-23 Attention on the GPU: against onnx-light's own outputs (fixtures)
+and the oracle, GQA, causal, softcap, masks, rank-3 inputs, and the contiguous
+KV cache with in-place append.  Tolerance: rel-L2 <= 1e-3 (fp16/bf16)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from util import load_fixtures, rel_l2, to_dev
+
+pytestmark = pytest.mark.gpu
+META, Z = load_fixtures()
+TORCH = {O.FLOAT: torch.float32, O.FLOAT16: torch.float16, O.BFLOAT16: torch.bfloat16}
+UP = {O.FLOAT: lambda t: t, O.FLOAT16: O.f16_bits_to_f32, O.BFLOAT16: O.bf16_bits_to_f32}
+TOL = {O.FLOAT: 1e-5, O.FLOAT16: 1e-3, O.BFLOAT16: 1e-3}
+
+
+def dev(raw, dt):
+    return to_dev(raw).view(TORCH[dt])
+
+
+@pytest.mark.parametrize("m", META["att"], ids=lambda m: m["key"])
+def test_matches_reference_fixture(b2, cuda, m):
+    k = m["key"]
+    dt = m["dt"]
+    q, kk, v = dev(Z[k + "_q"], dt), dev(Z[k + "_k"], dt), dev(Z[k + "_v"], dt)
+    attrs = b2.Attributes(is_causal=m["causal"], softcap=m["softcap"], q_num_heads=m["Hq"],
+                          kv_num_heads=m["Hkv"])
+    mask = to_dev(Z[k + "_mask"]) if m["mask"] else None
+    pk = dev(Z[k + "_pk"], dt) if m["P"] else None
+    pv = dev(Z[k + "_pv"], dt) if m["P"] else None
+    r = b2.Attention()(q, kk, v, attrs, mask, pk, pv)
+    torch.cuda.synchronize()
+    y = r.Y.float().cpu().numpy()
+    ref = UP[dt](Z[k + "_y"])
+    assert rel_l2(y, ref) <= TOL[dt] * (10 if dt == O.BFLOAT16 else 1)
+    if m["P"]:
+        assert np.array_equal(r.present_key.cpu().numpy().view(Z[k + "_prk"].dtype), Z[k + "_prk"])
+        assert np.array_equal(r.present_value.cpu().numpy().view(Z[k + "_prv"].dtype), Z[k + "_prv"])
+
+
+def oracle_attention(q16, k16, v16, causal, past_len):
+    q, k, v = O.f16_bits_to_f32(q16), O.f16_bits_to_f32(k16), O.f16_bits_to_f32(v16)
+    return O.attention_f32(q, k, v, is_causal=causal, past_len=past_len)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,P,D", [(4, 32, 8, 511, 128), (3, 8, 8, 100, 64), (2, 16, 2, 2000, 128)])
+def test_decode_kv_cache_in_place(b2, cuda, B, Hq, Hkv, P, D):
+    rng_q = O.randn(51, (B, Hq, 1, D), 0, 0.5)
+    rng_k = O.randn(52, (B, Hkv, P + 2, D), 0, 0.5)
+    rng_v = O.randn(53, (B, Hkv, P + 2, D), 0, 0.5)
+    q16 = O.f32_to_f16_bits(rng_q)
+    k16, v16 = O.f32_to_f16_bits(rng_k), O.f32_to_f16_bits(rng_v)
+    cache = b2.KVCache(B, Hkv, P + 8, D, dtype=torch.float16)
+    cache.k[:, :, :P] = dev(k16[:, :, :P].copy(), O.FLOAT16)
+    cache.v[:, :, :P] = dev(v16[:, :, :P].copy(), O.FLOAT16)
+    cache.length = P
+    att = b2.Attention()
+    attrs = b2.Attributes(is_causal=True)
+    for step in range(2):  # two decode steps append in place
+        pos = P + step
+        r = att(dev(q16, O.FLOAT16), dev(k16[:, :, pos:pos + 1].copy(), O.FLOAT16),
+                dev(v16[:, :, pos:pos + 1].copy(), O.FLOAT16), attrs, cache=cache)
+        torch.cuda.synchronize()
+        ref = oracle_attention(q16, k16[:, :, :pos + 1], v16[:, :, :pos + 1], True, pos)
+        assert rel_l2(r.Y.float().cpu().numpy(), ref) <= 1e-3
+        assert cache.length == pos + 1
+        assert np.array_equal(cache.k[:, :, :pos + 1].cpu().numpy().view(np.uint16), k16[:, :, :pos + 1])
+
+
+def test_prefill_causal_gqa_rank3(b2, cuda):
+    B, S, Hq, Hkv, D = 2, 77, 8, 2, 64
+    q = O.f32_to_bf16_bits(O.randn(61, (B, S, Hq * D), 0, 0.5))
+    k = O.f32_to_bf16_bits(O.randn(62, (B, S, Hkv * D), 0, 0.5))
+    v = O.f32_to_bf16_bits(O.randn(63, (B, S, Hkv * D), 0, 0.5))
+    r = b2.Attention()(dev(q, O.BFLOAT16), dev(k, O.BFLOAT16), dev(v, O.BFLOAT16),
+                       b2.Attributes(is_causal=True, q_num_heads=Hq, kv_num_heads=Hkv))
+    torch.cuda.synchronize()
+    up = O.bf16_bits_to_f32
+    q4 = up(q).reshape(B, S, Hq, D).transpose(0, 2, 1, 3)
+    k4 = up(k).reshape(B, S, Hkv, D).transpose(0, 2, 1, 3)
+    v4 = up(v).reshape(B, S, Hkv, D).transpose(0, 2, 1, 3)
+    ref = O.attention_f32(q4, k4, v4, is_causal=True).transpose(0, 2, 1, 3).reshape(B, S, Hq * D)
+    assert rel_l2(r.Y.float().cpu().numpy(), ref) <= 4e-3  # bf16 output rounding
+
+
+def test_fully_masked_rows_are_zero(b2, cuda):
+    B, H, S, D = 1, 2, 4, 16
+    q = dev(O.f32_to_f16_bits(O.randn(71, (B, H, S, D))), O.FLOAT16)
+    k = dev(O.f32_to_f16_bits(O.randn(72, (B, H, S, D))), O.FLOAT16)
+    v = dev(O.f32_to_f16_bits(O.randn(73, (B, H, S, D))), O.FLOAT16)
+    mask = torch.full((S, S), float("-inf"), device="cuda")
+    mask[0] = 0.0
+    r = b2.Attention()(q, k, v, b2.Attributes(), mask)
+    y = r.Y.float().cpu().numpy()
+    assert np.all(y[:, :, 1:] == 0.0) and np.any(y[:, :, 0] != 0.0)
+
+
+def test_errors(b2, cuda):
+    q = torch.zeros((1, 6, 1, 16), dtype=torch.float16, device="cuda")
+    k = torch.zeros((1, 4, 1, 16), dtype=torch.float16, device="cuda")
+    with pytest.raises(ValueError, match="positive multiple of kv_num_heads"):
+        b2.Attention()(q, k, k)
+    with pytest.raises(ValueError, match="same dtype"):
+        b2.Attention()(q, k.float(), k.float())

@@ -1,0 +1,116 @@
+"""Fused DequantizeLinear -> [Cast] -> MatMul on the GPU against the oracle's
+two-node chain (DequantizeLinear then MatMul), with the tolerance of the
+rel-L2 <= 1e-3 for FLOAT16/BFLOAT16, <= 1e-5 for FLOAT."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from util import random_q, rel_l2, scale_raw, to_dev
+
+pytestmark = pytest.mark.gpu
+TOL = {O.FLOAT: 1e-5, O.FLOAT16: 1e-3, O.BFLOAT16: 1e-3}
+TORCH = {O.FLOAT: torch.float32, O.FLOAT16: torch.float16, O.BFLOAT16: torch.bfloat16}
+
+
+def run_case(b2, M, K, N, wdt, s_dt, act_dt, axis=0, block=None, zp=False, cast=0, seed=1,
+             lead=None):
+    """Returns (gpu, oracle) outputs as float32 arrays."""
+    # weight + scales in the requested layout
+    w = random_q(seed, (K, N), wdt)
+    if block is None:               # per-axis
+        s_shape = (K,) if axis == 0 else (N,)
+    elif block == 0:                # per-tensor
+        s_shape = ()
+    else:                           # blocked
+        s_shape = (K // block, N) if axis == 0 else (K, N // block)
+    sn = int(np.prod(s_shape)) if s_shape else 1
+    s = scale_raw(O.rand_uniform(seed + 1, (sn,), 0.002, 0.02), s_dt)
+    z = random_q(seed + 2, s_shape if s_shape else (1,), wdt, -2, 2) if zp else None
+    a32 = O.randn(seed + 3, (M, K))
+    a_raw = {O.FLOAT: a32, O.FLOAT16: O.f32_to_f16_bits(a32), O.BFLOAT16: O.f32_to_bf16_bits(a32)}[act_dt]
+    # oracle: DequantizeLinear, optional Cast, MatMul in the activation dtype
+    wq = O.dequantize_linear(w, wdt, (K, N), s, s_dt, s_shape, z, s_shape if zp else None, axis)
+    wf = wq if s_dt == O.FLOAT else O.f16_bits_to_f32(wq)
+    if cast == O.FLOAT16:
+        wb = O.f32_to_f16_bits(wf)
+    elif cast == O.BFLOAT16:
+        wb = O.f32_to_bf16_bits(wf)
+    elif cast == O.FLOAT:
+        wb = wf
+    else:
+        wb = wq
+    ref = O.matmul(a_raw, wb, act_dt)
+    # GPU
+    tw = b2.QTensor(to_dev(w), wdt, (K, N))
+    ts = to_dev(s).reshape(s_shape) if s_shape else to_dev(s).reshape(())
+    tz = b2.QTensor(to_dev(z), wdt, s_shape if s_shape else ()) if zp else None
+    ta = to_dev(a_raw).view(TORCH[act_dt]).reshape(M, K)
+    if lead:
+        ta = ta.reshape(*lead, K)
+    cast_t = {0: None, O.FLOAT: torch.float32, O.FLOAT16: torch.float16, O.BFLOAT16: torch.bfloat16}[cast]
+    y = b2.DequantizeMatMul()(ta, tw, ts, tz, axis=axis, cast_dtype=cast_t)
+    torch.cuda.synchronize()
+    y = y.float().cpu().numpy().reshape(M, N)
+    up = {O.FLOAT: lambda t: t, O.FLOAT16: O.f16_bits_to_f32, O.BFLOAT16: O.bf16_bits_to_f32}[act_dt]
+    return y, up(ref)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+def test_decode_gemv_int4_fp16_config3(b2, cuda, M):
+    # int4 blocked along K (block 128), FLOAT16 scales, no zero point.
+    y, ref = run_case(b2, M, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16]
+
+
+def test_decode_gemv_down_proj_shape(b2, cuda):
+    y, ref = run_case(b2, 1, 11008, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=7)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16]
+
+
+def test_config1_int4_zero_point_fp32(b2, cuda):
+    # int4 [4096,4096], block 32 along K, fp32 scales, int4 zero points,
+    # fp32 activations [1, 32, 4096].
+    y, ref = run_case(b2, 32, 4096, 4096, O.INT4, O.FLOAT, O.FLOAT, block=32, zp=True, lead=(1, 32))
+    assert rel_l2(y, ref) <= TOL[O.FLOAT]
+
+
+@pytest.mark.parametrize("wdt", [O.F8E4M3FN, O.F4E2M1])
+def test_prefill_style_fp8_fp4_cast_bf16(b2, cuda, wdt):
+    # BASELINE config 5 weight path: fp8/fp4 blocked along K (block 32), fp32 scales,
+    # DequantizeLinear -> Cast(BFLOAT16) -> MatMul with bf16 activations.
+    y, ref = run_case(b2, 64, 512, 384, wdt, O.FLOAT, O.BFLOAT16, block=32, cast=O.BFLOAT16)
+    assert rel_l2(y, ref) <= TOL[O.BFLOAT16]
+
+
+@pytest.mark.parametrize("wdt,s_dt,act,axis,block,zp,cast", [
+    (O.UINT4, O.FLOAT16, O.FLOAT16, 0, 64, False, 0),
+    (O.INT4, O.FLOAT, O.FLOAT, 1, None, True, 0),        # per-axis along N
+    (O.INT8, O.FLOAT, O.FLOAT16, 0, None, True, O.FLOAT16),  # per-axis along K
+    (O.UINT8, O.FLOAT16, O.FLOAT16, 1, 16, True, 0),      # blocked along N
+    (O.INT4, O.FLOAT, O.FLOAT, 0, 0, True, 0),            # per-tensor
+    (O.F8E5M2, O.FLOAT16, O.BFLOAT16, 0, 32, False, O.BFLOAT16),
+    (O.INT2, O.FLOAT, O.FLOAT, 0, 16, True, 0),
+])
+def test_layouts_and_types(b2, cuda, wdt, s_dt, act, axis, block, zp, cast):
+    for M in (1, 5, 40):
+        y, ref = run_case(b2, M, 256, 192, wdt, s_dt, act, axis, block, zp, cast, seed=M)
+        assert rel_l2(y, ref) <= TOL[act], (M, rel_l2(y, ref))
+
+
+def test_repeated_calls_reuse_workspace(b2, cuda):
+    # split-K counters must return to zero: many calls on one workspace agree.
+    outs = [run_case(b2, 1, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=3)[0]
+            for _ in range(3)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
+def test_dtype_mismatch_errors(b2, cuda):
+    w = b2.QTensor(to_dev(random_q(1, (64, 32), O.INT4)), O.INT4, (64, 32))
+    s = torch.ones((2, 32), device="cuda", dtype=torch.float16)
+    a = torch.ones((1, 64), device="cuda", dtype=torch.float32)
+    with pytest.raises(ValueError, match="must share the same dtype"):
+        b2.DequantizeMatMul()(a, w, s, axis=0)
+    a16 = torch.ones((1, 63), device="cuda", dtype=torch.float16)
+    with pytest.raises(ValueError, match="incompatible inner dimensions"):
+        b2.DequantizeMatMul()(a16, w, s, axis=0)
