@@ -34,7 +34,7 @@ B2_ERR_UNSUPPORTED = -6
 TORCH_TO_ONNX = {
     torch.float32: FLOAT, torch.float16: FLOAT16, torch.bfloat16: BFLOAT16, torch.uint8: UINT8,
     torch.int8: INT8, torch.int16: INT16, torch.int32: INT32, torch.int64: INT64,
-    torch.uint16: UINT16, torch.bool: BOOL,
+    torch.uint16: UINT16, torch.bool: BOOL, torch.float64: DOUBLE,
 }
 ONNX_TO_TORCH = {FLOAT: torch.float32, FLOAT16: torch.float16, BFLOAT16: torch.bfloat16,
                  UINT8: torch.uint8, INT8: torch.int8, INT16: torch.int16, INT32: torch.int32,

@@ -507,7 +507,8 @@ static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *
   const int row_tiles = (rows_total + rows_cta - 1) / rows_cta;
   const int64_t ctas_base = B * Hkv * row_tiles;
   const int sms = sm_count();
-  int64_t splits = ctas_base >= 2 * sms ? 1 : (2 * sms + ctas_base - 1) / ctas_base;
+  int64_t splits = ctas_base >= 2 * sms || ctas_base > (int64_t)kMaxCounters
+                       ? 1 : (2 * sms + ctas_base - 1) / ctas_base;
   int64_t kps = (L + splits - 1) / splits;
   kps = (kps + 4 * ATT_TK - 1) / (4 * ATT_TK) * (4 * ATT_TK);
   if (kps < 4 * ATT_TK) kps = 4 * ATT_TK;
@@ -516,7 +517,7 @@ static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *
   const int64_t nrow_all = B * Hkv * rows_total;
   size_t need = 0;
   if (splits > 1)
-    need = (size_t)splits * nrow_all * (D + 2) * 4 + (size_t)ctas_base * 4;
+    need = kCounterBytes + (size_t)splits * nrow_all * (D + 2) * 4;
   int rc = workspace_check(ws, ws_bytes, need);
   if (rc < 0) return rc;
   if (rc == 1) return B2_OK;
@@ -564,9 +565,9 @@ static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *
   p.keys_per_split = kps;
   p.dt = q->dtype;
   if (splits > 1) {
-    p.ws_o = static_cast<float *>(ws);
+    p.counters = static_cast<uint32_t *>(ws);
+    p.ws_o = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kCounterBytes);
     p.ws_ml = p.ws_o + (size_t)splits * nrow_all * D;
-    p.counters = reinterpret_cast<uint32_t *>(p.ws_ml + (size_t)splits * nrow_all * 2);
   }
   if (L == 0) {
     // No keys: every row is fully masked and the reference writes zeros.

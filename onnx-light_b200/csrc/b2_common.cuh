@@ -102,6 +102,18 @@ inline const char *dtype_name(int dt) {
   }
 }
 
+// Workspace layout shared by every entry point: the first kCounterBytes hold
+// uint32 arrival counters (split-K / split-KV "last CTA" detection).  Every
+// kernel that uses counters returns them to zero before it exits, and no
+// kernel ever writes anything else there, so the region stays all-zero across
+// calls of any shape.  Per-call partial results follow the counter region.
+constexpr size_t kCounterBytes = 64 * 1024;
+// The last 16 bytes of the counter region hold a status word that a bounded
+// device-side wait sets when it gives up (0 = no error); counters stop short
+// of it.
+constexpr size_t kStatusOffset = kCounterBytes - 16;
+constexpr size_t kMaxCounters = kStatusOffset / 4;
+
 // Workspace protocol shared by every entry point that needs scratch.
 // Returns 1 when the call is a size query (workspace == NULL), 0 when the
 // caller offered enough, and a negative status otherwise.

@@ -1,12 +1,474 @@
-// FLOAT16/BFLOAT16 fused dequant GEMM on tcgen05 tensor cores (M > 8).
+// Fused DequantizeLinear -> [Cast] -> MatMul on tcgen05 tensor cores (sm_100a)
+// for FLOAT16 / BFLOAT16 activations.
+//
+// Orientation ("swap AB"): the MMA computes D^T[n, m] = W^T[n, k] . A^T[k, m],
+// so 128 weight columns fill the MMA's M = 128 side and the activation rows
+// (BN = 16 .. 256 of them) are the MMA's N side.  Decode batches of 8..64
+// rows therefore run at full tile height, and prefill uses BN = 256.
+//
+// Per CTA (one 128-column x BN-row output tile, K range of one split):
+//   warp 0      TMA: raw packed weight tile [64 k x 128 n] (no swizzle) and the
+//               activation tile [BN m x 64 k] (128-byte swizzle, K-major) into
+//               a STAGES-deep ring;
+//   warps 2-5   dequantize the raw weight tile in registers with the
+//               reference's rounding (fp32 (q - zp) * s, rounded to the
+//               DequantizeLinear output type and to the Cast type) and store
+//               it as the MMA's A operand in the 128-byte-swizzled MN-major
+//               layout (64-element rows of n, 8-row atoms along k);
+//   warp 1      allocates TMEM and one thread issues tcgen05.mma.kind::f16
+//               (M=128, N=BN, K=16, fp32 accumulation in TMEM), releasing each
+//               stage with tcgen05.commit;
+//   warps 2-5   finally read the accumulator (tcgen05.ld) and write y, or
+//               split-K partials merged by the last-arriving CTA.
 #include "dq_matmul.cuh"
+#include "tc_common.cuh"
 
 namespace b2 {
 
-bool dq_tc_supported(const DqMmParams &) { return false; }
-size_t dq_tc_workspace(const DqMmParams &) { return 0; }
-int dq_tc_launch(const DqMmParams &, void *, cudaStream_t) {
-  B2_FAIL(B2_ERR_UNSUPPORTED, "tensor-core dequant GEMM not built");
+constexpr int DT_BM = 128;     // weight columns per tile (MMA M)
+constexpr int DT_BK = 64;      // k per stage (one 128-byte swizzle row of fp16)
+constexpr int DT_THREADS = 192;
+constexpr uint32_t DT_AOP_BYTES = DT_BM * DT_BK * 2; // 16 KB dequantized operand
+
+enum DqMode : int { kModeI4H = 0, kModeF8 = 1, kModeF4 = 2, kModeGeneric = 3 };
+
+struct DqTcArgs {
+  DqMmParams p;
+  int bn;          // activation rows per tile (MMA N)
+  int stages;
+  int mode;
+  uint32_t raw_bytes;   // raw weight bytes per stage
+  uint32_t b_bytes;     // activation bytes per stage
+  uint32_t stage_bytes; // raw + aop + b + scales
+  uint32_t s_bytes;     // scale bytes per stage (0: scales read from global memory)
+  int s_rows;           // scale rows per stage
+  int op_bf16;          // MMA operand type: 1 bf16, 0 f16
+  int *status;
+};
+
+// Packs two fp32 values into fp16x2 / bf16x2 bits with the reference's RNE.
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
+  if (bf16) return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+  return (uint32_t)f32_to_f16_bits(lo) | ((uint32_t)f32_to_f16_bits(hi) << 16);
+}
+
+// Dequantizes the 8 weights (k, n..n+7) into 8 operand values (uint4).
+// `srow` points at the staged scale row of this weight row (nullptr: read the
+// scale tensor in global memory).
+__device__ __forceinline__ uint4 dequant8(const DqTcArgs &a, const uint8_t *raw_row, int nl,
+                                          int64_t k, int64_t n, const uint8_t *srow) {
+  const DqMmParams &p = a.p;
+  if (a.mode == kModeI4H) {
+    // int4/uint4 x fp16 scale (blocked along K or per column), fp16 operand.
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(raw_row + nl / 2);
+    const int64_t kb = p.slayout == kScaleAxis0Block ? k / p.block : 0;
+    const int64_t si = p.slayout == kScaleTensor ? 0 : kb * p.N + n;
+    const uint16_t *sp = reinterpret_cast<const uint16_t *>(p.scale);
+    uint32_t s4[4];
+    if (p.slayout == kScaleTensor) {
+      const uint32_t s = sp[0];
+      s4[0] = s4[1] = s4[2] = s4[3] = s | (s << 16);
+    } else {
+      const uint4 v = srow ? *reinterpret_cast<const uint4 *>(srow + nl * 2)
+                           : *reinterpret_cast<const uint4 *>(sp + si);
+      s4[0] = __byte_perm(v.x, v.z, 0x5410); // (0, 4)
+      s4[1] = __byte_perm(v.x, v.z, 0x7632); // (1, 5)
+      s4[2] = __byte_perm(v.y, v.w, 0x5410); // (2, 6)
+      s4[3] = __byte_perm(v.y, v.w, 0x7632); // (3, 7)
+    }
+    const bool sgn = p.wdt == kInt4;
+    const uint32_t x = sgn ? (w ^ 0x88888888u) : w;
+    const uint32_t bias = sgn ? 0x64086408u : 0x64006400u;
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t h = ((x >> (4 * j)) & 0x000f000fu) | 0x64006400u;
+      uint32_t q;
+      asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q) : "r"(h), "r"(bias));
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(q), "r"(s4[j]));
+    }
+    // r[j] = (elem j, elem j+4) -> output order (0,1),(2,3),(4,5),(6,7)
+    uint4 o;
+    o.x = __byte_perm(r[0], r[1], 0x5410);
+    o.y = __byte_perm(r[2], r[3], 0x5410);
+    o.z = __byte_perm(r[0], r[1], 0x7632);
+    o.w = __byte_perm(r[2], r[3], 0x7632);
+    return o;
+  }
+  // fp32 path: value = (q - zp) * s in fp32, rounded to the DequantizeLinear
+  // output type (fp16 when the scale is fp16), then to the operand type.
+  float q[8];
+  if (a.mode == kModeF8) {
+    const uint2 w = *reinterpret_cast<const uint2 *>(raw_row + nl);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = dec_f8e4m3fn(((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xffu);
+  } else if (a.mode == kModeF4) {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(raw_row + nl / 2);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = dec_f4e2m1((w >> (4 * j)) & 0xfu);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = qval(p.wdt, p.w, k * p.N + n + j);
+  }
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    int64_t si;
+    switch (p.slayout) {
+    case kScaleTensor: si = 0; break;
+    case kScaleAxis0Block: si = (k / p.block) * p.N + n + j; break;
+    case kScaleAxis0: si = k; break;
+    case kScaleAxis1Block: si = k * p.s_alen + (n + j) / p.block; break;
+    default: si = n + j; break;
+    }
+    float s;
+    if (srow) s = p.s_f16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t *>(srow)[nl + j])
+                          : reinterpret_cast<const float *>(srow)[nl + j];
+    else s = p.s_f16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t *>(p.scale)[si])
+                     : reinterpret_cast<const float *>(p.scale)[si];
+    const float z = p.zp ? qval(p.wdt, p.zp, si) : 0.0f;
+    float x = x86_mul(x86_sub(q[j], z), s);
+    if (p.s_f16) x = f16_bits_to_f32(f32_to_f16_bits(x));
+    v[j] = x;
+  }
+  const bool bf = a.op_bf16 != 0;
+  return make_uint4(pack2(v[0], v[1], bf), pack2(v[2], v[3], bf), pack2(v[4], v[5], bf),
+                    pack2(v[6], v[7], bf));
+}
+
+__device__ __forceinline__ void store_val(const DqMmParams &p, int64_t m, int64_t n, float v) {
+  if (p.ydt == kFloat16) reinterpret_cast<uint16_t *>(p.y)[m * p.N + n] = f32_to_f16_bits(v);
+  else reinterpret_cast<uint16_t *>(p.y)[m * p.N + n] = f32_to_bf16_bits(v);
+}
+
+__global__ void __launch_bounds__(DT_THREADS, 1)
+    dq_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
+                      const __grid_constant__ CUtensorMap map_s, const DqTcArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const DqMmParams &p = args.p;
+  const int S = args.stages;
+  // ring layout per stage: [aop 16 KB][b bn*128 B][raw]
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * args.stage_bytes);
+  uint64_t *deq = full + S;
+  uint64_t *empty = deq + S;
+  uint64_t *done = empty + S;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  __shared__ volatile int abort_flag;
+  __shared__ bool last_cta;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n0 = (int64_t)blockIdx.x * DT_BM;
+  const int64_t m0 = (int64_t)blockIdx.y * args.bn;
+  const int split = blockIdx.z;
+  const int64_t kbeg = (int64_t)split * p.kchunk;
+  const int64_t kend = min(p.K, kbeg + p.kchunk);
+  const int kt_count = (int)((kend - kbeg + DT_BK - 1) / DT_BK);
+  const uint32_t tmem_cols = args.bn <= 32 ? 32 : args.bn <= 64 ? 64 : args.bn <= 128 ? 128 : 256;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < S; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&deq[s], 4);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(done, 1);
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, tmem_cols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (tc::elect_one()) {
+      tc::prefetch_tensormap(&map_w);
+      tc::prefetch_tensormap(&map_a);
+      if (args.s_bytes) tc::prefetch_tensormap(&map_s);
+      for (int kt = 0; kt < kt_count; ++kt) {
+        const int s = kt % S;
+        if (kt >= S && !tc::mbar_wait(&empty[s], ((kt / S) - 1) & 1)) {
+          atomicExch(args.status, tc::kTimeoutEmpty);
+          abort_flag = 1;
+          break;
+        }
+        uint8_t *st = smem + (size_t)s * args.stage_bytes;
+        const int32_t k = (int32_t)(kbeg + (int64_t)kt * DT_BK);
+        const bool raw_tma = args.mode != kModeGeneric;
+        tc::mbar_expect_tx(&full[s], (raw_tma ? args.raw_bytes : 0u) + args.b_bytes + args.s_bytes);
+        tc::tma_load_2d(st + DT_AOP_BYTES, &map_a, &full[s], k, (int32_t)m0);
+        if (args.s_bytes)
+          tc::tma_load_2d(st + DT_AOP_BYTES + args.b_bytes + args.raw_bytes, &map_s, &full[s],
+                          (int32_t)n0, (int32_t)(k / p.block));
+        if (raw_tma) {
+          // raw weights: [k rows][128 n] as bytes (int4: 64 bytes, 8-bit: 128 bytes per row)
+          const int32_t xb = args.mode == kModeF8 ? (int32_t)n0 : (int32_t)(n0 / 2);
+          tc::tma_load_2d(st + DT_AOP_BYTES + args.b_bytes, &map_w, &full[s], xb, k);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (tc::elect_one()) {
+      const uint32_t id = tc::idesc(1, args.op_bf16, args.op_bf16, 1, 0, DT_BM, (uint32_t)args.bn);
+      for (int kt = 0; kt < kt_count; ++kt) {
+        const int s = kt % S;
+        if (!tc::mbar_wait(&deq[s], (kt / S) & 1)) {
+          atomicExch(args.status, tc::kTimeoutFull);
+          abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t a_base = tc::smem_u32(smem + (size_t)s * args.stage_bytes);
+        const uint32_t b_base = a_base + DT_AOP_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < DT_BK / 16; ++kk) {
+          // A: MN-major, 2 blocks of 64 n (8 KB apart), 8-row atoms along k (1 KB)
+          const uint64_t ad = tc::sdesc_sw128(a_base + kk * 16 * 128, 8192, 1024);
+          // B: K-major activation rows, 128-byte rows, 8-row atoms (1 KB)
+          const uint64_t bd = tc::sdesc_sw128(b_base + kk * 32, 16, 1024);
+          tc::mma_f16(tmem, ad, bd, id, (kt > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::tc_commit(&empty[s]);
+      }
+      tc::tc_commit(done);
+    }
+  } else {
+    // ----- dequant producers (warps 2..5, 128 threads) -----
+    const int t = threadIdx.x - 64;
+    const int cc = t & 15;   // 8-column chunk (n_local = cc * 8)
+    const int r0 = t >> 4;   // first k row (0..7), rows r0 + 8 i
+    const uint32_t raw_row_bytes = args.mode == kModeF8 ? 128 : 64;
+    for (int kt = 0; kt < kt_count && !abort_flag; ++kt) {
+      const int s = kt % S;
+      if (!tc::mbar_wait(&full[s], (kt / S) & 1)) {
+        atomicExch(args.status, tc::kTimeoutFull);
+        abort_flag = 1;
+        break;
+      }
+      uint8_t *st = smem + (size_t)s * args.stage_bytes;
+      const uint8_t *raw = st + DT_AOP_BYTES + args.b_bytes;
+      const uint8_t *sst = args.s_bytes ? raw + args.raw_bytes : nullptr;
+      const int64_t kst = kbeg + (int64_t)kt * DT_BK; // first k of the stage
+      const uint32_t s_esz = p.s_f16 ? 2u : 4u;
+#pragma unroll 2
+      for (int i = 0; i < DT_BK / 8; ++i) {
+        const int r = r0 + 8 * i; // k row within the stage
+        const int64_t k = kst + r;
+        const int nl = cc * 8;
+        const uint8_t *srow =
+            sst ? sst + (size_t)(k / p.block - kst / p.block) * DT_BM * s_esz : nullptr;
+        uint4 o = make_uint4(0, 0, 0, 0);
+        if (k < kend && n0 + nl < p.N) o = dequant8(args, raw + r * raw_row_bytes, nl, k, n0 + nl, srow);
+        // MN-major 128-byte swizzle: block (nl / 64) at 8 KB, row r at 128 B,
+        // 16-byte chunk (nl % 64) / 8 XOR (r % 8)
+        const int blk = nl >> 6, chunk = (nl & 63) >> 3;
+        uint8_t *dst = st + blk * 8192 + r * 128 + ((chunk ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4 *>(dst) = o;
+      }
+      tc::fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&deq[s]);
+    }
+    // ----- epilogue -----
+    const int g = warp & 3; // TMEM lane group
+    const bool ok = tc::mbar_wait(done, 0, 4000000000ull);
+    if (!ok) atomicExch(args.status, tc::kTimeoutMma);
+    tc::tc_fence_after();
+    const int64_t n = n0 + g * 32 + lane;
+    if (ok && !abort_flag) {
+      float *part = p.ksplit > 1 ? p.partials + (int64_t)split * p.M * p.N : nullptr;
+      for (int ch = 0; ch < args.bn / 32 + ((args.bn & 31) ? 1 : 0); ++ch) {
+        uint32_t r[32];
+        tc::tmem_ld32(tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(ch * 32), r);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int64_t m = m0 + ch * 32 + j;
+          if (ch * 32 + j < args.bn && m < p.M && n < p.N) {
+            const float v = __uint_as_float(r[j]);
+            if (part) part[m * p.N + n] = v;
+            else store_val(p, m, n, v);
+          }
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, tmem_cols);
+  if (p.ksplit <= 1 || abort_flag) return;
+  // split-K: the last CTA of this output tile sums the partials in split order
+  if (threadIdx.x == 0) {
+    __threadfence();
+    uint32_t *ctr = p.counters + (blockIdx.y * gridDim.x + blockIdx.x);
+    const uint32_t prev = atomicAdd(ctr, 1u);
+    last_cta = prev + 1 == (uint32_t)p.ksplit;
+    if (last_cta) {
+      __threadfence();
+      *ctr = 0u;
+    }
+  }
+  __syncthreads();
+  if (!last_cta) return;
+  for (int e = threadIdx.x; e < DT_BM * args.bn; e += DT_THREADS) {
+    const int64_t m = m0 + e / DT_BM, n = n0 + e % DT_BM;
+    if (m >= p.M || n >= p.N) continue;
+    float s = 0.0f;
+    for (int sp = 0; sp < p.ksplit; ++sp) s += __ldcg(p.partials + ((int64_t)sp * p.M + m) * p.N + n);
+    store_val(p, m, n, s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+static int dq_tc_mode(const DqMmParams &p) {
+  if ((p.wdt == kInt4 || p.wdt == kUint4) && p.s_f16 && p.zp == nullptr && p.ydt == kFloat16 &&
+      (p.cast_dt == 0 || p.cast_dt == kFloat16) &&
+      (p.slayout == kScaleTensor || (p.slayout == kScaleAxis0Block && p.block % 8 == 0) ||
+       p.slayout == kScaleAxis1))
+    return kModeI4H;
+  if (p.wdt == kF8E4M3FN) return kModeF8;
+  if (p.wdt == kF4E2M1) return kModeF4;
+  return kModeGeneric;
+}
+
+struct TcPlan {
+  int bn = 0, stages = 0, ksplit = 1, mode = 0, s_rows = 0;
+  uint32_t s_bytes = 0;
+  int64_t kchunk = 0;
+  uint32_t raw_bytes = 0, b_bytes = 0, stage_bytes = 0;
+  size_t smem = 0;
+  dim3 grid;
+};
+
+static TcPlan tc_plan(const DqMmParams &p) {
+  TcPlan t;
+  t.mode = dq_tc_mode(p);
+  t.bn = p.M >= 256 ? 256 : (int)((p.M + 15) / 16 * 16);
+  if (t.bn < 16) t.bn = 16;
+  t.raw_bytes = (t.mode == kModeF8 ? 128u : 64u) * DT_BK;
+  if (t.mode == kModeGeneric) t.raw_bytes = 64u * DT_BK; // raw tile unused, keep the ring uniform
+  t.b_bytes = (uint32_t)t.bn * 128u;
+  // Blocked-along-K scales are staged per stage by TMA: ceil(64 / block) rows
+  // of 128 columns (the stage start is block-aligned when block >= 64).
+  const uint32_t s_esz = p.s_f16 ? 2u : 4u;
+  const bool s_ok = p.slayout == kScaleAxis0Block && t.mode != kModeGeneric &&
+                    (p.block % DT_BK == 0 || DT_BK % p.block == 0) &&
+                    ((uint64_t)p.N * s_esz) % 16 == 0;
+  t.s_rows = s_ok ? (p.block >= DT_BK ? 1 : (int)(DT_BK / p.block)) : 0;
+  t.s_bytes = (uint32_t)t.s_rows * DT_BM * s_esz;
+  t.stage_bytes = DT_AOP_BYTES + t.b_bytes + t.raw_bytes + t.s_bytes;
+  t.stage_bytes = (t.stage_bytes + 1023) & ~1023u;
+  const size_t budget = 220 * 1024;
+  t.stages = (int)std::min<size_t>(6, budget / t.stage_bytes);
+  t.smem = (size_t)t.stages * t.stage_bytes + 1024 + 256;
+  const int64_t ntiles = (p.N + DT_BM - 1) / DT_BM, mtiles = (p.M + t.bn - 1) / t.bn;
+  const int sms = sm_count();
+  int64_t split = 1;
+  if (ntiles * mtiles < sms && ntiles * mtiles <= (int64_t)kMaxCounters) {
+    split = (sms + ntiles * mtiles - 1) / (ntiles * mtiles);
+    const int64_t maxsplit = (p.K + 4 * DT_BK - 1) / (4 * DT_BK); // >= 4 stages per split
+    if (split > maxsplit) split = maxsplit;
+    if (split < 1) split = 1;
+  }
+  int64_t kchunk = (p.K + split - 1) / split;
+  kchunk = (kchunk + DT_BK - 1) / DT_BK * DT_BK;
+  t.kchunk = kchunk;
+  t.ksplit = (int)((p.K + kchunk - 1) / kchunk);
+  t.grid = dim3((unsigned)ntiles, (unsigned)mtiles, (unsigned)t.ksplit);
+  return t;
+}
+
+bool dq_tc_supported(const DqMmParams &p) { return p.M > 4 && dq_tc_eligible(p); }
+
+bool dq_tc_eligible(const DqMmParams &p) {
+  if (p.ydt != kFloat16 && p.ydt != kBfloat16) return false;
+  // TMA: activation rows K * 2 bytes and packed weight rows must be 16-byte multiples.
+  if ((p.K * 2) % 16 != 0) return false;
+  const int mode = dq_tc_mode(p);
+  const int64_t wrow = mode == kModeF8 ? p.N : p.N / 2;
+  if (mode != kModeGeneric && ((wrow % 16) != 0 || (p.N % 2) != 0)) return false;
+  if (mode == kModeGeneric && (p.N % 8) != 0) return false;
+  if (mode == kModeI4H && p.slayout != kScaleTensor && (p.N % 8) != 0) return false;
+  return p.K >= DT_BK && p.N >= 8;
+}
+
+size_t dq_tc_workspace(const DqMmParams &p) {
+  const TcPlan t = tc_plan(p);
+  size_t ws = kCounterBytes;
+  if (t.ksplit > 1) ws += (size_t)t.ksplit * p.M * p.N * 4;
+  return ws;
+}
+
+int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st) {
+  const TcPlan t = tc_plan(pin);
+  DqTcArgs a{};
+  a.p = pin;
+  a.p.kchunk = t.kchunk;
+  a.p.ksplit = t.ksplit;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  a.status = reinterpret_cast<int *>(ws + kStatusOffset);
+  if (t.ksplit > 1) {
+    a.p.counters = reinterpret_cast<uint32_t *>(ws);
+    a.p.partials = reinterpret_cast<float *>(ws + kCounterBytes);
+  }
+  a.bn = t.bn;
+  a.stages = t.stages;
+  a.mode = t.mode;
+  a.raw_bytes = t.raw_bytes;
+  a.b_bytes = t.b_bytes;
+  a.stage_bytes = t.stage_bytes;
+  a.s_bytes = t.s_bytes;
+  a.s_rows = t.s_rows;
+  a.op_bf16 = pin.ydt == kBfloat16;
+  CUtensorMap map_a, map_w, map_s;
+  if (t.s_bytes) {
+    // scales [K / block, N] (FLOAT16 or FLOAT), box 128 columns x s_rows rows
+    const uint64_t esz = pin.s_f16 ? 2 : 4;
+    const uint64_t dims[2] = {(uint64_t)pin.N, (uint64_t)(pin.K / pin.block)};
+    const uint64_t strides[1] = {(uint64_t)pin.N * esz};
+    const uint32_t box[2] = {(uint32_t)DT_BM, (uint32_t)t.s_rows};
+    int rc = make_tensor_map(&map_s, pin.s_f16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32,
+                             2, pin.scale, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  {
+    // activations [M, K] 16-bit, K innermost; box 64 k x bn rows, 128-byte swizzle
+    const uint64_t dims[2] = {(uint64_t)pin.K, (uint64_t)pin.M};
+    const uint64_t strides[1] = {(uint64_t)pin.K * 2};
+    const uint32_t box[2] = {64, (uint32_t)t.bn};
+    int rc = make_tensor_map(&map_a, a.op_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                             2, pin.a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    // packed weights as bytes [K, row_bytes]; box 128 n (64 or 128 bytes) x 64 k
+    const bool is8 = t.mode == kModeF8;
+    const uint64_t row = is8 ? (uint64_t)pin.N : (uint64_t)pin.N / 2;
+    const uint64_t dims[2] = {row, (uint64_t)pin.K};
+    const uint64_t strides[1] = {row};
+    const uint32_t box[2] = {is8 ? 128u : 64u, (uint32_t)DT_BK};
+    if (t.mode == kModeGeneric) {
+      // the generic path reads weights with plain loads; the map is not used
+      map_w = map_a;
+    } else {
+      int rc = make_tensor_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, pin.w, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+    }
+  }
+  if (!t.s_bytes) map_s = map_a; // unused
+  B2_CUDA(cudaFuncSetAttribute(dq_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)t.smem));
+  dq_gemm_tc_kernel<<<t.grid, DT_THREADS, t.smem, st>>>(map_w, map_a, map_s, a);
+  B2_LAUNCH_CHECK();
+  return B2_OK;
 }
 
 } // namespace b2

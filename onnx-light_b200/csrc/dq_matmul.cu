@@ -22,6 +22,10 @@
 //    tcgen05 tensor cores.
 #include "b2_common.cuh"
 #include "dq_matmul.cuh"
+#include "tc_common.cuh"
+
+#include <cstdlib>
+#include <cstring>
 
 namespace b2 {
 
@@ -243,100 +247,21 @@ __device__ __forceinline__ void int4x8_times_scale_f16(uint32_t w, bool is_signe
   }
 }
 
-// Nibble order of the (j, j+4) pairing above: word element e = 4*hi + j.
 __device__ __forceinline__ float act_load_rt(const DqMmParams &p, int64_t i) {
   if (p.ydt == kFloat) return act_load<float>(p.a, i);
   if (p.ydt == kFloat16) return act_load<__half>(p.a, i);
   return act_load<__nv_bfloat16>(p.a, i);
 }
 
-template <int MT, int BITS, bool FAST16>
-__global__ void __launch_bounds__(GEMV_THREADS) dq_gemv(const DqMmParams p) {
-  extern __shared__ float smem[];
-  // smem: activations [MT][kchunk] fp32, then per-warp reduction buffer
-  float *a_s = smem;
-  float *red = smem + MT * p.kchunk;
+// Reduction epilogue shared by the GEMV kernels: acc[m][j] holds this lane's
+// partial sums for columns ncol..ncol+31 of row group r.  Lanes r = 0..3 are
+// summed with shuffles, warps through shared memory, CTAs (split-K) through
+// the workspace partials and the last-arriving CTA.
+template <int MT>
+__device__ __forceinline__ void gemv_reduce(const DqMmParams &p, float (&acc)[MT][32], float *red,
+                                            int64_t n0, int split) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = lane & 7, r = lane >> 3;
-  const int64_t n0 = (int64_t)blockIdx.x * GEMV_TN;
-  const int64_t ncol = n0 + c * 32;
-  const int split = blockIdx.y;
-  const int64_t kbeg = (int64_t)split * p.kchunk;
-  const int64_t kend = min((int64_t)p.K, kbeg + p.kchunk);
-  const int64_t klen = kend - kbeg;
-  for (int e = threadIdx.x; e < MT * p.kchunk; e += GEMV_THREADS) {
-    const int mm = e / p.kchunk;
-    const int64_t kk = e % p.kchunk;
-    a_s[e] = (mm < p.M && kk < klen) ? act_load_rt(p, (int64_t)mm * p.K + kbeg + kk) : 0.0f;
-  }
-  __syncthreads();
-
-  float acc[MT][32];
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int j = 0; j < 32; ++j) acc[m][j] = 0.0f;
-
-  const bool col_ok = ncol + 32 <= p.N;
-  float sc[32], zc[32];
-  int64_t cur_kb = -1;
-  const int64_t row_bytes = p.N * BITS / 8;
-  const uint8_t *wcol = p.w + ncol * BITS / 8;
-  for (int64_t kk = warp * 4 + r; kk < klen; kk += 32) {
-    const int64_t k = kbeg + kk;
-    if (!col_ok) break;
-    // per-row scale / zero point for this lane's 32 columns
-    const int64_t kb = p.slayout == kScaleAxis0Block ? k / p.block : 0;
-    if (kb != cur_kb) {
-      cur_kb = kb;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int64_t si = p.slayout == kScaleTensor ? 0
-                           : p.slayout == kScaleAxis0Block ? kb * p.N + ncol + j
-                                                           : ncol + j;
-        sc[j] = p.s_f16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t *>(p.scale)[si])
-                        : reinterpret_cast<const float *>(p.scale)[si];
-        zc[j] = p.zp ? qval(p.wdt, p.zp, si) : 0.0f;
-      }
-    }
-    uint4 raw[BITS / 4];
-    gemv_load<BITS>(wcol + k * row_bytes, raw);
-    float wv[32];
-    if (FAST16) {
-      __half2 s2[4], o[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t words[4] = {raw[0].x, raw[0].y, raw[0].z, raw[0].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) s2[j] = __floats2half2_rn(sc[q * 8 + j], sc[q * 8 + j + 4]);
-        int4x8_times_scale_f16(words[q], p.wdt == kInt4, s2, o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          wv[q * 8 + j] = __low2float(o[j]);
-          wv[q * 8 + j + 4] = __high2float(o[j]);
-        }
-      }
-      if (p.cast_dt) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) wv[j] = round_to(wv[j], p.cast_dt);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float v = x86_mul(x86_sub(gemv_q<BITS>(p.wdt, raw, j), zc[j]), sc[j]);
-        v = round_to(v, p.s_f16 ? kFloat16 : kFloat);
-        if (p.cast_dt) v = round_to(v, p.cast_dt);
-        wv[j] = v;
-      }
-    }
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      const float av = a_s[m * p.kchunk + kk];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) acc[m][j] = fmaf(av, wv[j], acc[m][j]);
-    }
-  }
-  // reduce the 4 row-lanes (r) sharing a column chunk
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -344,7 +269,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) dq_gemv(const DqMmParams p) {
       acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], 8);
       acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], 16);
     }
-  // warps -> shared: red[warp][m][256]
+  __syncthreads(); // red may alias staging buffers
   if (r == 0) {
 #pragma unroll
     for (int m = 0; m < MT; ++m)
@@ -374,6 +299,291 @@ __global__ void __launch_bounds__(GEMV_THREADS) dq_gemv(const DqMmParams p) {
     for (int sp = 0; sp < p.ksplit; ++sp)
       s += __ldcg(p.partials + ((int64_t)sp * p.M + m) * p.N + gn);
     store_out(p.y, p.ydt, (int64_t)m * p.N + gn, s);
+  }
+}
+
+// fp32 += fp16 * fp16 with one rounding (mixed-precision FMA, sm_100).
+__device__ __forceinline__ float fma_f16(uint16_t a, uint16_t b, float c) {
+  asm("fma.rn.f32.f16 %0, %1, %2, %0;" : "+f"(c) : "h"(a), "h"(b));
+  return c;
+}
+
+// Generic decode GEMV: any 4-/8-bit weight type, zero points, FLOAT/FLOAT16
+// scales, any activation type; "column" scale layouts only.
+template <int MT, int BITS>
+__global__ void __launch_bounds__(GEMV_THREADS) dq_gemv(const DqMmParams p) {
+  extern __shared__ float smem[];
+  float *a_s = smem;                  // [MT][kchunk] fp32 activations
+  float *red = smem + MT * p.kchunk;  // [8][MT][256] reduction
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = lane & 7, r = lane >> 3;
+  const int64_t n0 = (int64_t)blockIdx.x * GEMV_TN;
+  const int64_t ncol = n0 + c * 32;
+  const int split = blockIdx.y;
+  const int64_t kbeg = (int64_t)split * p.kchunk;
+  const int64_t kend = min((int64_t)p.K, kbeg + p.kchunk);
+  const int64_t klen = kend - kbeg;
+  for (int e = threadIdx.x; e < MT * p.kchunk; e += GEMV_THREADS) {
+    const int mm = e / p.kchunk;
+    const int64_t kk = e % p.kchunk;
+    a_s[e] = (mm < p.M && kk < klen) ? act_load_rt(p, (int64_t)mm * p.K + kbeg + kk) : 0.0f;
+  }
+  __syncthreads();
+  float acc[MT][32];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[m][j] = 0.0f;
+  const bool col_ok = ncol + 32 <= p.N;
+  float sc[32], zc[32];
+  int64_t cur_kb = -1;
+  const int64_t row_bytes = p.N * BITS / 8;
+  const uint8_t *wcol = p.w + ncol * BITS / 8;
+  constexpr int U = 4;
+  for (int64_t kk0 = warp * 4 + r; col_ok && kk0 < klen; kk0 += 32 * U) {
+    uint4 raw[U][BITS / 4];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t kk = kk0 + 32 * u;
+      if (kk < klen) gemv_load<BITS>(wcol + (kbeg + kk) * row_bytes, raw[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t kk = kk0 + 32 * u;
+      if (kk >= klen) break;
+      const int64_t k = kbeg + kk;
+      const int64_t kb = p.slayout == kScaleAxis0Block ? k / p.block : 0;
+      if (kb != cur_kb) {
+        cur_kb = kb;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int64_t si = p.slayout == kScaleTensor ? 0
+                             : p.slayout == kScaleAxis0Block ? kb * p.N + ncol + j
+                                                             : ncol + j;
+          sc[j] = p.s_f16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t *>(p.scale)[si])
+                          : reinterpret_cast<const float *>(p.scale)[si];
+          zc[j] = p.zp ? qval(p.wdt, p.zp, si) : 0.0f;
+        }
+      }
+      float wv[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float v = x86_mul(x86_sub(gemv_q<BITS>(p.wdt, raw[u], j), zc[j]), sc[j]);
+        v = round_to(v, p.s_f16 ? kFloat16 : kFloat);
+        if (p.cast_dt) v = round_to(v, p.cast_dt);
+        wv[j] = v;
+      }
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const float av = a_s[m * p.kchunk + kk];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[m][j] = fmaf(av, wv[j], acc[m][j]);
+      }
+    }
+  }
+  gemv_reduce<MT>(p, acc, red, n0, split);
+}
+
+// Decode GEMV fast path: INT4/UINT4 weights, FLOAT16 scales (blocked along K
+// with block % 32 == 0, per-tensor, or per-column), no zero point, FLOAT16
+// activations and output.
+//
+// The packed weight rows of the CTA's [kchunk x 256] tile stream through an
+// 8-stage shared-memory ring (32 rows x 128 bytes per stage) filled by TMA
+// from a dedicated producer warp, so 32 KB per CTA stay in flight whatever
+// the consumers are doing.  The CTA's scale rows are staged once with bulk
+// copies.  Each consumer lane takes one weight row segment of 32 nibbles per
+// stage: magic-number nibble -> fp16 conversion, fp16 product with the scale
+// (the correctly rounded fp16 of the exact product, i.e. the reference's
+// FloatToFloat16Bits((q - 0) * s)), and fp32 accumulation with the
+// mixed-precision FMA.
+constexpr int GV_STAGES = 8, GV_ROWS = 32, GV_CONSUMERS = 256, GV_THREADS = 288;
+constexpr uint32_t GV_STAGE_BYTES = GV_ROWS * 128;
+
+template <int MT>
+__global__ void __launch_bounds__(GV_THREADS, MT == 1 ? 2 : 1)
+    dq_gemv_i4h(const __grid_constant__ CUtensorMap map_w, const DqMmParams p) {
+  extern __shared__ __align__(1024) uint8_t gsm[];
+  uint8_t *ring = gsm;                                                 // [S][32][128]
+  __half *s_s = reinterpret_cast<__half *>(gsm + GV_STAGES * GV_STAGE_BYTES); // [nkb][256]
+  __half *a_s = s_s + (size_t)p.gemv_nkb * GEMV_TN;                    // [MT][kchunk]
+  uint64_t *full = reinterpret_cast<uint64_t *>(
+      (reinterpret_cast<uintptr_t>(a_s + (size_t)MT * p.kchunk) + 15) & ~uintptr_t(15));
+  uint64_t *empty = full + GV_STAGES;
+  uint64_t *sbar = empty + GV_STAGES;
+  float *red = reinterpret_cast<float *>(gsm);                         // reuses the ring
+  __shared__ volatile int abort_flag;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = lane & 7, r = lane >> 3;
+  const int64_t n0 = (int64_t)blockIdx.x * GEMV_TN;
+  const int split = blockIdx.y;
+  const int64_t kbeg = (int64_t)split * p.kchunk;
+  const int64_t kend = min((int64_t)p.K, kbeg + p.kchunk);
+  const int64_t klen = kend - kbeg;
+  const int ntiles = (int)((klen + GV_ROWS - 1) / GV_ROWS);
+  const int64_t kb0 = p.slayout == kScaleAxis0Block ? kbeg / p.block : 0;
+  const int nrows_s = p.slayout == kScaleAxis0Block ? (int)((kend - 1) / p.block - kb0 + 1) : 1;
+  int *status = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(p.counters) + kStatusOffset);
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < GV_STAGES; ++i) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], GV_CONSUMERS / 32);
+    }
+    tc::mbar_init(sbar, 1);
+    tc::fence_barrier_init();
+  }
+  // Activations of this K range, staged by every thread before the roles
+  // split (no block-wide barrier may follow the split until both roles are
+  // done, or the producer's ring waits would deadlock against it).
+  for (int e = threadIdx.x; e < MT * p.kchunk; e += GV_THREADS) {
+    const int mm = e / p.kchunk;
+    const int64_t kk = e % p.kchunk;
+    a_s[e] = (mm < p.M && kk < klen)
+                 ? reinterpret_cast<const __half *>(p.a)[(int64_t)mm * p.K + kbeg + kk]
+                 : __ushort_as_half(0);
+  }
+  __syncthreads();
+
+  if (warp == GV_CONSUMERS / 32) {
+    // ---------------- producer warp ----------------
+    if (tc::elect_one()) {
+      tc::prefetch_tensormap(&map_w);
+      if (p.slayout == kScaleTensor) {
+        const __half v = reinterpret_cast<const __half *>(p.scale)[0];
+        for (int i = 0; i < GEMV_TN; ++i) s_s[i] = v;
+        tc::mbar_arrive(sbar); // release semantics publish the stores above
+      } else {
+        tc::mbar_expect_tx(sbar, (uint32_t)(nrows_s * GEMV_TN * 2));
+        for (int i = 0; i < nrows_s; ++i) {
+          const int64_t srow = p.slayout == kScaleAxis0Block ? kb0 + i : 0;
+          const uint8_t *src = p.scale + (srow * p.N + n0) * 2;
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+              ::"r"(tc::smem_u32(s_s + (size_t)i * GEMV_TN)), "l"(src), "r"(GEMV_TN * 2),
+              "r"(tc::smem_u32(sbar))
+              : "memory");
+        }
+      }
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % GV_STAGES;
+        if (t >= GV_STAGES && !tc::mbar_wait(&empty[s], ((t / GV_STAGES) - 1) & 1)) {
+          atomicExch(status, tc::kTimeoutEmpty);
+          abort_flag = 1;
+          break;
+        }
+        tc::mbar_expect_tx(&full[s], GV_STAGE_BYTES);
+        tc::tma_load_2d(ring + s * GV_STAGE_BYTES, &map_w, &full[s], (int32_t)(n0 / 2),
+                        (int32_t)(kbeg + (int64_t)t * GV_ROWS));
+      }
+    }
+    __syncwarp();
+  }
+  float acc[MT][32];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[m][j] = 0.0f;
+
+  if (warp < GV_CONSUMERS / 32) {
+    bool ok = tc::mbar_wait(sbar, 0);
+    if (!ok) {
+      atomicExch(status, tc::kTimeoutFull);
+      abort_flag = 1;
+    }
+    const bool is_signed = p.wdt == kInt4;
+    const uint32_t flip = is_signed ? 0x88888888u : 0u;
+    const uint32_t bias_bits = is_signed ? 0x64086408u : 0x64006400u;
+    const int row = warp * 4 + r; // row within a stage
+    uint32_t s2[16];
+    int cur_sr = -1;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const int s = t % GV_STAGES;
+      if (!tc::mbar_wait(&full[s], (t / GV_STAGES) & 1)) {
+        atomicExch(status, tc::kTimeoutFull);
+        abort_flag = 1;
+        break;
+      }
+      const int64_t kk = (int64_t)t * GV_ROWS + row;
+      const uint4 raw = *reinterpret_cast<const uint4 *>(ring + s * GV_STAGE_BYTES + row * 128 + c * 16);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty[s]);
+      if (kk >= klen) continue;
+      const int sr = p.slayout == kScaleAxis0Block ? (int)((kbeg + kk) / p.block - kb0) : 0;
+      if (sr != cur_sr) {
+        cur_sr = sr;
+        const uint4 *sp = reinterpret_cast<const uint4 *>(s_s + (size_t)sr * GEMV_TN + c * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 v = sp[q]; // halves q*8 .. q*8+7
+          s2[q * 4 + 0] = __byte_perm(v.x, v.z, 0x5410); // (0, 4)
+          s2[q * 4 + 1] = __byte_perm(v.x, v.z, 0x7632); // (1, 5)
+          s2[q * 4 + 2] = __byte_perm(v.y, v.w, 0x5410); // (2, 6)
+          s2[q * 4 + 3] = __byte_perm(v.y, v.w, 0x7632); // (3, 7)
+        }
+      }
+      uint16_t av[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) av[m] = __half_as_ushort(a_s[m * p.kchunk + kk]);
+      const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t x = words[q] ^ flip;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint32_t h = ((x >> (4 * jj)) & 0x000f000fu) | 0x64006400u;
+          uint32_t qh, w2;
+          asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(qh) : "r"(h), "r"(bias_bits));
+          asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w2) : "r"(qh), "r"(s2[q * 4 + jj]));
+          const uint16_t wl = (uint16_t)(w2 & 0xffffu), wh = (uint16_t)(w2 >> 16);
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            acc[m][q * 8 + jj] = fma_f16(av[m], wl, acc[m][q * 8 + jj]);
+            acc[m][q * 8 + jj + 4] = fma_f16(av[m], wh, acc[m][q * 8 + jj + 4]);
+          }
+        }
+      }
+    }
+    // reduce the 4 row-lanes (r) sharing a column chunk
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], 8);
+        acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], 16);
+      }
+  }
+  __syncthreads(); // the ring is free: reuse it for the cross-warp reduction
+  if (warp < GV_CONSUMERS / 32 && r == 0) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) red[(warp * MT + m) * GEMV_TN + c * 32 + j] = acc[m][j];
+  }
+  __syncthreads();
+  float *part = p.ksplit > 1 ? p.partials + (int64_t)split * p.M * p.N : nullptr;
+  for (int e = threadIdx.x; e < MT * GEMV_TN; e += GV_THREADS) {
+    const int m = e / GEMV_TN, nn = e % GEMV_TN;
+    float sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < GV_CONSUMERS / 32; ++w) sum += red[(w * MT + m) * GEMV_TN + nn];
+    const int64_t gn = n0 + nn;
+    if (m < p.M && gn < p.N && !abort_flag) {
+      if (part) part[(int64_t)m * p.N + gn] = sum;
+      else store_out(p.y, p.ydt, (int64_t)m * p.N + gn, sum);
+    }
+  }
+  if (!part || abort_flag) return;
+  if (!arrive_last(p.counters + blockIdx.x, p.ksplit)) return;
+  for (int e = threadIdx.x; e < MT * GEMV_TN; e += GV_THREADS) {
+    const int m = e / GEMV_TN;
+    const int64_t gn = n0 + e % GEMV_TN;
+    if (m >= p.M || gn >= p.N) continue;
+    float sum = 0.0f;
+    for (int sp = 0; sp < p.ksplit; ++sp)
+      sum += __ldcg(p.partials + ((int64_t)sp * p.M + m) * p.N + gn);
+    store_out(p.y, p.ydt, (int64_t)m * p.N + gn, sum);
   }
 }
 
@@ -436,6 +646,7 @@ struct Plan {
   int mt = 1;
   int bits = 4;
   bool fast16 = false;
+  int nkb = 0;
   size_t ws = 0;
 };
 
@@ -445,27 +656,46 @@ static int wbits(int dt) {
   return 0;
 }
 
+// Kernel selection.  ONNXL_B200_DQ_KERNEL=tc|gemv|simt forces one family
+// (tests use it to exercise every kernel on the same shapes); the default
+// picks the decode GEMV for M <= 4, the tensor-core kernel for 16-bit
+// activations otherwise, and the CUDA-core GEMM for FLOAT activations.
+enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3 };
+
+static DqPath forced_path() {
+  const char *e = getenv("ONNXL_B200_DQ_KERNEL");
+  if (!e) return kPathAuto;
+  if (!strcmp(e, "tc")) return kPathTc;
+  if (!strcmp(e, "gemv")) return kPathGemv;
+  if (!strcmp(e, "simt")) return kPathSimt;
+  return kPathAuto;
+}
+
 static Plan make_plan(const DqMmParams &p) {
   Plan pl;
   const int sms = sm_count();
   const int bits = wbits(p.wdt);
   const bool col_layout = p.slayout == kScaleTensor || p.slayout == kScaleAxis0Block ||
                           p.slayout == kScaleAxis1;
-  const bool fast16 = (p.wdt == kInt4 || p.wdt == kUint4) && p.s_f16 && p.zp == nullptr;
+  const bool fast16 = (p.wdt == kInt4 || p.wdt == kUint4) && p.s_f16 && p.zp == nullptr &&
+                      p.ydt == kFloat16 && (p.cast_dt == 0 || p.cast_dt == kFloat16) &&
+                      p.N % GEMV_TN == 0;
   const bool gemv_ok = p.M <= (fast16 ? 4 : 2) && bits && col_layout && p.N % 32 == 0 &&
                        (p.slayout != kScaleAxis0Block || p.block % 32 == 0) &&
                        ((p.N * bits / 8) % 16 == 0);
-  if (dq_tc_supported(p)) {
+  const DqPath forced = forced_path();
+  if ((forced == kPathAuto && dq_tc_supported(p)) || (forced == kPathTc && dq_tc_eligible(p))) {
     pl.kind = 2;
     pl.ws = dq_tc_workspace(p);
     return pl;
   }
-  if (gemv_ok) {
+  if (gemv_ok && (forced == kPathAuto || forced == kPathGemv || forced == kPathTc)) {
     pl.kind = 1;
     pl.bits = bits;
     pl.mt = p.M <= 1 ? 1 : p.M <= 2 ? 2 : 4;
     pl.fast16 = fast16;
     const int64_t ntiles = (p.N + GEMV_TN - 1) / GEMV_TN;
+    // about two CTAs per SM in one wave
     int64_t want = (2 * sms + ntiles - 1) / ntiles;
     int64_t kchunk = (p.K + want - 1) / want;
     const int64_t align = p.slayout == kScaleAxis0Block ? std::max<int64_t>(32, p.block) : 32;
@@ -473,9 +703,21 @@ static Plan make_plan(const DqMmParams &p) {
     if (kchunk < 32) kchunk = 32;
     pl.kchunk = kchunk;
     pl.ksplit = (int)((p.K + kchunk - 1) / kchunk);
+    if (pl.ksplit > 1 && ntiles > (int64_t)kMaxCounters) {
+      pl.kchunk = p.K;
+      pl.ksplit = 1;
+    }
     pl.grid = dim3((unsigned)ntiles, (unsigned)pl.ksplit, 1);
-    pl.smem = (size_t)pl.mt * kchunk * 4 + (size_t)(GEMV_THREADS / 32) * pl.mt * GEMV_TN * 4;
-    if (pl.ksplit > 1) pl.ws = (size_t)pl.ksplit * p.M * p.N * 4 + (size_t)ntiles * 4;
+    const size_t red = (size_t)(GEMV_THREADS / 32) * pl.mt * GEMV_TN * 4;
+    if (fast16) {
+      pl.nkb = p.slayout == kScaleAxis0Block ? (int)(pl.kchunk / p.block) + 1 : 1;
+      pl.smem = (size_t)GV_STAGES * GV_STAGE_BYTES + (size_t)pl.nkb * GEMV_TN * 2 +
+                (size_t)pl.mt * pl.kchunk * 2 + 16 + (2 * GV_STAGES + 1) * 8 + 1024;
+      pl.smem = std::max(pl.smem, red + 1024);
+    } else {
+      pl.smem = (size_t)pl.mt * pl.kchunk * 4 + red;
+    }
+    pl.ws = kCounterBytes + (pl.ksplit > 1 ? (size_t)pl.ksplit * p.M * p.N * 4 : 0);
     return pl;
   }
   pl.kind = 0;
@@ -487,9 +729,12 @@ static Plan make_plan(const DqMmParams &p) {
   if (kchunk < SIMT_BK) kchunk = SIMT_BK;
   pl.kchunk = kchunk;
   pl.ksplit = (int)((p.K + kchunk - 1) / kchunk);
-  if (pl.ksplit < 1) pl.ksplit = 1;
+  if (pl.ksplit < 1 || tn * tm > (int64_t)kMaxCounters) {
+    pl.kchunk = p.K;
+    pl.ksplit = 1;
+  }
   pl.grid = dim3((unsigned)tn, (unsigned)tm, (unsigned)pl.ksplit);
-  if (pl.ksplit > 1) pl.ws = (size_t)pl.ksplit * p.M * p.N * 4 + (size_t)tn * tm * 4;
+  if (pl.ksplit > 1) pl.ws = kCounterBytes + (size_t)pl.ksplit * p.M * p.N * 4;
   return pl;
 }
 
@@ -499,9 +744,8 @@ template <typename T> static int launch_simt(const DqMmParams &p, const Plan &pl
   return B2_OK;
 }
 
-template <int MT, int BITS, bool FAST>
-static int launch_gemv_t(const DqMmParams &p, const Plan &pl, cudaStream_t st) {
-  auto kern = dq_gemv<MT, BITS, FAST>;
+template <typename K>
+static int launch_smem(K kern, const Plan &pl, const DqMmParams &p, cudaStream_t st) {
   if (pl.smem > 48 * 1024)
     B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
   kern<<<pl.grid, GEMV_THREADS, pl.smem, st>>>(p);
@@ -509,20 +753,37 @@ static int launch_gemv_t(const DqMmParams &p, const Plan &pl, cudaStream_t st) {
   return B2_OK;
 }
 
-static int launch_gemv(const DqMmParams &p, const Plan &pl, cudaStream_t st) {
+template <int MT>
+static int launch_gemv_i4h(const DqMmParams &p, const Plan &pl, cudaStream_t st) {
+  CUtensorMap map_w;
+  const uint64_t dims[2] = {(uint64_t)p.N / 2, (uint64_t)p.K};
+  const uint64_t strides[1] = {(uint64_t)p.N / 2};
+  const uint32_t box[2] = {128, GV_ROWS};
+  int rc = make_tensor_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p.w, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  auto kern = dq_gemv_i4h<MT>;
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+  kern<<<pl.grid, GV_THREADS, pl.smem, st>>>(map_w, p);
+  B2_LAUNCH_CHECK();
+  return B2_OK;
+}
+
+static int launch_gemv(DqMmParams p, const Plan &pl, cudaStream_t st) {
+  p.gemv_nkb = pl.nkb;
   if (pl.fast16) {
     switch (pl.mt) {
-    case 1: return launch_gemv_t<1, 4, true>(p, pl, st);
-    case 2: return launch_gemv_t<2, 4, true>(p, pl, st);
-    default: return launch_gemv_t<4, 4, true>(p, pl, st);
+    case 1: return launch_gemv_i4h<1>(p, pl, st);
+    case 2: return launch_gemv_i4h<2>(p, pl, st);
+    default: return launch_gemv_i4h<4>(p, pl, st);
     }
   }
   if (pl.bits == 4) {
-    if (pl.mt == 1) return launch_gemv_t<1, 4, false>(p, pl, st);
-    return launch_gemv_t<2, 4, false>(p, pl, st);
+    if (pl.mt == 1) return launch_smem(dq_gemv<1, 4>, pl, p, st);
+    return launch_smem(dq_gemv<2, 4>, pl, p, st);
   }
-  if (pl.mt == 1) return launch_gemv_t<1, 8, false>(p, pl, st);
-  return launch_gemv_t<2, 8, false>(p, pl, st);
+  if (pl.mt == 1) return launch_smem(dq_gemv<1, 8>, pl, p, st);
+  return launch_smem(dq_gemv<2, 8>, pl, p, st);
 }
 
 } // namespace b2
@@ -548,10 +809,9 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
   p.y = y->data;
   p.kchunk = pl.kchunk;
   p.ksplit = pl.ksplit;
-  if (pl.ksplit > 1) {
-    p.partials = static_cast<float *>(workspace);
-    p.counters = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) +
-                                              (size_t)pl.ksplit * p.M * p.N * 4);
+  if (workspace) {
+    p.counters = static_cast<uint32_t *>(workspace);
+    p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kCounterBytes);
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p.K == 0) {

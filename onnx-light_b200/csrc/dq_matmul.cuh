@@ -29,12 +29,14 @@ struct DqMmParams {
   int slayout;
   int64_t kchunk;
   int ksplit;
+  int gemv_nkb;       // scale rows staged per CTA (GEMV fast path)
   float *partials;    // split-K workspace
   uint32_t *counters; // split-K arrival counters (zero between calls)
 };
 
 // Tensor-core path (dq_gemm_tc.cu).
-bool dq_tc_supported(const DqMmParams &p);
+bool dq_tc_eligible(const DqMmParams &p);  // shape/type constraints only
+bool dq_tc_supported(const DqMmParams &p); // eligible and chosen by default
 size_t dq_tc_workspace(const DqMmParams &p);
 int dq_tc_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
 

@@ -19,7 +19,8 @@ KAT = json.load(open(os.path.join(HERE, "golden", "kat_reference_tests.json")))
 
 def gpu_dq(b2, x_raw, x_dt, x_shape, s_raw, s_dt, s_shape, zp_raw=None, axis=1):
     x = b2.QTensor(to_dev(x_raw), x_dt, tuple(x_shape))
-    s = to_dev(s_raw).reshape(tuple(s_shape)) if len(s_shape) else to_dev(s_raw).reshape(())
+    s = to_dev(s_raw, torch.float16 if s_dt == O.FLOAT16 else None)
+    s = s.reshape(tuple(s_shape)) if len(s_shape) else s.reshape(())
     zp = b2.QTensor(to_dev(zp_raw), x_dt, tuple(s_shape)) if zp_raw is not None else None
     y = b2.DequantizeLinear()(x, s, zp, axis=axis)
     torch.cuda.synchronize()
@@ -81,7 +82,7 @@ def test_fp16_output_rounding_exhaustive(b2, cuda):
     s = O.f32_to_f16_bits(scales)  # FLOAT16 scale -> FLOAT16 output
     got = gpu_dq(b2, x, O.INT8, (64, 256), s, O.FLOAT16, (64,), None, 0)
     ref = O.dequantize_linear(x, O.INT8, (64, 256), s, O.FLOAT16, (64,), None, None, 0)
-    np.testing.assert_array_equal(got, ref)
+    np.testing.assert_array_equal(bits(got), bits(ref))
 
 
 def test_empty_and_ragged(b2, cuda):

@@ -13,11 +13,23 @@ TOL = {O.FLOAT: 1e-5, O.FLOAT16: 1e-3, O.BFLOAT16: 1e-3}
 TORCH = {O.FLOAT: torch.float32, O.FLOAT16: torch.float16, O.BFLOAT16: torch.bfloat16}
 
 
+def finite_q(seed, shape, dt):
+    """Random weight codes without the NaN/Inf encodings of the float8 types."""
+    if dt == O.F8E4M3FN:
+        return O.f32_to_f8e4m3fn(O.randn(seed, shape))
+    if dt in (O.F8E5M2, O.F8E4M3FNUZ, O.F8E5M2FNUZ):
+        n = int(np.prod(shape))
+        mag = O.randint(seed, (n,), 0, 100)
+        sign = O.randint(seed + 1000, (n,), 0, 1) * 128
+        return (mag + sign).astype(np.uint8) if dt == O.F8E5M2 else mag.astype(np.uint8)
+    return random_q(seed, shape, dt)
+
+
 def run_case(b2, M, K, N, wdt, s_dt, act_dt, axis=0, block=None, zp=False, cast=0, seed=1,
              lead=None):
     """Returns (gpu, oracle) outputs as float32 arrays."""
     # weight + scales in the requested layout
-    w = random_q(seed, (K, N), wdt)
+    w = finite_q(seed, (K, N), wdt)
     if block is None:               # per-axis
         s_shape = (K,) if axis == 0 else (N,)
     elif block == 0:                # per-tensor
@@ -43,7 +55,8 @@ def run_case(b2, M, K, N, wdt, s_dt, act_dt, axis=0, block=None, zp=False, cast=
     ref = O.matmul(a_raw, wb, act_dt)
     # GPU
     tw = b2.QTensor(to_dev(w), wdt, (K, N))
-    ts = to_dev(s).reshape(s_shape) if s_shape else to_dev(s).reshape(())
+    ts = to_dev(s, torch.float16 if s_dt == O.FLOAT16 else None)
+    ts = ts.reshape(s_shape) if s_shape else ts.reshape(())
     tz = b2.QTensor(to_dev(z), wdt, s_shape if s_shape else ()) if zp else None
     ta = to_dev(a_raw).view(TORCH[act_dt]).reshape(M, K)
     if lead:
@@ -114,3 +127,48 @@ def test_dtype_mismatch_errors(b2, cuda):
     a16 = torch.ones((1, 63), device="cuda", dtype=torch.float16)
     with pytest.raises(ValueError, match="incompatible inner dimensions"):
         b2.DequantizeMatMul()(a16, w, s, axis=0)
+
+
+# ---------------------------------------------------------------------------
+# Every kernel family on the same shapes (ONNXL_B200_DQ_KERNEL forces one).
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M", [1, 3, 5, 8, 32, 64, 100, 300])
+def test_tensor_core_int4_fp16(b2, cuda, monkeypatch, M):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "tc")
+    y, ref = run_case(b2, M, 1024, 512, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=M)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16]
+
+
+def test_tensor_core_config3_shape_batch32(b2, cuda, monkeypatch):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "tc")
+    y, ref = run_case(b2, 32, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=11)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16]
+
+
+@pytest.mark.parametrize("wdt", [O.F8E4M3FN, O.F4E2M1])
+@pytest.mark.parametrize("M", [8, 64, 300])
+def test_tensor_core_fp8_fp4_bf16(b2, cuda, monkeypatch, wdt, M):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "tc")
+    y, ref = run_case(b2, M, 512, 384, wdt, O.FLOAT, O.BFLOAT16, block=32, cast=O.BFLOAT16, seed=M)
+    assert rel_l2(y, ref) <= TOL[O.BFLOAT16]
+
+
+@pytest.mark.parametrize("wdt,s_dt,act,axis,block,zp,cast", [
+    (O.UINT8, O.FLOAT16, O.FLOAT16, 0, 64, True, 0),
+    (O.INT4, O.FLOAT16, O.FLOAT16, 0, 32, True, 0),
+    (O.INT4, O.FLOAT, O.BFLOAT16, 1, None, True, O.BFLOAT16),
+    (O.UINT4, O.FLOAT16, O.FLOAT16, 0, 0, False, 0),
+])
+def test_tensor_core_generic_layouts(b2, cuda, monkeypatch, wdt, s_dt, act, axis, block, zp, cast):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "tc")
+    for M in (6, 40):
+        y, ref = run_case(b2, M, 256, 192, wdt, s_dt, act, axis, block, zp, cast, seed=M + 3)
+        assert rel_l2(y, ref) <= TOL[act], (M, rel_l2(y, ref))
+
+
+@pytest.mark.parametrize("path", ["simt", "gemv"])
+def test_cuda_core_paths_config3_decode(b2, cuda, monkeypatch, path):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", path)
+    y, ref = run_case(b2, 2, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=21)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16]

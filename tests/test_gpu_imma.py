@@ -94,3 +94,40 @@ def test_int32_wraparound_matches_reference(b2, cuda):
     y = b2.MatMulInteger()(dev(a_np, O.UINT8, (M, K)), dev(b_np, O.UINT8, (K, N)))
     o = O.matmul_integer(a_np, O.UINT8, b_np, O.UINT8)
     np.testing.assert_array_equal(y.cpu().numpy(), o)
+
+
+@pytest.mark.parametrize("M,K,N,adt,bdt,az,bz", [
+    (128, 256, 256, O.UINT8, O.INT8, "scalar128", "col"),
+    (200, 512, 272, O.UINT8, O.UINT8, "row", "scalar"),
+    (64, 128, 128, O.INT8, O.INT8, "scalar", "col"),
+    (300, 4096, 1024, O.UINT8, O.INT8, "scalar128", "col"),
+])
+def test_tensor_core_matmul_integer_vs_oracle(b2, cuda, M, K, N, adt, bdt, az, bz):
+    a_np = encode_codes(O.randint(4001 + M, (M * K,), *(0, 255) if adt == O.UINT8 else (-128, 127)), adt).reshape(M, K)
+    b_np = encode_codes(O.randint(4002 + N, (K * N,), *(0, 255) if bdt == O.UINT8 else (-128, 127)), bdt).reshape(K, N)
+    azn = {"scalar128": np.array([128]), "scalar": np.array([-3]), "row": O.randint(7, (M,), 100, 140)}[az]
+    bzn = {"col": O.randint(8, (N,), -4, 4) if bdt == O.INT8 else O.randint(8, (N,), 120, 130),
+           "scalar": np.array([125])}[bz]
+    azr = encode_codes(azn, adt)
+    bzr = encode_codes(bzn, bdt)
+    a, b = dev(a_np, adt, (M, K)), dev(b_np, bdt, (K, N))
+    azt = dev(azr, adt, (azr.size,)) if azr.size > 1 else dev(azr, adt, ())
+    bzt = dev(bzr, bdt, (bzr.size,)) if bzr.size > 1 else dev(bzr, bdt, ())
+    y = b2.MatMulInteger()(a, b, azt, bzt)
+    o = O.matmul_integer(np_int(a_np, adt), adt, np_int(b_np, bdt), bdt, np_int(azr, adt), np_int(bzr, bdt))
+    np.testing.assert_array_equal(y.cpu().numpy(), o)
+
+
+def test_tensor_core_qlinear_matmul_vs_oracle(b2, cuda):
+    M, K, N = 256, 1024, 512
+    a_np = encode_codes(O.randint(5001, (M * K,), 0, 255), O.UINT8).reshape(M, K)
+    b_np = encode_codes(O.randint(5002, (K * N,), 0, 255), O.UINT8).reshape(K, N)
+    sc = (0.0066, 0.00705, 0.0107 * 40)
+    zp = (113, 114, 118)
+    a, b = dev(a_np, O.UINT8, (M, K)), dev(b_np, O.UINT8, (K, N))
+    s = [torch.tensor(v, dtype=torch.float32, device="cuda") for v in sc]
+    z = [torch.tensor(v, dtype=torch.uint8, device="cuda") for v in zp]
+    y = b2.QLinearMatMul()(a, s[0], z[0], b, s[1], z[1], s[2], z[2])
+    o = O.qlinear_matmul(a_np, O.UINT8, float(np.float32(sc[0])), zp[0], b_np, O.UINT8,
+                         float(np.float32(sc[1])), zp[1], float(np.float32(sc[2])), zp[2], O.UINT8)
+    np.testing.assert_array_equal(y.cpu().numpy(), o)

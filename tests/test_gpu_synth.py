@@ -28,7 +28,7 @@ def test_conversions_match_oracle(b2, cuda):
     fh = f.cpu().numpy()
     assert np.array_equal(synth.convert(f, _capi.FLOAT16).cpu().numpy().view(np.uint16),
                           O.f32_to_f16_bits(fh))
-    assert np.array_equal(synth.convert(f, _capi.BFLOAT16).cpu().numpy().view(np.uint16),
+    assert np.array_equal(synth.convert(f, _capi.BFLOAT16).view(torch.int16).cpu().numpy().view(np.uint16),
                           O.f32_to_bf16_bits(fh))
     assert np.array_equal(synth.convert(f, _capi.FLOAT8E4M3FN).data.cpu().numpy(),
                           O.f32_to_f8e4m3fn(fh))
