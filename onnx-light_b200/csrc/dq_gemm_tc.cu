@@ -61,8 +61,8 @@ __device__ __forceinline__ uint4 dequant8(const DqTcArgs &a, const uint8_t *raw_
   if (a.mode == kModeI4H) {
     // int4/uint4 x fp16 scale (blocked along K or per column), fp16 operand.
     const uint32_t w = *reinterpret_cast<const uint32_t *>(raw_row + nl / 2);
-    const int64_t kb = p.slayout == kScaleAxis0Block ? k / p.block : 0;
-    const int64_t si = p.slayout == kScaleTensor ? 0 : kb * p.N + n;
+    const int64_t kb = p.slayout == kScaleAxis0Block ? (int64_t)p.fdiv_block.div((uint32_t)k) : 0;
+    const int64_t si = p.slayout == kScaleTensor ? 0 : p.slayout == kScaleAxis1 ? n : kb * p.N + n;
     const uint16_t *sp = reinterpret_cast<const uint16_t *>(p.scale);
     uint32_t s4[4];
     if (p.slayout == kScaleTensor) {
@@ -116,9 +116,9 @@ __device__ __forceinline__ uint4 dequant8(const DqTcArgs &a, const uint8_t *raw_
     int64_t si;
     switch (p.slayout) {
     case kScaleTensor: si = 0; break;
-    case kScaleAxis0Block: si = (k / p.block) * p.N + n + j; break;
+    case kScaleAxis0Block: si = (int64_t)p.fdiv_block.div((uint32_t)k) * p.N + n + j; break;
     case kScaleAxis0: si = k; break;
-    case kScaleAxis1Block: si = k * p.s_alen + (n + j) / p.block; break;
+    case kScaleAxis1Block: si = k * p.s_alen + p.fdiv_block.div((uint32_t)(n + j)); break;
     default: si = n + j; break;
     }
     float s;
@@ -254,13 +254,14 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
       const uint8_t *sst = args.s_bytes ? raw + args.raw_bytes : nullptr;
       const int64_t kst = kbeg + (int64_t)kt * DT_BK; // first k of the stage
       const uint32_t s_esz = p.s_f16 ? 2u : 4u;
+      const uint32_t kst_b = sst ? p.fdiv_block.div((uint32_t)kst) : 0u;
 #pragma unroll 2
       for (int i = 0; i < DT_BK / 8; ++i) {
         const int r = r0 + 8 * i; // k row within the stage
         const int64_t k = kst + r;
         const int nl = cc * 8;
         const uint8_t *srow =
-            sst ? sst + (size_t)(k / p.block - kst / p.block) * DT_BM * s_esz : nullptr;
+            sst ? sst + (size_t)(p.fdiv_block.div((uint32_t)k) - kst_b) * DT_BM * s_esz : nullptr;
         uint4 o = make_uint4(0, 0, 0, 0);
         if (k < kend && n0 + nl < p.N) o = dequant8(args, raw + r * raw_row_bytes, nl, k, n0 + nl, srow);
         // MN-major 128-byte swizzle: block (nl / 64) at 8 KB, row r at 128 B,

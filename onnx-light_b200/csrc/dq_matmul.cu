@@ -42,9 +42,9 @@ __device__ __forceinline__ float round_to(float v, int dt) {
 __device__ __forceinline__ int64_t w_scale_index(const DqMmParams &p, int64_t k, int64_t n) {
   switch (p.slayout) {
   case kScaleTensor: return 0;
-  case kScaleAxis0Block: return (k / p.block) * p.N + n;
+  case kScaleAxis0Block: return (int64_t)p.fdiv_block.div((uint32_t)k) * p.N + n;
   case kScaleAxis0: return k;
-  case kScaleAxis1Block: return k * p.s_alen + n / p.block;
+  case kScaleAxis1Block: return k * p.s_alen + p.fdiv_block.div((uint32_t)n);
   default: return n; // kScaleAxis1
   }
 }
@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) dq_gemv(const DqMmParams p) {
       const int64_t kk = kk0 + 32 * u;
       if (kk >= klen) break;
       const int64_t k = kbeg + kk;
-      const int64_t kb = p.slayout == kScaleAxis0Block ? k / p.block : 0;
+      const int64_t kb = p.slayout == kScaleAxis0Block ? (int64_t)p.fdiv_block.div((uint32_t)k) : 0;
       if (kb != cur_kb) {
         cur_kb = kb;
 #pragma unroll
@@ -507,10 +507,14 @@ __global__ void __launch_bounds__(GV_THREADS, MT == 1 ? 2 : 1)
       }
       const int64_t kk = (int64_t)t * GV_ROWS + row;
       const uint4 raw = *reinterpret_cast<const uint4 *>(ring + s * GV_STAGE_BYTES + row * 128 + c * 16);
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&empty[s]);
-      if (kk >= klen) continue;
-      const int sr = p.slayout == kScaleAxis0Block ? (int)((kbeg + kk) / p.block - kb0) : 0;
+      if (kk >= klen) {
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[s]);
+        continue;
+      }
+      const int sr = p.slayout == kScaleAxis0Block
+                         ? (int)(p.fdiv_block.div((uint32_t)(kbeg + kk)) - (uint32_t)kb0)
+                         : 0;
       if (sr != cur_sr) {
         cur_sr = sr;
         const uint4 *sp = reinterpret_cast<const uint4 *>(s_s + (size_t)sr * GEMV_TN + c * 32);
@@ -544,6 +548,10 @@ __global__ void __launch_bounds__(GV_THREADS, MT == 1 ? 2 : 1)
           }
         }
       }
+      // Release the stage only after its data has been consumed: the next TMA
+      // fill of this slot must not overtake a shared-memory read in flight.
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty[s]);
     }
     // reduce the 4 row-lanes (r) sharing a column chunk
 #pragma unroll
@@ -634,6 +642,9 @@ static int dq_mm_validate(const b2_tensor *a, const b2_tensor *w, const b2_tenso
   else p.slayout = dqp.layout == 2 ? kScaleAxis1Block : kScaleAxis1;
   p.block = dqp.block;
   p.s_alen = dqp.s_alen;
+  B2_ENFORCE(K < (int64_t(1) << 31) && N < (int64_t(1) << 31),
+             "b2_dequantize_matmul: K and N must be below 2^31");
+  p.fdiv_block = FastDiv((uint32_t)(p.block > 0 ? p.block : 1));
   return B2_OK;
 }
 

@@ -22,6 +22,7 @@ struct DqMmParams {
   void *y;              // [M, N], dtype of a
   int64_t M, K, N;
   int64_t block, s_alen;
+  FastDiv fdiv_block;   // k / block (and n / block) in 32-bit arithmetic
   int wdt;
   int s_f16;    // scale (and DequantizeLinear output) is FLOAT16
   int cast_dt;  // 0 or the Cast target dtype
