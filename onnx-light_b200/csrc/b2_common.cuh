@@ -124,8 +124,8 @@ inline int workspace_check(void *ws, size_t *ws_bytes, size_t need) {
       set_error(B2_ERR_WORKSPACE, "workspace of %zu bytes required", need);
       return B2_ERR_WORKSPACE;
     }
-    *ws_bytes = need;
-    return need == 0 ? 0 : 1;
+    *ws_bytes = need; // size query: nothing runs, whatever the size
+    return 1;
   }
   if (ws_bytes == nullptr || *ws_bytes < need) {
     set_error(B2_ERR_WORKSPACE, "workspace too small: %zu bytes required, %zu offered", need,

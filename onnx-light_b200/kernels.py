@@ -72,10 +72,12 @@ def _call_with_workspace(fn, args_before, args_after, device):
     """Queries the workspace size (workspace=NULL), then runs."""
     need = C.c_size_t(0)
     check(fn(*args_before, None, C.byref(need), *args_after))
-    ws = workspace(device, need.value) if need.value else None
-    cap = C.c_size_t(ws.numel() if ws is not None else 0)
-    check(fn(*args_before, C.c_void_p(ws.data_ptr()) if ws is not None else None, C.byref(cap),
-             *args_after))
+    if need.value == 0:
+        check(fn(*args_before, None, None, *args_after))
+        return
+    ws = workspace(device, need.value)
+    cap = C.c_size_t(ws.numel())
+    check(fn(*args_before, C.c_void_p(ws.data_ptr()), C.byref(cap), *args_after))
 
 
 # ---------------------------------------------------------------------------
