@@ -107,6 +107,28 @@ B2_API int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w, const b2
                          const b2_tensor *w_zero_point, int64_t axis, int32_t cast_dtype,
                          b2_tensor *y, void *workspace, size_t *workspace_bytes, void *stream);
 
+
+/*
+ * Fused DequantizeLinear -> [Cast] -> MatMul without a caller-provided
+ * workspace, for callers that cannot allocate device memory: sessions whose
+ * memory plan is sealed before the run, real-time loops that forbid
+ * allocation after start-up, and host plugins that only receive their input
+ * and output buffers.  Same arguments, kernels and results as
+ * b2_dequantize_matmul (no counterpart in onnx-light: the reference CPU kernel
+ * allocates its temporaries itself).
+ * Scratch: a fixed 8 MiB device array inside this library, held by every GPU
+ * that loads it until the process exits.  Calls whose plan needs more are
+ * rejected with B2_ERR_WORKSPACE.  All calls on a device share that array, so
+ * calls that overlap on the GPU (other streams or host threads) race; calls
+ * on one stream are safe.  The first call on each device resolves the array's
+ * device address and should come before any stream capture.  Nothing is
+ * allocated.
+ */
+B2_API int b2_dequantize_matmul_noalloc(const b2_tensor *a, const b2_tensor *w,
+                                        const b2_tensor *w_scale, const b2_tensor *w_zero_point,
+                                        int64_t axis, int32_t cast_dtype, b2_tensor *y,
+                                        void *stream);
+
 /*
  * MatMulInteger: y[i,j] = sum_k (a[i,k] - a_zp[i]) * (b[k,j] - b_zp[j]) in
  * int32, bit-exact.

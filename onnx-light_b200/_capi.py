@@ -42,7 +42,7 @@ ONNX_TO_TORCH = {FLOAT: torch.float32, FLOAT16: torch.float16, BFLOAT16: torch.b
 
 # Every symbol the header declares (checked by the CPU tests).
 EXPORTS = ("b2_version", "b2_last_error", "b2_dequantize_linear", "b2_dequantize_matmul",
-           "b2_matmul_integer", "b2_qlinear_matmul", "b2_attention", "b2_synth_fill",
+           "b2_dequantize_matmul_noalloc", "b2_matmul_integer", "b2_qlinear_matmul", "b2_attention", "b2_synth_fill",
            "b2_convert")
 
 
