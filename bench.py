@@ -79,55 +79,63 @@ def step_flops(batch: int) -> int:
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons of one GPU, polled through NVML every
+    ~2 ms on a background thread while the block runs (nvidia-smi's fastest
+    loop, 100 ms, would miss a timed region of a few tens of milliseconds)."""
+
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40), ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.samples = []
+        self.max_mhz = None
         self._stop = threading.Event()
-        self._proc = None
+        self._thread = None
 
     def __enter__(self):
         try:
-            self._proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = self.gpu
+            if vis:
+                try:
+                    index = int(vis.split(",")[self.gpu])
+                except ValueError:
+                    index = self.gpu
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._thread = threading.Thread(target=self._poll, daemon=True)
             self._thread.start()
-        except (OSError, ValueError):
-            self._proc = None
+        except Exception:
+            self._thread = None
         return self
 
-    def _read(self):
-        for line in self._proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.samples.append(parts)
+    def _poll(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __exit__(self, *exc):
-        if self._proc is not None:
-            self._proc.terminate()
-            try:
-                self._proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self._proc.kill()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
     def summary(self):
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = sorted(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
-        mx = max((float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()), default=None)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for s in self.samples:
-            for name, v in zip(names, s[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(self.samples)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        sm = sorted(m for m, _ in self.samples)
+        reasons = sorted({name for _, r in self.samples for name, bit in self.REASONS if r & bit})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "NVML, 2 ms polling over the timed region"}
 
 
 # ---------------------------------------------------------------------------
@@ -192,116 +200,145 @@ def gpu_arm(args):
                 dist.all_gather_into_tensor(gat[name].view(-1), loc[name].view(-1))
                 acts[name].copy_(gat[name].permute(1, 0, 2).reshape(B, N))
 
-    # warm up the library (plans, function attributes, workspace) outside capture
+    def run_steps(n, offset):
+        for i in range(n):
+            run_step(layers[(offset + i) % NCOPIES])
+
+    # Warm the library (plans, function attributes, workspace, NCCL
+    # communicators) outside capture.
     with torch.cuda.stream(stream):
-        for layer in layers:
-            run_step(layer)
+        run_steps(NCOPIES, 0)
     torch.cuda.synchronize()
 
-    use_graph = world == 1
-    graphs = []
-    if use_graph:
-        for layer in layers:
+    # The steps run as CUDA graphs of up to CHUNK steps each (NCCL calls
+    # captured too when sharded), so the device time measured is the steps'
+    # own and never the host's launch rate.  K steps = K // CHUNK replays of the
+    # chunk graph + one graph of the remainder.
+    chunk = max(NCOPIES, min(256, args.steps) // NCOPIES * NCOPIES)
+    graphs = {}
+
+    def graph_of(n):
+        if n not in graphs:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                run_step(layer)
-            graphs.append(g)
+                run_steps(n, 0)
+            graphs[n] = g
+        return graphs[n]
 
-    def launch(i):
-        if use_graph:
-            graphs[i % NCOPIES].replay()
-        else:
-            with torch.cuda.stream(stream):
-                run_step(layers[i % NCOPIES])
+    def play(n):
+        with torch.cuda.stream(stream):
+            for _ in range(n // chunk):
+                graph_of(chunk).replay()
+            if n % chunk:
+                graph_of(n % chunk).replay()
 
-    for i in range(args.warmup):
-        launch(i)
+    graph_of(chunk)
+    if args.steps % chunk:
+        graph_of(args.steps % chunk)
+    if args.warmup % chunk:
+        graph_of(args.warmup % chunk)
+    play(args.warmup)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        for i in range(args.steps):
-            starts[i].record(stream)
-            with torch.cuda.stream(stream):
-                launch(i)
-            ends[i].record(stream)
+        ev0.record(stream)
+        play(args.steps)
+        ev1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    ms = ev0.elapsed_time(ev1) / args.steps
     if world > 1:
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     nbytes = step_bytes(B)
     value = nbytes / (ms * 1e-3) / 1e9
+    graphs.clear()
+    torch.cuda.synchronize()
 
-    # Dominant kernel: time each projection's GEMV alone (events on its stream),
-    # rotating weight copies so every launch reads from HBM.
+    # Roofline.  The fused kernel is the only kernel of a single-GPU step, so
+    # its average launch duration is the timed region / (7 K): achieved =
+    # algorithmic bytes of the step / step time.  Each projection is also
+    # timed alone: a graph of REPS launches rotating the weight copies.
     roof = None
     if rank == 0:
         per = []
-        with torch.cuda.stream(stream):
-            for name, K, N, src in PROJ:
-                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                reps = 8
-                out = acts[name] if world == 1 else loc[name]
-                for c in range(NCOPIES):  # warm
-                    w, s = layers[c][name]
-                    mm(acts[src], w, s, None, axis=0, out=out)
-                ev0.record(stream)
+        reps = 8 * NCOPIES
+        for name, K, N, src in PROJ:
+            out = acts[name] if world == 1 else loc[name]
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
                 for r in range(reps):
                     w, s = layers[r % NCOPIES][name]
                     mm(acts[src], w, s, None, axis=0, out=out)
-                ev1.record(stream)
-                torch.cuda.synchronize()
-                t_launch = ev0.elapsed_time(ev1) / reps
-                n_loc = N // world
-                b = K * n_loc // 2 + (K // BLOCK) * n_loc * 2 + B * K * 2 + B * n_loc * 2
-                per.append((name, b, t_launch))
-        tot_b = sum(p[1] for p in per)
-        tot_t = sum(p[2] for p in per)
+            with torch.cuda.stream(stream):
+                g.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            n_loc = N // world
+            b = K * n_loc // 2 + (K // BLOCK) * n_loc * 2 + B * K * 2 + B * n_loc * 2
+            per.append((name, b, e0.elapsed_time(e1) / reps))
+            del g
         peak, peak_src = measured_peak()
-        achieved = tot_b / (tot_t * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "dq_gemv", "achieved": round(achieved, 1),
+        if world == 1:
+            achieved = nbytes / (ms * 1e-3) / 1e9
+        else:
+            achieved = sum(p[1] for p in per) / (sum(p[2] for p in per) * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "dq_gemv_mma", "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_source": peak_src, "traffic": traffic_from_profile(),
-                "per_launch_us": {p[0]: round(p[2] * 1e3, 2) for p in per},
-                "algorithmic_bytes_per_step": tot_b}
+                "algorithmic_bytes_per_step": nbytes,
+                "per_projection_us": {p[0]: round(p[2] * 1e3, 2) for p in per},
+                "per_projection_gbs": {p[0]: round(p[1] / (p[2] * 1e-3) / 1e9, 1) for p in per}}
 
-    # e2e: public API with host buffers, H2D of x and D2H of the step's result.
+    # e2e: the public API (DequantizeMatMul -> b2_dequantize_matmul) with the
+    # step input copied from pinned host memory and the step result copied
+    # back to pinned host memory inside every step; the calls are captured in
+    # CUDA graphs the way a serving loop captures its decode step.
     e2e = None
     if rank == 0 and world == 1:
         x_host = x0.cpu().pin_memory()
         y_host = torch.empty((B, 4096), dtype=torch.float16).pin_memory()
-        for i in range(args.warmup):
-            with torch.cuda.stream(stream):
+
+        def e2e_steps(n):
+            for i in range(n):
                 acts["x"].copy_(x_host, non_blocking=True)
                 run_step(layers[i % NCOPIES])
                 y_host.copy_(acts["down"], non_blocking=True)
+
+        ge = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ge, stream=stream):
+            e2e_steps(chunk)
+        with torch.cuda.stream(stream):
+            ge.replay()
         torch.cuda.synchronize()
+        reps_e2e = max(1, args.steps // chunk)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record(stream)
-        for i in range(args.steps):
-            with torch.cuda.stream(stream):
-                acts["x"].copy_(x_host, non_blocking=True)
-                run_step(layers[i % NCOPIES])
-                y_host.copy_(acts["down"], non_blocking=True)
-        ev1.record(stream)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps_e2e):
+                ge.replay()
+            e1.record(stream)
         torch.cuda.synchronize()
-        wall = (time.perf_counter() - t0) / args.steps
-        dev_ms = ev0.elapsed_time(ev1) / args.steps
+        wall = (time.perf_counter() - t0) / (reps_e2e * chunk)
+        dev_ms = e0.elapsed_time(e1) / (reps_e2e * chunk)
         e2e_ms = max(wall * 1e3, dev_ms)
         e2e = {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-               "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": B * 4096 * 2,
+               "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": B * 4096 * 2,
                "d2h_bytes_per_step": B * 4096 * 2,
-               "path": "DequantizeMatMul python API -> b2_dequantize_matmul, no graph"}
+               "path": "DequantizeMatMul python API -> b2_dequantize_matmul, pinned H2D + "
+                       "7 calls + D2H per step, captured in CUDA graphs"}
+        del ge
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -320,9 +357,10 @@ def gpu_arm(args):
                        "parallelism": f"column-sharded tp{world}" if world > 1 else "single GPU",
                        "l2_policy": f"{NCOPIES} weight copies in rotation "
                                     f"({NCOPIES * step_bytes(B) / 1e6:.0f} MB > 126 MB L2)",
-                       "launch": "CUDA graph per step" if use_graph else "eager + NCCL all_gather"},
+                       "launch": f"CUDA graphs of {chunk} steps"
+                                 + (" with NCCL all_gather per projection" if world > 1 else "")},
             "tflops": round(step_flops(B) / (ms * 1e-3) / 1e12, 3),
-            "gpu_launches": 7 * args.steps if world == 1 else 7 * args.steps,
+            "gpu_launches": 7 * args.steps,
             "clocks": clocks,
             "roofline": roof,
             "cpu_baseline": cpu,
@@ -423,18 +461,58 @@ def reference_arm(args):
     if not O.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref.so not built"}))
         return
-    subset = tuple(p[0] for p in PROJ)
-    O, np, data, x = _ref_inputs(B, subset)
-    for _ in range(args.warmup):
-        _ref_step(O, np, data, x, B, subset)
+    # Each step is a bounded sample of the layer: one projection (DequantizeLinear
+    # + MatMul), q, k, v, o, gate, up, down in turn, restricted to its first
+    # `cols` output columns, with `cols` sized from a calibration call so that
+    # the W + K steps take about a minute; value = bytes processed / time.
+    import numpy as np
+    xs = {}
+    for name, K, N, src in PROJ:
+        xs[name] = O.f32_to_f16_bits(O.randn(2001, (B, K)))
+
+    def col_slice(name, K, N, cols):
+        seed = 3000 + [p[0] for p in PROJ].index(name)
+        codes = O.randint(seed, (K * N,), -8, 7).reshape(K, N)[:, :cols]
+        sc = O.f32_to_f16_bits(O.rand_uniform(seed + 50, (K // BLOCK * N,), 0.002, 0.02))
+        sc = sc.reshape(K // BLOCK, N)[:, :cols]
+        return O.pack_bits(np.ascontiguousarray(codes), 4), np.ascontiguousarray(sc)
+
+    def run(name, K, w, sc, cols):
+        wq = O.ref_dequantize_linear(w, O.INT4, (K, cols), sc, O.FLOAT16, (K // BLOCK, cols),
+                                     None, None, 0)
+        O.ref_matmul(xs[name], wq, O.FLOAT16)
+        return K * cols // 2 + (K // BLOCK) * cols * 2 + B * K * 2 + B * cols * 2
+
+    cal_w, cal_s = col_slice("q", 4096, 4096, 512)
+    run("q", 4096, cal_w, cal_s, 512)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        _ref_step(O, np, data, x, B, subset)
-    t = (time.perf_counter() - t0) / args.steps
-    value = step_bytes(B) / t / 1e9
+    run("q", 4096, cal_w, cal_s, 512)
+    per_weight = (time.perf_counter() - t0) / (4096 * 512)
+    budget = 60.0 / (args.steps + args.warmup)
+    slices = []
+    for name, K, N, _ in PROJ:
+        cols = int(budget / per_weight / K) // 128 * 128
+        cols = max(128, min(N, cols))
+        slices.append((name, K, cols) + col_slice(name, K, N, cols))
+
+    def proj_step(i):
+        name, K, cols, w, sc = slices[i % len(slices)]
+        return run(name, K, w, sc, cols)
+
+    for i in range(args.warmup):
+        proj_step(i)
+    t0 = time.perf_counter()
+    tot_b = 0
+    for i in range(args.steps):
+        tot_b += proj_step(i)
+    el = time.perf_counter() - t0
+    t = el / args.steps
+    value = tot_b / el / 1e9
+    col_note = ", ".join(f"{n}:{c}" for n, _, c, _, _ in slices)
     cores = O.ref_thread_count()
-    sample = (f"full config-3 layer (7 x DequantizeLinear + MatMul fp16, B={B}) per step, "
-              f"onnx-light kernels compiled from source, {cores} threads")
+    sample = (f"one config-3 projection per step in turn (DequantizeLinear int4 + MatMul fp16, "
+              f"B={B}) over its first columns ({col_note}), onnx-light kernels compiled "
+              f"from source, {cores} threads")
     print(json.dumps({
         "impl": "reference",
         "metric": "int4 dequant-MatMul HBM GB/s (Llama-7B decode layer, config 3)",
@@ -454,7 +532,7 @@ def reference_arm(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])

@@ -1,0 +1,578 @@
+// Decode-shaped fused DequantizeLinear -> [Cast] -> MatMul (M <= 16 rows of
+// activations), INT4/UINT4 weights with FLOAT16 scales and FLOAT16
+// activations: the int4 weight-only projection of LLM decoding.
+//
+// Reference semantics (onnx_light/onnx_extensions/kernels/kernels/quantization/
+// kernel_dequantizelinear.cc:332-520 then kernels/math/kernel_matmul.cc:181-223):
+// y[m, n] = sum_k a[m, k] * w[k, n] with w[k, n] = (q[k, n] - 0) * s[k / block, n]
+// and fp32 accumulation.
+//
+// Arithmetic.  Each packed nibble is turned into an fp16 "magic number" with one
+// logic operation per pair of weights: 1024 + (q + 8) for the low nibble of a
+// byte and 1024 + 16 (q + 8) for the high one (signed; unsigned codes drop the
+// + 8).  These exact fp16 integers go straight into mma.sync m16n8k16 (fp16
+// inputs, fp32 accumulators) against the activations, together with one
+// all-ones row that yields sum_k a[m, k] of the same k range.  At the end of
+// every scale block the offset is removed and the scale applied in fp32:
+//   sum_k a q s = s * (D - bias * sum_k a)            (low nibbles, bias 1032)
+//   sum_k a q s = (s / 16) * (D - bias * sum_k a)     (high nibbles, bias 1152)
+// so the weight is never rounded to fp16: the result differs from the
+// reference's only by the reference's own fp16 rounding of each dequantized
+// weight (at most 2^-11 relative per weight), and by the order of the fp32
+// sums.  The fp32 cancellation of the offset costs about 2^-24 * 1152 / |q|
+// relative per block sum (about 1e-5), far inside the rel-L2 1e-3 contract.
+//
+// Why register-level MMA and not tcgen05 here: the kernel is bound by HBM
+// (half a byte per weight) and by the instructions spent per weight.  tcgen05
+// takes its operands from shared memory or tensor memory, so every expanded
+// weight would cost 2 bytes of shared-memory writes and reads per 0.5 byte
+// fetched; built in registers, the fragment feeds the MMA directly and shared
+// memory carries the packed weights once.  Large M goes to the tcgen05 kernel
+// (dq_gemm_tc.cu).
+//
+// Work split ("stream-K"): the weight is cut into units of 128 rows x 256
+// columns (16 KB packed, one pipeline stage), numbered tile-major (tile = 256
+// columns); the grid's CTAs (one per SM) take equal contiguous ranges of units,
+// so every SM streams the same number of bytes whatever the shape.  A tile
+// covered by one CTA is written directly; a tile shared by several CTAs is
+// finished by the last one to arrive, which sums the fp32 partials in CTA
+// order (deterministic).
+//
+// Pipeline: one producer warp fills an 8-stage ring with TMA (packed weights
+// 128 x 128 bytes with the 128-byte swizzle, the activation slice 128 x M in
+// two swizzled boxes, the stage's scale rows).  Eight consumer warps form four
+// groups of two (one per 128-column half); group j consumes stages j, j + 4,
+// ..., so four stages are being multiplied while four are in flight.  Before
+// waiting on the kernel launched ahead of it (programmatic dependent launch),
+// each CTA asks the TMA unit to prefetch its whole weight range into L2: the
+// prefetch changes no value (L2 is the point of coherence), so it is safe
+// whatever the earlier kernel writes, and it lets consecutive projections
+// stream HBM back to back.
+#include "dq_matmul.cuh"
+#include "tc_common.cuh"
+
+namespace b2 {
+
+// Wait time-outs of the decode kernel (a TMA copy or a consumer that never
+// arrived) are recorded here; the kernel then skips its remaining work.
+__device__ int g_gemv_mma_status;
+
+namespace {
+
+constexpr int GM_TN = 256;                         // columns per tile (128 packed bytes / row)
+constexpr int GM_TK = 128;                         // weight rows per stage
+constexpr int GM_STAGES = 8;                       // ring depth
+constexpr int GM_GROUPS = 4;                       // stage groups of consumer warps
+constexpr int GM_CONSUMERS = 2 * GM_GROUPS;        // consumer warps
+constexpr int GM_THREADS = (GM_CONSUMERS + 1) * 32;
+constexpr uint32_t GM_W_BYTES = GM_TK * GM_TN / 2; // 16 KB
+constexpr int GM_SC_ROWS = 4;                      // scale rows per stage at most (block 32)
+constexpr uint32_t GM_SC_BYTES = GM_SC_ROWS * GM_TN * 2;
+constexpr uint32_t GM_ONES = 0x3c003c00u;          // (1.0, 1.0) in fp16
+
+struct GmArgs {
+  __half *y;
+  float *partials;
+  uint32_t *counters;
+  int M, N, K;
+  int ntiles, kunits, units, grid;
+  int block;     // scale block along K (0: one scale row for all K)
+  int srows;     // scale rows loaded per stage (0: per-tensor scale)
+  const uint16_t *scalar_scale; // the per-tensor scale (srows == 0)
+  int is_signed;
+};
+
+template <int NT> struct GmSmem {
+  static constexpr uint32_t kA = 2u * 8 * NT * 128; // two 64-column boxes, 8*NT rows each
+  static constexpr uint32_t kOffA = GM_STAGES * GM_W_BYTES;
+  static constexpr uint32_t kOffS = kOffA + GM_STAGES * kA;
+  static constexpr uint32_t kOffRed = kOffS + GM_STAGES * GM_SC_BYTES;
+  // GM_GROUPS / 2 slots per column half for the tree reduction over the groups
+  static constexpr uint32_t kRedBytes = (GM_GROUPS / 2) * 2u * 32 * NT * 32 * 4;
+  static constexpr uint32_t kOffBar = kOffRed + kRedBytes;
+  static constexpr uint32_t kBytes = kOffBar + 2 * GM_STAGES * 8 + 16;
+  static constexpr size_t kDynamic = kBytes + 1024; // alignment slack
+};
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void prefetch_l2_2d(const CUtensorMap *map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(GM_CONSUMERS * 32) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t *p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
+      "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ int unit_begin(int c, int U, int G) {
+  return (int)((uint32_t)c * (uint32_t)U / (uint32_t)G); // units * grid < 2^31 (host check)
+}
+__device__ __forceinline__ int cta_of(int u, int U, int G) {
+  return (int)(((uint32_t)(u + 1) * (uint32_t)G - 1u) / (uint32_t)U);
+}
+
+// One k16 step of one consumer warp: rows r0 .. r0+15 of the stage, the 128
+// columns of column half `wn`.  Lane (g, t) holds packed columns
+// c0 = wn*128 + g*16 .. c0+15 of rows r0+2t, r0+2t+1, r0+2t+8, r0+2t+9; m-tile
+// mt of the MMA takes columns c0+2mt (row g: the low nibble of byte mt) and
+// c0+2mt+1 (row g+8: the high nibble), so the byte holding both nibbles feeds
+// one A fragment directly.  D accumulates sum a * magic and O sum a (ones row)
+// for activation rows nt*8 .. nt*8+7.
+template <int NT>
+__device__ __forceinline__ void k16_step(const uint8_t *wst, const uint8_t *ast, int r0, int wn,
+                                         int g, int t, int nt, uint32_t mlo, uint32_t mhi,
+                                         float (&D)[8][4], float (&O)[4]) {
+  const int cb = wn * 64 + g * 8; // logical byte of the lane's 16 columns in a 128-byte row
+  uint2 R[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int rr = r0 + 2 * t + (q & 1) + ((q >> 1) << 3);
+    R[q] = *reinterpret_cast<const uint2 *>(wst + rr * 128 +
+                                            ((((cb >> 4) ^ (rr & 7)) << 4) | (cb & 15)));
+  }
+  uint32_t B0, B1;
+  {
+    const int kb = ((r0 & 63) + 2 * t) * 2; // byte within the 64-column activation box
+    const uint8_t *box = ast + (r0 >= 64 ? 8 * NT * 128 : 0);
+    const int row = nt * 8 + g;
+    const uint8_t *rb = box + row * 128;
+    B0 = *reinterpret_cast<const uint32_t *>(rb + ((((kb >> 4) ^ (row & 7)) << 4) | (kb & 15)));
+    const int kb2 = kb + 16;
+    B1 = *reinterpret_cast<const uint32_t *>(rb + ((((kb2 >> 4) ^ (row & 7)) << 4) | (kb2 & 15)));
+  }
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int jb = mt & 3;
+    const uint32_t sel = jb | (jb << 4) | ((jb + 4) << 8) | ((jb + 4) << 12);
+    const uint32_t x01 = (mt >> 2) ? R[0].y : R[0].x, y01 = (mt >> 2) ? R[1].y : R[1].x;
+    const uint32_t x89 = (mt >> 2) ? R[2].y : R[2].x, y89 = (mt >> 2) ? R[3].y : R[3].x;
+    // Byte jb of row k in the low half-word, of row k+1 in the high one.
+    const uint32_t v01 = __byte_perm(x01, y01, sel);
+    const uint32_t v89 = __byte_perm(x89, y89, sel);
+    const uint32_t a0 = (v01 & 0x000f000fu) ^ mlo, a1 = (v01 & 0x00f000f0u) ^ mhi;
+    const uint32_t a2 = (v89 & 0x000f000fu) ^ mlo, a3 = (v89 & 0x00f000f0u) ^ mhi;
+    mma16816(D[mt], a0, a1, a2, a3, B0, B1);
+  }
+  mma16816(O, GM_ONES, GM_ONES, GM_ONES, GM_ONES, B0, B1);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    dq_gemv_mma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
+                const __grid_constant__ CUtensorMap map_s, const GmArgs g) {
+  using L = GmSmem<NT>;
+  extern __shared__ uint8_t dsm[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(sm + L::kOffBar);
+  uint64_t *empty = full + GM_STAGES;
+  volatile int *flags = reinterpret_cast<volatile int *>(empty + GM_STAGES); // [0] abort, [1] last
+  float *red = reinterpret_cast<float *>(sm + L::kOffRed);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x;
+  const int u0 = unit_begin(b, g.units, g.grid);
+  const int u1 = unit_begin(b + 1, g.units, g.grid);
+  const int nun = u1 - u0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < GM_STAGES; ++i) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], 2); // the two warps of the stage's group
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == GM_CONSUMERS && lane == 0) {
+    tc::prefetch_tensormap(&map_w);
+    tc::prefetch_tensormap(&map_a);
+    if (g.srows) tc::prefetch_tensormap(&map_s);
+    for (int u = u0; u < u1; ++u)
+      prefetch_l2_2d(&map_w, (u / g.kunits) * (GM_TN / 2), (u % g.kunits) * GM_TK);
+  }
+  __syncthreads();
+  // Everything below may read what the previous kernel on the stream wrote
+  // (activations) or write what it reads (output, workspace).
+  griddep_wait();
+  griddep_launch();
+
+  if (warp == GM_CONSUMERS) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      const uint32_t tx = GM_W_BYTES + L::kA + (uint32_t)g.srows * GM_TN * 2;
+      for (int i = 0; i < nun; ++i) {
+        const int s = i % GM_STAGES;
+        if (i >= GM_STAGES && !tc::mbar_wait(&empty[s], ((i / GM_STAGES) - 1) & 1)) {
+          atomicExch(&g_gemv_mma_status, tc::kTimeoutEmpty);
+          flags[0] = 1;
+          break;
+        }
+        const int u = u0 + i, tile = u / g.kunits, kb = u % g.kunits;
+        uint8_t *st = sm + s * GM_W_BYTES;
+        uint8_t *sa = sm + L::kOffA + s * L::kA;
+        tc::mbar_expect_tx(&full[s], tx);
+        tc::tma_load_2d(st, &map_w, &full[s], tile * (GM_TN / 2), kb * GM_TK);
+        tc::tma_load_2d(sa, &map_a, &full[s], kb * GM_TK, 0);
+        tc::tma_load_2d(sa + L::kA / 2, &map_a, &full[s], kb * GM_TK + 64, 0);
+        if (g.srows) {
+          const int srow = g.block ? (kb * GM_TK) / g.block : 0;
+          tc::tma_load_2d(sm + L::kOffS + s * GM_SC_BYTES, &map_s, &full[s], tile * GM_TN, srow);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------ consumers -------------------------------
+  const int wn = warp & 1, grp = warp >> 1;
+  const int gq = lane >> 2, t = lane & 3;
+  const uint32_t mlo = g.is_signed ? 0x64086408u : 0x64006400u;
+  const uint32_t mhi = g.is_signed ? 0x64806480u : 0x64006400u;
+  const float blo = g.is_signed ? 1032.0f : 1024.0f;
+  const float bhi = g.is_signed ? 1152.0f : 1024.0f;
+  // scale rows per stage and k16 steps per scale row
+  const int nsub = (g.block && g.block < GM_TK) ? GM_TK / g.block : 1;
+  const int ksub = 8 / nsub;
+  const float scalar = g.srows ? 0.0f : __half2float(__ushort_as_half(__ldg(g.scalar_scale)));
+  float acc[8][NT][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.0f;
+  bool ok = true;
+  const int first_tile = u0 / g.kunits;
+
+  int seg0 = 0; // first stage of the current tile segment
+  while (seg0 < nun) {
+    const int tile = (u0 + seg0) / g.kunits;
+    const int seg1 = min(nun, (tile + 1) * g.kunits - u0);
+    // this group's stages of the segment: i = seg0 .. seg1-1 with i % GROUPS == grp
+    for (int i = seg0 + ((grp - seg0 % GM_GROUPS + GM_GROUPS) % GM_GROUPS); i < seg1; i += GM_GROUPS) {
+      const int s = i % GM_STAGES;
+      const int kb = (u0 + i) % g.kunits;
+      if (ok && flags[0]) ok = false;
+      if (ok && !tc::mbar_wait(&full[s], (i / GM_STAGES) & 1)) {
+        atomicExch(&g_gemv_mma_status, tc::kTimeoutFull);
+        flags[0] = 1;
+        ok = false;
+      }
+      if (ok) {
+        const uint8_t *wst = sm + s * GM_W_BYTES;
+        const uint8_t *ast = sm + L::kOffA + s * L::kA;
+        const uint8_t *sst = sm + L::kOffS + s * GM_SC_BYTES;
+        for (int sub = 0; sub < nsub; ++sub) {
+          const int r0 = sub * ksub * 16;
+          if (kb * GM_TK + r0 >= g.K) break;
+          // this scale row's factors for the lane's 16 columns (odd: high nibbles, / 16)
+          float se[16];
+          if (g.srows) {
+            const uint4 *sp = reinterpret_cast<const uint4 *>(sst + sub * GM_TN * 2 +
+                                                              (wn * 128 + gq * 16) * 2);
+            const uint4 v0 = sp[0], v1 = sp[1];
+            const uint32_t w8[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              se[2 * j] = __half2float(__ushort_as_half((uint16_t)(w8[j] & 0xffffu)));
+              se[2 * j + 1] = __half2float(__ushort_as_half((uint16_t)(w8[j] >> 16))) * 0.0625f;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) se[j] = (j & 1) ? scalar * 0.0625f : scalar;
+          }
+          // Rows 8..15 of the activations (M > 8) take a second pass over the
+          // stage, so the registers stay those of one 8-row tile.
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            float D[8][4], O[4];
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) D[mt][e] = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) O[e] = 0.0f;
+            for (int j = 0; j < ksub; ++j)
+              if (kb * GM_TK + r0 + 16 * j < g.K)
+                k16_step<NT>(wst, ast, r0 + 16 * j, wn, gq, t, nt, mlo, mhi, D, O);
+            // scale block done: acc += s_eff * (D - bias * sum a)
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float c = fmaf(-(e < 2 ? blo : bhi), O[e & 1], D[mt][e]);
+                acc[mt][nt][e] = fmaf(se[2 * mt + (e >> 1)], c, acc[mt][nt][e]);
+              }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty[s]);
+    }
+
+    // ------------------------ end of a tile segment ------------------------
+    // Sum the four groups of each column half (fixed-order tree); the warps of
+    // group 0 end with the column half's sums.
+#pragma unroll
+    for (int half = GM_GROUPS / 2; half >= 1; half >>= 1) {
+      consumers_sync();
+      if (grp >= half && grp < 2 * half) {
+        float *r = red + (size_t)((grp - half) * 2 + wn) * 32 * NT * 32;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) r[((mt * NT + nt) * 4 + e) * 32 + lane] = acc[mt][nt][e];
+      }
+      consumers_sync();
+      if (grp < half) {
+        const float *r = red + (size_t)(grp * 2 + wn) * 32 * NT * 32;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][nt][e] += r[((mt * NT + nt) * 4 + e) * 32 + lane];
+      }
+    }
+    const int uf = tile * g.kunits, ul = uf + g.kunits - 1;
+    const int cf = cta_of(uf, g.units, g.grid), cl = cta_of(ul, g.units, g.grid);
+    const int n0 = tile * GM_TN;
+    if (cf == cl) {
+      // The whole tile is this CTA's: write the output.
+      if (grp == 0 && ok) {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int col = n0 + wn * 128 + gq * 16 + 2 * mt;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int m = nt * 8 + 2 * t;
+            if (m < g.M)
+              *reinterpret_cast<__half2 *>(g.y + (int64_t)m * g.N + col) =
+                  __floats2half2_rn(acc[mt][nt][0], acc[mt][nt][2]);
+            if (m + 1 < g.M)
+              *reinterpret_cast<__half2 *>(g.y + (int64_t)(m + 1) * g.N + col) =
+                  __floats2half2_rn(acc[mt][nt][1], acc[mt][nt][3]);
+          }
+        }
+      }
+    } else {
+      const int slot = tile == first_tile ? 0 : 1;
+      float *part = g.partials + (size_t)(b * 2 + slot) * g.M * GM_TN;
+      if (grp == 0) {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int col = wn * 128 + gq * 16 + 2 * mt;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int m = nt * 8 + 2 * t;
+            if (m < g.M)
+              *reinterpret_cast<float2 *>(part + m * GM_TN + col) =
+                  make_float2(acc[mt][nt][0], acc[mt][nt][2]);
+            if (m + 1 < g.M)
+              *reinterpret_cast<float2 *>(part + (m + 1) * GM_TN + col) =
+                  make_float2(acc[mt][nt][1], acc[mt][nt][3]);
+          }
+        }
+      }
+      consumers_sync();
+      if (threadIdx.x == 0) {
+        // Release this CTA's partial (the barrier above orders the other
+        // threads' stores before it), acquire the others' if last.
+        const uint32_t prev = atom_add_acq_rel(g.counters + tile, 1u);
+        const bool last = prev + 1 == (uint32_t)(cl - cf + 1);
+        if (last) g.counters[tile] = 0u;
+        flags[1] = last ? 1 : 0;
+      }
+      consumers_sync();
+      if (flags[1] && ok) {
+        // Last to arrive: sum the contributors' partials in CTA order, with the
+        // loads of up to 16 contributors in flight before the first add.
+        const int nc = cl - cf + 1;
+        for (int e = threadIdx.x; e < g.M * (GM_TN / 4); e += GM_CONSUMERS * 32) {
+          float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          for (int c0 = 0; c0 < nc; c0 += 16) {
+            float4 v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+              const int c = cf + c0 + j;
+              if (c0 + j < nc) {
+                const int cslot = unit_begin(c, g.units, g.grid) / g.kunits == tile ? 0 : 1;
+                v[j] = __ldcg(reinterpret_cast<const float4 *>(
+                                  g.partials + (size_t)(c * 2 + cslot) * g.M * GM_TN) + e);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              sum.x += v[j].x;
+              sum.y += v[j].y;
+              sum.z += v[j].z;
+              sum.w += v[j].w;
+            }
+          }
+          const int m = e / (GM_TN / 4), col = (e % (GM_TN / 4)) * 4;
+          __half2 *dst = reinterpret_cast<__half2 *>(g.y + (int64_t)m * g.N + n0 + col);
+          dst[0] = __floats2half2_rn(sum.x, sum.y);
+          dst[1] = __floats2half2_rn(sum.z, sum.w);
+        }
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.0f;
+    seg0 = seg1;
+  }
+}
+
+struct MmaPlan {
+  int nt = 1, grid = 0, units = 0, kunits = 0, ntiles = 0, srows = 0, block = 0;
+  size_t ws = 0;
+};
+
+MmaPlan mma_plan(const DqMmParams &p) {
+  MmaPlan m;
+  m.nt = p.M <= 8 ? 1 : 2;
+  m.ntiles = (int)(p.N / GM_TN);
+  m.kunits = (int)((p.K + GM_TK - 1) / GM_TK);
+  m.units = m.ntiles * m.kunits;
+  m.grid = std::min(m.units, sm_count());
+  if (p.slayout == kScaleTensor) {
+    m.srows = 0;
+  } else if (p.slayout == kScaleAxis1) {
+    m.srows = 1;
+  } else {
+    m.block = (int)p.block;
+    m.srows = p.block < GM_TK ? (int)(GM_TK / p.block) : 1;
+  }
+  bool split = false;
+  for (int tile = 0; tile < m.ntiles && !split; ++tile) {
+    const int uf = tile * m.kunits, ul = uf + m.kunits - 1;
+    const int cf = (int)(((int64_t)(uf + 1) * m.grid - 1) / m.units);
+    const int cl = (int)(((int64_t)(ul + 1) * m.grid - 1) / m.units);
+    split = cf != cl;
+  }
+  // Arrival counters always (they start the workspace); partials when a tile is shared.
+  m.ws = kCounterBytes + (split ? (size_t)m.grid * 2 * p.M * GM_TN * 4 : 0);
+  return m;
+}
+
+template <int NT>
+int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStream_t st) {
+  CUtensorMap map_w, map_a, map_s;
+  {
+    const uint64_t dims[2] = {(uint64_t)p.N / 2, (uint64_t)p.K};
+    const uint64_t strides[1] = {(uint64_t)p.N / 2};
+    const uint32_t box[2] = {GM_TN / 2, GM_TK};
+    int rc = make_tensor_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p.w, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    const uint64_t strides[1] = {(uint64_t)p.K * 2};
+    const uint32_t box[2] = {64, (uint32_t)(8 * NT)};
+    int rc = make_tensor_map(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.a, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  map_s = map_w;
+  if (m.srows) {
+    const uint64_t rows = p.slayout == kScaleAxis1 ? 1 : (uint64_t)p.s_alen;
+    const uint64_t dims[2] = {(uint64_t)p.N, rows};
+    const uint64_t strides[1] = {(uint64_t)p.N * 2};
+    const uint32_t box[2] = {GM_TN, (uint32_t)m.srows};
+    int rc = make_tensor_map(&map_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.scale, dims, strides,
+                             box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  GmArgs a{};
+  a.y = static_cast<__half *>(p.y);
+  a.counters = static_cast<uint32_t *>(workspace);
+  a.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kCounterBytes);
+  a.M = (int)p.M;
+  a.N = (int)p.N;
+  a.K = (int)p.K;
+  a.ntiles = m.ntiles;
+  a.kunits = m.kunits;
+  a.units = m.units;
+  a.grid = m.grid;
+  a.block = m.block;
+  a.srows = m.srows;
+  a.is_signed = p.wdt == kInt4;
+  a.scalar_scale = reinterpret_cast<const uint16_t *>(p.scale);
+  auto kern = dq_gemv_mma<NT>;
+  const size_t smem = GmSmem<NT>::kDynamic;
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)m.grid);
+  cfg.blockDim = dim3(GM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2_CUDA(cudaLaunchKernelEx(&cfg, kern, map_w, map_a, map_s, a));
+  return B2_OK;
+}
+
+} // namespace
+
+bool dq_mma_eligible(const DqMmParams &p) {
+  if (p.wdt != kInt4 && p.wdt != kUint4) return false;
+  if (!p.s_f16 || p.zp != nullptr || p.ydt != kFloat16) return false;
+  if (p.cast_dt != 0 && p.cast_dt != kFloat16) return false;
+  if (p.M < 1 || p.M > 16 || p.N < GM_TN || p.N % GM_TN != 0 || p.K < 16 || p.K % 8 != 0)
+    return false;
+  if (p.N > (int64_t)1 << 30 || p.K > (int64_t)1 << 30) return false;
+  if (p.N / GM_TN > (int64_t)kMaxCounters) return false;
+  // unit numbers times the grid size stay below 2^31 (32-bit index arithmetic)
+  const int64_t units = (p.N / GM_TN) * ((p.K + GM_TK - 1) / GM_TK);
+  if (units * (int64_t)(sm_count() + 1) >= ((int64_t)1 << 31)) return false;
+  switch (p.slayout) {
+  case kScaleTensor:
+  case kScaleAxis1: return true;
+  case kScaleAxis0Block:
+    if (p.block % 32 != 0) return false;
+    return p.block <= GM_TK ? GM_TK % p.block == 0 : p.block % GM_TK == 0;
+  default: return false;
+  }
+}
+
+bool dq_mma_aligned(const DqMmParams &p) {
+  auto al = [](const void *q, uintptr_t n) { return (reinterpret_cast<uintptr_t>(q) % n) == 0; };
+  return al(p.a, 16) && al(p.w, 16) && al(p.y, 4) &&
+         (p.slayout == kScaleTensor || al(p.scale, 16));
+}
+
+size_t dq_mma_workspace(const DqMmParams &p) { return mma_plan(p).ws; }
+
+int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
+  const MmaPlan m = mma_plan(p);
+  if (m.ws && workspace == nullptr) B2_FAIL(B2_ERR_WORKSPACE, "workspace of %zu bytes required", m.ws);
+  if (m.nt == 1) return launch_mma<1>(p, m, workspace, st);
+  return launch_mma<2>(p, m, workspace, st);
+}
+
+} // namespace b2

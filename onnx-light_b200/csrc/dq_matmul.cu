@@ -649,7 +649,7 @@ static int dq_mm_validate(const b2_tensor *a, const b2_tensor *w, const b2_tenso
 }
 
 struct Plan {
-  int kind = 0; // 0 simt, 1 gemv, 2 tensor core
+  int kind = 0; // 0 simt, 1 gemv, 2 tensor core, 3 register-MMA decode
   int ksplit = 1;
   int64_t kchunk = 0;
   dim3 grid;
@@ -671,7 +671,7 @@ static int wbits(int dt) {
 // (tests use it to exercise every kernel on the same shapes); the default
 // picks the decode GEMV for M <= 4, the tensor-core kernel for 16-bit
 // activations otherwise, and the CUDA-core GEMM for FLOAT activations.
-enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3 };
+enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3, kPathMma = 4 };
 
 static DqPath forced_path() {
   const char *e = getenv("ONNXL_B200_DQ_KERNEL");
@@ -679,6 +679,7 @@ static DqPath forced_path() {
   if (!strcmp(e, "tc")) return kPathTc;
   if (!strcmp(e, "gemv")) return kPathGemv;
   if (!strcmp(e, "simt")) return kPathSimt;
+  if (!strcmp(e, "mma")) return kPathMma;
   return kPathAuto;
 }
 
@@ -695,6 +696,11 @@ static Plan make_plan(const DqMmParams &p) {
                        (p.slayout != kScaleAxis0Block || p.block % 32 == 0) &&
                        ((p.N * bits / 8) % 16 == 0);
   const DqPath forced = forced_path();
+  if ((forced == kPathAuto || forced == kPathMma) && dq_mma_eligible(p)) {
+    pl.kind = 3;
+    pl.ws = dq_mma_workspace(p);
+    return pl;
+  }
   if ((forced == kPathAuto && dq_tc_supported(p)) || (forced == kPathTc && dq_tc_eligible(p))) {
     pl.kind = 2;
     pl.ws = dq_tc_workspace(p);
@@ -829,6 +835,19 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
     // Empty reduction: y = 0.
     B2_CUDA(cudaMemsetAsync(y->data, 0, (size_t)p.M * p.N * (p.ydt == kFloat ? 4 : 2), st));
     return B2_OK;
+  }
+  if (pl.kind == 3) {
+    if (dq_mma_aligned(p)) return dq_mma_launch(p, workspace, st);
+    // TMA needs 16-byte aligned tensors: fall back to the unsplit CUDA-core
+    // kernel, which needs no workspace.
+    Plan one;
+    one.kchunk = p.K;
+    one.ksplit = 1;
+    one.grid = dim3((unsigned)((p.N + SIMT_BN - 1) / SIMT_BN),
+                    (unsigned)((p.M + SIMT_BM - 1) / SIMT_BM), 1);
+    p.kchunk = p.K;
+    p.ksplit = 1;
+    return launch_simt<__half>(p, one, st);
   }
   if (pl.kind == 2) return dq_tc_launch(p, workspace, st);
   if (pl.kind == 1) return launch_gemv(p, pl, st);

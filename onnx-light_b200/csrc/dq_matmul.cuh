@@ -41,4 +41,11 @@ bool dq_tc_supported(const DqMmParams &p); // eligible and chosen by default
 size_t dq_tc_workspace(const DqMmParams &p);
 int dq_tc_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
 
+// Decode path on register-level MMA (dq_gemv_mma.cu): M <= 16, INT4/UINT4
+// weights, FLOAT16 scales, activations and output.
+bool dq_mma_eligible(const DqMmParams &p); // shape/type constraints
+bool dq_mma_aligned(const DqMmParams &p);  // pointer alignment TMA needs
+size_t dq_mma_workspace(const DqMmParams &p);
+int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
+
 } // namespace b2

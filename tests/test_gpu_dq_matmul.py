@@ -172,3 +172,59 @@ def test_cuda_core_paths_config3_decode(b2, cuda, monkeypatch, path):
     monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", path)
     y, ref = run_case(b2, 2, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=21)
     assert rel_l2(y, ref) <= TOL[O.FLOAT16]
+
+
+# ---------------------------------------------------------------------------
+# Decode path on register-level MMA (M <= 16, INT4/UINT4, FLOAT16 chain): the
+# default for these shapes.  Stream-K splits, whole-tile CTAs, partial last
+# stages, every supported scale layout.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 12, 16])
+def test_mma_decode_config3_batches(b2, cuda, M):
+    y, ref = run_case(b2, M, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=40 + M)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16]
+
+
+@pytest.mark.parametrize("K,N", [(4096, 11008), (11008, 4096), (128, 256), (128, 76800),
+                                 (256, 1024), (4096, 1024)])
+def test_mma_decode_llama_and_edge_shapes(b2, cuda, K, N):
+    for M in (1, 4):
+        y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=K + N + M)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+@pytest.mark.parametrize("wdt,block,axis", [
+    (O.INT4, 32, 0), (O.UINT4, 64, 0), (O.UINT4, 128, 0), (O.INT4, 256, 0),
+    (O.INT4, None, 1),   # per-column scales
+    (O.UINT4, 0, 0),     # per-tensor scale
+])
+def test_mma_decode_scale_layouts(b2, cuda, wdt, block, axis):
+    for M in (1, 6):
+        y, ref = run_case(b2, M, 1024, 768, wdt, O.FLOAT16, O.FLOAT16, axis=axis, block=block,
+                          seed=M + 7)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+def test_mma_decode_partial_last_stage_and_cast(b2, cuda):
+    # K = 200: the last 128-row stage is partly outside the weight (TMA zero fill);
+    # per-column scales; an explicit Cast(FLOAT16) between the nodes.
+    for M in (1, 11):
+        y, ref = run_case(b2, M, 200, 512, O.INT4, O.FLOAT16, O.FLOAT16, axis=1, block=None,
+                          cast=O.FLOAT16, seed=M)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+def test_mma_decode_unaligned_activations_fall_back(b2, cuda):
+    # Activations at an address that is not 16-byte aligned cannot be read by
+    # TMA; the call still succeeds (CUDA-core kernel) and agrees.
+    M, K, N = 2, 512, 512
+    w = random_q(5, (K, N), O.INT4)
+    s = to_dev(scale_raw(O.rand_uniform(6, (K // 128 * N,), 0.002, 0.02), O.FLOAT16),
+               torch.float16).reshape(K // 128, N)
+    a = torch.randn(M * K + 1, device="cuda").half()
+    tw = b2.QTensor(to_dev(w), O.INT4, (K, N))
+    y_off = b2.DequantizeMatMul()(a[1:].view(M, K), tw, s, None, axis=0)
+    y_al = b2.DequantizeMatMul()(a[1:].clone().view(M, K), tw, s, None, axis=0)
+    torch.cuda.synchronize()
+    assert rel_l2(y_off.float().cpu().numpy(), y_al.float().cpu().numpy()) <= TOL[O.FLOAT16]

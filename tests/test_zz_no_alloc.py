@@ -53,7 +53,8 @@ def _call(b2, fn_name, w, s, a, K, N, M):
 @pytest.mark.parametrize("M", [1, 32])
 def test_noalloc_matches_workspace_entry_point_twice_in_a_row(b2, cuda, M):
     # Two different shapes back to back: the second call reuses the fixed
-    # scratch the first one left behind (both plans split K across CTAs).
+    # scratch the first one left behind (M = 32 takes the tensor-core plan,
+    # which splits K across CTAs through the scratch; M = 1 needs none).
     for seed, (K, N) in ((11, (4096, 4096)), (12, (11008, 4096))):
         w, s, a = _inputs(seed + M, K, N, M)
         got = _call(b2, "noalloc", w, s, a, K, N, M)
