@@ -10,7 +10,7 @@
 //   warp 0      TMA: raw packed weight tile [64 k x 128 n] (no swizzle) and the
 //               activation tile [BN m x 64 k] (128-byte swizzle, K-major) into
 //               a STAGES-deep ring;
-//   warps 2-5   dequantize the raw weight tile in registers with the
+//   warps 2-9   dequantize the raw weight tile in registers with the
 //               reference's rounding (fp32 (q - zp) * s, rounded to the
 //               DequantizeLinear output type and to the Cast type) and store
 //               it as the MMA's A operand in the 128-byte-swizzled MN-major
@@ -27,7 +27,8 @@ namespace b2 {
 
 constexpr int DT_BM = 128;     // weight columns per tile (MMA M)
 constexpr int DT_BK = 64;      // k per stage (one 128-byte swizzle row of fp16)
-constexpr int DT_THREADS = 192;
+constexpr int DT_PROD_WARPS = 8; // dequantizing warps (2 .. 9)
+constexpr int DT_THREADS = 64 + DT_PROD_WARPS * 32;
 constexpr uint32_t DT_AOP_BYTES = DT_BM * DT_BK * 2; // 16 KB dequantized operand
 
 enum DqMode : int { kModeI4H = 0, kModeF8 = 1, kModeF4 = 2, kModeGeneric = 3 };
@@ -55,10 +56,11 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
 // Dequantizes the 8 weights (k, n..n+7) into 8 operand values (uint4).
 // `srow` points at the staged scale row of this weight row (nullptr: read the
 // scale tensor in global memory).
+template <int MODE>
 __device__ __forceinline__ uint4 dequant8(const DqTcArgs &a, const uint8_t *raw_row, int nl,
                                           int64_t k, int64_t n, const uint8_t *srow) {
   const DqMmParams &p = a.p;
-  if (a.mode == kModeI4H) {
+  if constexpr (MODE == kModeI4H) {
     // int4/uint4 x fp16 scale (blocked along K or per column), fp16 operand.
     const uint32_t w = *reinterpret_cast<const uint32_t *>(raw_row + nl / 2);
     const int64_t kb = p.slayout == kScaleAxis0Block ? (int64_t)p.fdiv_block.div((uint32_t)k) : 0;
@@ -98,11 +100,11 @@ __device__ __forceinline__ uint4 dequant8(const DqTcArgs &a, const uint8_t *raw_
   // fp32 path: value = (q - zp) * s in fp32, rounded to the DequantizeLinear
   // output type (fp16 when the scale is fp16), then to the operand type.
   float q[8];
-  if (a.mode == kModeF8) {
+  if constexpr (MODE == kModeF8) {
     const uint2 w = *reinterpret_cast<const uint2 *>(raw_row + nl);
 #pragma unroll
     for (int j = 0; j < 8; ++j) q[j] = dec_f8e4m3fn(((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xffu);
-  } else if (a.mode == kModeF4) {
+  } else if constexpr (MODE == kModeF4) {
     const uint32_t w = *reinterpret_cast<const uint32_t *>(raw_row + nl / 2);
 #pragma unroll
     for (int j = 0; j < 8; ++j) q[j] = dec_f4e2m1((w >> (4 * j)) & 0xfu);
@@ -141,6 +143,7 @@ __device__ __forceinline__ void store_val(const DqMmParams &p, int64_t m, int64_
   else reinterpret_cast<uint16_t *>(p.y)[m * p.N + n] = f32_to_bf16_bits(v);
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(DT_THREADS, 1)
     dq_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_s, const DqTcArgs args) {
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
     abort_flag = 0;
     for (int s = 0; s < S; ++s) {
       tc::mbar_init(&full[s], 1);
-      tc::mbar_init(&deq[s], 4);
+      tc::mbar_init(&deq[s], DT_PROD_WARPS);
       tc::mbar_init(&empty[s], 1);
     }
     tc::mbar_init(done, 1);
@@ -198,7 +201,7 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
         }
         uint8_t *st = smem + (size_t)s * args.stage_bytes;
         const int32_t k = (int32_t)(kbeg + (int64_t)kt * DT_BK);
-        const bool raw_tma = args.mode != kModeGeneric;
+        const bool raw_tma = MODE != kModeGeneric;
         tc::mbar_expect_tx(&full[s], (raw_tma ? args.raw_bytes : 0u) + args.b_bytes + args.s_bytes);
         tc::tma_load_2d(st + DT_AOP_BYTES, &map_a, &full[s], k, (int32_t)m0);
         if (args.s_bytes)
@@ -206,7 +209,7 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
                           (int32_t)n0, (int32_t)(k / p.block));
         if (raw_tma) {
           // raw weights: [k rows][128 n] as bytes (int4: 64 bytes, 8-bit: 128 bytes per row)
-          const int32_t xb = args.mode == kModeF8 ? (int32_t)n0 : (int32_t)(n0 / 2);
+          const int32_t xb = MODE == kModeF8 ? (int32_t)n0 : (int32_t)(n0 / 2);
           tc::tma_load_2d(st + DT_AOP_BYTES + args.b_bytes, &map_w, &full[s], xb, k);
         }
       }
@@ -237,11 +240,12 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
       tc::tc_commit(done);
     }
   } else {
-    // ----- dequant producers (warps 2..5, 128 threads) -----
+    // ----- dequant producers (warps 2..9) -----
+    constexpr int kRowStep = DT_PROD_WARPS * 32 / 16; // rows of the stage a pass covers
     const int t = threadIdx.x - 64;
     const int cc = t & 15;   // 8-column chunk (n_local = cc * 8)
-    const int r0 = t >> 4;   // first k row (0..7), rows r0 + 8 i
-    const uint32_t raw_row_bytes = args.mode == kModeF8 ? 128 : 64;
+    const int r0 = t >> 4;   // first k row, rows r0 + kRowStep i
+    const uint32_t raw_row_bytes = MODE == kModeF8 ? 128 : 64;
     for (int kt = 0; kt < kt_count && !abort_flag; ++kt) {
       const int s = kt % S;
       if (!tc::mbar_wait(&full[s], (kt / S) & 1)) {
@@ -256,14 +260,14 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
       const uint32_t s_esz = p.s_f16 ? 2u : 4u;
       const uint32_t kst_b = sst ? p.fdiv_block.div((uint32_t)kst) : 0u;
 #pragma unroll 2
-      for (int i = 0; i < DT_BK / 8; ++i) {
-        const int r = r0 + 8 * i; // k row within the stage
+      for (int i = 0; i < DT_BK / kRowStep; ++i) {
+        const int r = r0 + kRowStep * i; // k row within the stage
         const int64_t k = kst + r;
         const int nl = cc * 8;
         const uint8_t *srow =
             sst ? sst + (size_t)(p.fdiv_block.div((uint32_t)k) - kst_b) * DT_BM * s_esz : nullptr;
         uint4 o = make_uint4(0, 0, 0, 0);
-        if (k < kend && n0 + nl < p.N) o = dequant8(args, raw + r * raw_row_bytes, nl, k, n0 + nl, srow);
+        if (k < kend && n0 + nl < p.N) o = dequant8<MODE>(args, raw + r * raw_row_bytes, nl, k, n0 + nl, srow);
         // MN-major 128-byte swizzle: block (nl / 64) at 8 KB, row r at 128 B,
         // 16-byte chunk (nl % 64) / 8 XOR (r % 8)
         const int blk = nl >> 6, chunk = (nl & 63) >> 3;
@@ -274,25 +278,27 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&deq[s]);
     }
-    // ----- epilogue -----
-    const int g = warp & 3; // TMEM lane group
-    const bool ok = tc::mbar_wait(done, 0, 4000000000ull);
-    if (!ok) atomicExch(args.status, tc::kTimeoutMma);
-    tc::tc_fence_after();
-    const int64_t n = n0 + g * 32 + lane;
-    if (ok && !abort_flag) {
-      float *part = p.ksplit > 1 ? p.partials + (int64_t)split * p.M * p.N : nullptr;
-      for (int ch = 0; ch < args.bn / 32 + ((args.bn & 31) ? 1 : 0); ++ch) {
-        uint32_t r[32];
-        tc::tmem_ld32(tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(ch * 32), r);
-        tc::tmem_ld_wait();
+    // ----- epilogue (warps 2..5: one TMEM lane group each) -----
+    if (warp < 6) {
+      const int g = warp & 3; // TMEM lane group
+      const bool ok = tc::mbar_wait(done, 0, 4000000000ull);
+      if (!ok) atomicExch(args.status, tc::kTimeoutMma);
+      tc::tc_fence_after();
+      const int64_t n = n0 + g * 32 + lane;
+      if (ok && !abort_flag) {
+        float *part = p.ksplit > 1 ? p.partials + (int64_t)split * p.M * p.N : nullptr;
+        for (int ch = 0; ch < args.bn / 32 + ((args.bn & 31) ? 1 : 0); ++ch) {
+          uint32_t r[32];
+          tc::tmem_ld32(tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(ch * 32), r);
+          tc::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int64_t m = m0 + ch * 32 + j;
-          if (ch * 32 + j < args.bn && m < p.M && n < p.N) {
-            const float v = __uint_as_float(r[j]);
-            if (part) part[m * p.N + n] = v;
-            else store_val(p, m, n, v);
+          for (int j = 0; j < 32; ++j) {
+            const int64_t m = m0 + ch * 32 + j;
+            if (ch * 32 + j < args.bn && m < p.M && n < p.N) {
+              const float v = __uint_as_float(r[j]);
+              if (part) part[m * p.N + n] = v;
+              else store_val(p, m, n, v);
+            }
           }
         }
       }
@@ -373,7 +379,8 @@ static TcPlan tc_plan(const DqMmParams &p) {
   const int sms = sm_count();
   int64_t split = 1;
   if (ntiles * mtiles < sms && ntiles * mtiles <= (int64_t)kMaxCounters) {
-    split = (sms + ntiles * mtiles - 1) / (ntiles * mtiles);
+    // one CTA per SM (the ring takes most of shared memory): stay within one wave
+    split = sms / (ntiles * mtiles);
     const int64_t maxsplit = (p.K + 4 * DT_BK - 1) / (4 * DT_BK); // >= 4 stages per split
     if (split > maxsplit) split = maxsplit;
     if (split < 1) split = 1;
@@ -465,9 +472,12 @@ int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st) {
     }
   }
   if (!t.s_bytes) map_s = map_a; // unused
-  B2_CUDA(cudaFuncSetAttribute(dq_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)t.smem));
-  dq_gemm_tc_kernel<<<t.grid, DT_THREADS, t.smem, st>>>(map_w, map_a, map_s, a);
+  auto kern = t.mode == kModeI4H ? dq_gemm_tc_kernel<kModeI4H>
+              : t.mode == kModeF8  ? dq_gemm_tc_kernel<kModeF8>
+              : t.mode == kModeF4  ? dq_gemm_tc_kernel<kModeF4>
+                                   : dq_gemm_tc_kernel<kModeGeneric>;
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)t.smem));
+  kern<<<t.grid, DT_THREADS, t.smem, st>>>(map_w, map_a, map_s, a);
   B2_LAUNCH_CHECK();
   return B2_OK;
 }
