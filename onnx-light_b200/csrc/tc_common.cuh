@@ -48,14 +48,17 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// The waiting thread is suspended in hardware until the phase completes or
+// about 0.1 ms pass (the suspend-time hint), so a waiting warp does not spin
+// and take issue slots from the warps that share its scheduler.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
       : "memory");
   return ok != 0;
 }
@@ -67,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && globaltimer() - t0 > limit_ns) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
 }
 
