@@ -295,7 +295,8 @@ def gpu_arm(args):
             achieved = sum(p[1] for p in per) / (sum(p[2] for p in per) * 1e-3) / 1e9
         roof = {"bound": "hbm", "kernel": "dq_gemv_mma", "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                "peak_source": peak_src, "traffic": traffic_from_profile(),
+                "peak_source": peak_src, "traffic": traffic_from_profile(B) if world == 1 else None,
+                "traffic_unit": "DRAM bytes per step (ncu capture of batch 1, profiles/traffic.json)",
                 "algorithmic_bytes_per_step": nbytes,
                 "per_projection_us": {p[0]: round(p[2] * 1e3, 2) for p in per},
                 "per_projection_gbs": {p[0]: round(p[1] / (p[2] * 1e-3) / 1e9, 1) for p in per}}
@@ -381,13 +382,15 @@ def measured_peak():
         return 6650.0, "fallback 6.65 TB/s"
 
 
-def traffic_from_profile():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+def traffic_from_profile(batch: int):
+    """DRAM bytes of one decode step measured by ncu (profiles/traffic.json, batch 1);
+    weights and scales are over 99.9 % of them, so other batches add their activation bytes."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get("dq_gemv")
-    except (OSError, ValueError):
+            t = json.load(f)["dq_gemv_mma"]
+        return int(t["bytes_per_step"]) + (batch - 1) * (step_bytes(batch) - step_bytes(batch - 1))
+    except (OSError, ValueError, KeyError):
         return None
 
 
