@@ -345,6 +345,14 @@ def gpu_arm(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(B)
 
+    # Secondary BASELINE metrics (same GPU, after the headline timing).
+    secondary = None
+    if rank == 0 and world == 1 and not args.no_secondary:
+        want_cpu = not args.no_cpu_baseline
+        secondary = {"attention_config4": attention_config4(b2, synth, device, stream, want_cpu),
+                     "matmul_integer_config2": matmul_integer_config2(b2, synth, device, stream,
+                                                                      want_cpu)}
+
     if rank == 0:
         clocks = clk.summary()
         line = {
@@ -366,11 +374,113 @@ def gpu_arm(args):
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _graph_time(stream, fn, reps, chunk=64):
+    """Device ms per call of fn(), replayed as CUDA graphs of `chunk` calls."""
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(chunk):
+            fn()
+    with torch.cuda.stream(stream):
+        g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        n = max(1, reps // chunk)
+        for _ in range(n):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / (n * chunk)
+
+
+def attention_config4(b2, synth, device, stream, cpu):
+    """GQA decode, fp16, batch 32, 32 query / 8 KV heads,
+    head 128, past 4096, causal, scale 1/sqrt(128); the new token is appended in
+    place into a capacity-reserved cache.  Every step reads the whole cache
+    (537 MB > L2).  Metric: tokens/s (batch rows per step / step time)."""
+    import math
+    import torch
+    B, Hq, Hkv, D, past = 32, 32, 8, 128, 4096
+    cache = b2.KVCache(B, Hkv, past + 1, D, device=device)
+    n = B * Hkv * (past + 1) * D
+    cache.k.view(-1).copy_(synth.convert(synth.randn(4001, (n,), 0.0, 0.5, device=device), FLOAT16, (n,)))
+    cache.v.view(-1).copy_(synth.convert(synth.randn(4002, (n,), 0.0, 0.5, device=device), FLOAT16, (n,)))
+    q = synth.convert(synth.randn(4003, (B * Hq * D,), 0.0, 0.5, device=device), FLOAT16, (B, Hq, 1, D))
+    k = synth.convert(synth.randn(4004, (B * Hkv * D,), 0.0, 0.5, device=device), FLOAT16, (B, Hkv, 1, D))
+    v = synth.convert(synth.randn(4005, (B * Hkv * D,), 0.0, 0.5, device=device), FLOAT16, (B, Hkv, 1, D))
+    y = torch.empty((B, Hq, 1, D), dtype=torch.float16, device=device)
+    att = b2.Attention()
+    attrs = b2.Attributes(has_scale=True, scale=1.0 / math.sqrt(D), is_causal=True)
+
+    def step():
+        cache.length = past
+        att(q, k, v, attrs, cache=cache, out=y)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    ms = _graph_time(stream, step, 512, chunk=32)
+    nbytes = 537657344  # KV read incl. the new token + Q/Y + the append
+    peak, src = measured_peak()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    out = {"metric": "GQA Attention decode tokens/s/GPU (config 4)",
+           "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 5),
+           "dtype": "fp16", "config": {"batch": B, "q_heads": Hq, "kv_heads": Hkv, "head": D,
+                                        "past": past, "causal": True},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 4), "peak_source": src,
+                        "algorithmic_bytes_per_step": nbytes}}
+    if cpu:
+        out["cpu_baseline"] = _cpu_attention_sample()
+    return out
+
+
+def matmul_integer_config2(b2, synth, device, stream, cpu):
+    """MatMulInteger uint8 A [512, 4096] (zero point 128) x
+    int8 B [4096, 11008] (per-column zero points in [-4, 4]) -> int32."""
+    import torch
+    M, K, N = 512, 4096, 11008
+    a = synth.randint(2001, (M * K,), 0, 255, device=device).to(torch.uint8).view(M, K)
+    bq = synth.randint(2002, (K * N,), -127, 127, device=device).to(torch.int8).view(K, N)
+    azp = torch.tensor(128, dtype=torch.uint8, device=device)
+    bzp = synth.randint(2003, (N,), -4, 4, device=device).to(torch.int8)
+    y = torch.empty((M, N), dtype=torch.int32, device=device)
+    mmi = b2.MatMulInteger()
+
+    def step():
+        mmi(a, bq, azp, bzp, out=y)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    ms = _graph_time(stream, step, 256, chunk=16)
+    ops = 2 * M * K * N
+    peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = 2.0 * float(json.load(f)["bf16_tflops"])
+        src = "2 x measured bf16 (MEASURED_PEAKS.json; dense int8 is twice bf16)"
+    except (OSError, KeyError, ValueError):
+        peak, src = 4500.0, "nominal 4.5 POPS dense int8"
+    tops = ops / (ms * 1e-3) / 1e12
+    out = {"metric": "MatMulInteger TOP/s (config 2)", "value": round(tops, 2), "unit": "TOP/s",
+           "ms_per_call": round(ms, 4), "dtype": "u8 x s8 -> s32",
+           "config": {"M": M, "K": K, "N": N, "a_zero_point": "scalar 128",
+                      "b_zero_point": "per column"},
+           "roofline": {"bound": "tensor", "achieved": round(tops, 2), "peak": peak,
+                        "unit": "TOP/s", "frac": round(tops / peak, 4), "peak_source": src}}
+    if cpu:
+        out["cpu_baseline"] = _cpu_mmi_sample()
+    return out
 
 
 def measured_peak():
@@ -451,6 +561,54 @@ def cpu_baseline_sample(B):
                           f"{t * 1e3:.1f} ms per call, onnx-light kernels compiled from source"}
     except Exception as e:  # the baseline must never break the GPU line
         return {"value": None, "unit": "GB/s", "cores": 0, "kind": "error", "sample": repr(e)[:200]}
+
+
+def _cpu_attention_sample():
+    """Reference Attention (oracle/_ref) for config 4 at batch 1, scaled x32."""
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        if not O.ref_available():
+            return None
+        Hq, Hkv, D, past = 32, 8, 128, 4096
+        h = lambda seed, shape: O.f32_to_f16_bits(O.randn(seed, shape, 0.0, 0.5))
+        q, k, v = h(1, (1, Hq, 1, D)), h(2, (1, Hkv, 1, D)), h(3, (1, Hkv, 1, D))
+        pk, pv = h(4, (1, Hkv, past, D)), h(5, (1, Hkv, past, D))
+        run = lambda: O.ref_attention(q, k, v, O.FLOAT16, scale=D ** -0.5, is_causal=True,
+                                      past_k=pk, past_v=pv)
+        run()
+        t0 = time.perf_counter()
+        run()
+        t = (time.perf_counter() - t0) * 32
+        return {"value": round(32 / t, 2), "unit": "tokens/s", "cores": O.ref_thread_count(),
+                "kind": "reference",
+                "sample": f"batch 1 of config 4 ({t / 32 * 1e3:.1f} ms), scaled x32 to batch 32"}
+    except Exception as e:
+        return {"value": None, "kind": "error", "sample": repr(e)[:200]}
+
+
+def _cpu_mmi_sample():
+    """Reference MatMulInteger (single-threaded in onnx-light) on N = 128
+    columns of config 2, scaled to N = 11008."""
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import numpy as np
+        import oracle as O
+        if not O.ref_available():
+            return None
+        M, K, n = 512, 4096, 128
+        a = O.randint(1, (M * K,), 0, 255).astype(np.uint8).reshape(M, K)
+        b = O.randint(2, (K * n,), -127, 127).astype(np.int8).reshape(K, n)
+        bz = O.randint(3, (n,), -4, 4).astype(np.int8)
+        t0 = time.perf_counter()
+        O.ref_matmul_integer(a, O.UINT8, b, O.INT8, np.array([128], np.uint8), bz, (), (n,))
+        t = (time.perf_counter() - t0) * (11008 / n)
+        return {"value": round(2 * M * K * 11008 / t / 1e12, 6), "unit": "TOP/s", "cores": 1,
+                "kind": "reference",
+                "sample": f"N = 128 of config 2 ({t * n / 11008:.2f} s), scaled x86 to N = 11008; "
+                          f"onnx-light's MatMulInteger is single-threaded"}
+    except Exception as e:
+        return {"value": None, "kind": "error", "sample": repr(e)[:200]}
 
 
 def reference_arm(args):
@@ -540,6 +698,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the config-4 attention and config-2 MatMulInteger measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
