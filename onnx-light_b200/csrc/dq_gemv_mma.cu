@@ -62,13 +62,17 @@ namespace {
 constexpr int GM_TN = 256;                         // columns per tile (128 packed bytes / row)
 constexpr int GM_TK = 128;                         // weight rows per stage
 constexpr int GM_STAGES = 8;                       // ring depth
-constexpr int GM_GROUPS = 4;                       // stage groups of consumer warps
-constexpr int GM_CONSUMERS = 2 * GM_GROUPS;        // consumer warps
+constexpr int GM_QUADS = 4;                        // consumer warps per column half
+constexpr int GM_CONSUMERS = 2 * GM_QUADS;         // consumer warps
 constexpr int GM_THREADS = (GM_CONSUMERS + 1) * 32;
 constexpr uint32_t GM_W_BYTES = GM_TK * GM_TN / 2; // 16 KB
 constexpr int GM_SC_ROWS = 4;                      // scale rows per stage at most (block 32)
 constexpr uint32_t GM_SC_BYTES = GM_SC_ROWS * GM_TN * 2;
 constexpr uint32_t GM_ONES = 0x3c003c00u;          // (1.0, 1.0) in fp16
+#ifndef GM_GROUPS_THRESHOLD
+#define GM_GROUPS_THRESHOLD 8
+#endif
+constexpr int kGroupsThreshold = GM_GROUPS_THRESHOLD; // stages per CTA up to which G = 1
 
 struct GmArgs {
   __half *y;
@@ -87,8 +91,8 @@ template <int NT> struct GmSmem {
   static constexpr uint32_t kOffA = GM_STAGES * GM_W_BYTES;
   static constexpr uint32_t kOffS = kOffA + GM_STAGES * kA;
   static constexpr uint32_t kOffRed = kOffS + GM_STAGES * GM_SC_BYTES;
-  // GM_GROUPS / 2 slots per column half for the tree reduction over the groups
-  static constexpr uint32_t kRedBytes = (GM_GROUPS / 2) * 2u * 32 * NT * 32 * 4;
+  // GM_QUADS / 2 slots per column half for the tree reduction over its warps
+  static constexpr uint32_t kRedBytes = (GM_QUADS / 2) * 2u * 32 * NT * 32 * 4;
   static constexpr uint32_t kOffBar = kOffRed + kRedBytes;
   static constexpr uint32_t kBytes = kOffBar + 2 * GM_STAGES * 8 + 16;
   static constexpr size_t kDynamic = kBytes + 1024; // alignment slack
@@ -171,7 +175,11 @@ __device__ __forceinline__ void k16_step(const uint8_t *wst, const uint8_t *ast,
   mma16816(O, GM_ONES, GM_ONES, GM_ONES, GM_ONES, B0, B1);
 }
 
-template <int NT>
+// G = stage groups: the four warps of a column half split into G groups that
+// take stages i with i % G == group, each stage's 128 rows cut into 4 / G slabs
+// (G = 1: all eight warps on every stage, 32 rows each -- lowest latency per
+// stage; G = 4: one warp pair per stage, 128 rows -- fewest epilogues).
+template <int NT, int G>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     dq_gemv_mma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
                 const __grid_constant__ CUtensorMap map_s, const GmArgs g) {
@@ -192,7 +200,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < GM_STAGES; ++i) {
       tc::mbar_init(&full[i], 1);
-      tc::mbar_init(&empty[i], 2); // the two warps of the stage's group
+      tc::mbar_init(&empty[i], 2 * (GM_QUADS / G)); // the warps that consume a stage
     }
     flags[0] = 0;
     flags[1] = 0;
@@ -239,15 +247,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   }
 
   // ------------------------------ consumers -------------------------------
-  const int wn = warp & 1, grp = warp >> 1;
+  const int wn = warp & 1, quad = warp >> 1;
+  constexpr int kSlabs = GM_QUADS / G;        // slabs per stage
+  constexpr int kSlabRows = GM_TK / kSlabs;   // rows per slab
+  const int grp = quad % G, slab = quad / G;
   const int gq = lane >> 2, t = lane & 3;
   const uint32_t mlo = g.is_signed ? 0x64086408u : 0x64006400u;
   const uint32_t mhi = g.is_signed ? 0x64806480u : 0x64006400u;
   const float blo = g.is_signed ? 1032.0f : 1024.0f;
   const float bhi = g.is_signed ? 1152.0f : 1024.0f;
-  // scale rows per stage and k16 steps per scale row
-  const int nsub = (g.block && g.block < GM_TK) ? GM_TK / g.block : 1;
-  const int ksub = 8 / nsub;
+  // scale blocks per slab and k16 steps per scale block
+  const int nsub = (g.block && g.block < kSlabRows) ? kSlabRows / g.block : 1;
+  const int ksub = (kSlabRows / 16) / nsub;
+  const int slab_row0 = slab * kSlabRows;
   const float scalar = g.srows ? 0.0f : __half2float(__ushort_as_half(__ldg(g.scalar_scale)));
   float acc[8][NT][4];
 #pragma unroll
@@ -263,8 +275,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   while (seg0 < nun) {
     const int tile = (u0 + seg0) / g.kunits;
     const int seg1 = min(nun, (tile + 1) * g.kunits - u0);
-    // this group's stages of the segment: i = seg0 .. seg1-1 with i % GROUPS == grp
-    for (int i = seg0 + ((grp - seg0 % GM_GROUPS + GM_GROUPS) % GM_GROUPS); i < seg1; i += GM_GROUPS) {
+    // this group's stages of the segment: i = seg0 .. seg1-1 with i % G == grp
+    for (int i = seg0 + ((grp - seg0 % G + G) % G); i < seg1; i += G) {
       const int s = i % GM_STAGES;
       const int kb = (u0 + i) % g.kunits;
       if (ok && flags[0]) ok = false;
@@ -278,12 +290,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const uint8_t *ast = sm + L::kOffA + s * L::kA;
         const uint8_t *sst = sm + L::kOffS + s * GM_SC_BYTES;
         for (int sub = 0; sub < nsub; ++sub) {
-          const int r0 = sub * ksub * 16;
+          const int r0 = slab_row0 + sub * ksub * 16;
           if (kb * GM_TK + r0 >= g.K) break;
+          const int srow = (g.block && g.block < GM_TK) ? r0 / g.block : 0;
           // this scale row's factors for the lane's 16 columns (odd: high nibbles, / 16)
           float se[16];
           if (g.srows) {
-            const uint4 *sp = reinterpret_cast<const uint4 *>(sst + sub * GM_TN * 2 +
+            const uint4 *sp = reinterpret_cast<const uint4 *>(sst + srow * GM_TN * 2 +
                                                               (wn * 128 + gq * 16) * 2);
             const uint4 v0 = sp[0], v1 = sp[1];
             const uint32_t w8[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
@@ -329,10 +342,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     // Sum the four groups of each column half (fixed-order tree); the warps of
     // group 0 end with the column half's sums.
 #pragma unroll
-    for (int half = GM_GROUPS / 2; half >= 1; half >>= 1) {
+    for (int half = GM_QUADS / 2; half >= 1; half >>= 1) {
       consumers_sync();
-      if (grp >= half && grp < 2 * half) {
-        float *r = red + (size_t)((grp - half) * 2 + wn) * 32 * NT * 32;
+      if (quad >= half && quad < 2 * half) {
+        float *r = red + (size_t)((quad - half) * 2 + wn) * 32 * NT * 32;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
@@ -341,8 +354,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             for (int e = 0; e < 4; ++e) r[((mt * NT + nt) * 4 + e) * 32 + lane] = acc[mt][nt][e];
       }
       consumers_sync();
-      if (grp < half) {
-        const float *r = red + (size_t)(grp * 2 + wn) * 32 * NT * 32;
+      if (quad < half) {
+        const float *r = red + (size_t)(quad * 2 + wn) * 32 * NT * 32;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
@@ -356,7 +369,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const int n0 = tile * GM_TN;
     if (cf == cl) {
       // The whole tile is this CTA's: write the output.
-      if (grp == 0 && ok) {
+      if (quad == 0 && ok) {
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
           const int col = n0 + wn * 128 + gq * 16 + 2 * mt;
@@ -375,7 +388,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     } else {
       const int slot = tile == first_tile ? 0 : 1;
       float *part = g.partials + (size_t)(b * 2 + slot) * g.M * GM_TN;
-      if (grp == 0) {
+      if (quad == 0) {
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
           const int col = wn * 128 + gq * 16 + 2 * mt;
@@ -445,7 +458,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 }
 
 struct MmaPlan {
-  int nt = 1, grid = 0, units = 0, kunits = 0, ntiles = 0, srows = 0, block = 0;
+  int nt = 1, groups = 4, grid = 0, units = 0, kunits = 0, ntiles = 0, srows = 0, block = 0;
   size_t ws = 0;
 };
 
@@ -456,6 +469,10 @@ MmaPlan mma_plan(const DqMmParams &p) {
   m.kunits = (int)((p.K + GM_TK - 1) / GM_TK);
   m.units = m.ntiles * m.kunits;
   m.grid = std::min(m.units, sm_count());
+  // Stages per CTA below about 2 per stage group leave groups idle: put all
+  // warps on every stage instead.
+  const int per_cta = (m.units + m.grid - 1) / m.grid;
+  m.groups = per_cta <= kGroupsThreshold ? 1 : 4;
   if (p.slayout == kScaleTensor) {
     m.srows = 0;
   } else if (p.slayout == kScaleAxis1) {
@@ -476,7 +493,7 @@ MmaPlan mma_plan(const DqMmParams &p) {
   return m;
 }
 
-template <int NT>
+template <int NT, int G>
 int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStream_t st) {
   CUtensorMap map_w, map_a, map_s;
   {
@@ -520,7 +537,7 @@ int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStrea
   a.srows = m.srows;
   a.is_signed = p.wdt == kInt4;
   a.scalar_scale = reinterpret_cast<const uint16_t *>(p.scale);
-  auto kern = dq_gemv_mma<NT>;
+  auto kern = dq_gemv_mma<NT, G>;
   const size_t smem = GmSmem<NT>::kDynamic;
   B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   cudaLaunchConfig_t cfg = {};
@@ -571,8 +588,12 @@ size_t dq_mma_workspace(const DqMmParams &p) { return mma_plan(p).ws; }
 int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
   const MmaPlan m = mma_plan(p);
   if (m.ws && workspace == nullptr) B2_FAIL(B2_ERR_WORKSPACE, "workspace of %zu bytes required", m.ws);
-  if (m.nt == 1) return launch_mma<1>(p, m, workspace, st);
-  return launch_mma<2>(p, m, workspace, st);
+  if (m.groups == 1) {
+    if (m.nt == 1) return launch_mma<1, 1>(p, m, workspace, st);
+    return launch_mma<2, 1>(p, m, workspace, st);
+  }
+  if (m.nt == 1) return launch_mma<1, 4>(p, m, workspace, st);
+  return launch_mma<2, 4>(p, m, workspace, st);
 }
 
 } // namespace b2
