@@ -373,6 +373,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
           const int col = n0 + wn * 128 + gq * 16 + 2 * mt;
+          if (col >= g.N) continue; // ragged last tile (N % 256 != 0); N is even
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             const int m = nt * 8 + 2 * t;
@@ -441,6 +442,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             }
           }
           const int m = e / (GM_TN / 4), col = (e % (GM_TN / 4)) * 4;
+          if (n0 + col >= g.N) continue; // ragged last tile; N % 4 == 0
           __half2 *dst = reinterpret_cast<__half2 *>(g.y + (int64_t)m * g.N + n0 + col);
           dst[0] = __floats2half2_rn(sum.x, sum.y);
           dst[1] = __floats2half2_rn(sum.z, sum.w);
@@ -465,7 +467,7 @@ struct MmaPlan {
 MmaPlan mma_plan(const DqMmParams &p) {
   MmaPlan m;
   m.nt = p.M <= 8 ? 1 : 2;
-  m.ntiles = (int)(p.N / GM_TN);
+  m.ntiles = (int)((p.N + GM_TN - 1) / GM_TN); // the last tile may be ragged (TMA zero-fills)
   m.kunits = (int)((p.K + GM_TK - 1) / GM_TK);
   m.units = m.ntiles * m.kunits;
   m.grid = std::min(m.units, sm_count());
@@ -560,12 +562,15 @@ bool dq_mma_eligible(const DqMmParams &p) {
   if (p.wdt != kInt4 && p.wdt != kUint4) return false;
   if (!p.s_f16 || p.zp != nullptr || p.ydt != kFloat16) return false;
   if (p.cast_dt != 0 && p.cast_dt != kFloat16) return false;
-  if (p.M < 1 || p.M > 16 || p.N < GM_TN || p.N % GM_TN != 0 || p.K < 16 || p.K % 8 != 0)
+  // N % 32: packed rows are whole 16-byte units (TMA strides); the last
+  // 256-column tile may be partial.
+  if (p.M < 1 || p.M > 16 || p.N < 32 || p.N % 32 != 0 || p.K < 16 || p.K % 8 != 0)
     return false;
   if (p.N > (int64_t)1 << 30 || p.K > (int64_t)1 << 30) return false;
-  if (p.N / GM_TN > (int64_t)kMaxCounters) return false;
+  const int64_t ntiles = (p.N + GM_TN - 1) / GM_TN;
+  if (ntiles > (int64_t)kMaxCounters) return false;
   // unit numbers times the grid size stay below 2^31 (32-bit index arithmetic)
-  const int64_t units = (p.N / GM_TN) * ((p.K + GM_TK - 1) / GM_TK);
+  const int64_t units = ntiles * ((p.K + GM_TK - 1) / GM_TK);
   if (units * (int64_t)(sm_count() + 1) >= ((int64_t)1 << 31)) return false;
   switch (p.slayout) {
   case kScaleTensor:

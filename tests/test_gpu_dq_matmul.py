@@ -187,7 +187,9 @@ def test_mma_decode_config3_batches(b2, cuda, M):
 
 
 @pytest.mark.parametrize("K,N", [(4096, 11008), (11008, 4096), (128, 256), (128, 76800),
-                                 (256, 1024), (4096, 1024)])
+                                 (256, 1024), (4096, 1024),
+                                 # column shards of 11008 over 2 / 4 / 8 ranks: ragged last tile
+                                 (4096, 5504), (4096, 2752), (4096, 1376), (512, 32)])
 def test_mma_decode_llama_and_edge_shapes(b2, cuda, K, N):
     for M in (1, 4):
         y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=K + N + M)
