@@ -26,6 +26,16 @@
 
 namespace b2 {
 
+// Tensor-core decode kernel (attention_decode.cu).
+bool attn_decode_eligible(int dtype, int64_t D, int64_t Sq, int64_t group, bool mask,
+                          int64_t left_window, int64_t right_window, int64_t k_sb, int64_t k_sh,
+                          int64_t k_ss, int64_t Hkv, int64_t L, bool causal, int64_t new_tokens);
+size_t attn_decode_workspace(int64_t B, int64_t Hkv);
+int attn_decode_launch(const void *q, int64_t q_sb, int64_t q_sh, const void *kc, const void *vc,
+                       int64_t kv_sh, int64_t B, int64_t Hkv, int64_t group, int64_t L, float scale,
+                       float softcap, void *y, int64_t y_sb, int64_t y_sh, void *ws,
+                       cudaStream_t st);
+
 constexpr int ATT_THREADS = 128; // 4 warps
 constexpr int ATT_ROWS = 16;     // query rows per CTA
 constexpr int ATT_TK = 32;       // keys per tile (one per lane)
@@ -385,6 +395,13 @@ __global__ void kv_copy(const T *__restrict__ src, int64_t s_sb, int64_t s_sh, i
 // Host side
 // ---------------------------------------------------------------------------
 
+// ONNXL_B200_ATTN_KERNEL=cuda forces the CUDA-core kernel where the tensor-core
+// decode kernel would run (tests compare both); returns 1 in that case.
+static int forced_attention_kernel() {
+  const char *e = getenv("ONNXL_B200_ATTN_KERNEL");
+  return (e && !strcmp(e, "cuda")) ? 1 : 0;
+}
+
 struct View { int64_t sb, sh, ss; };
 
 static View rank4_view(int64_t H, int64_t S, int64_t D) { return {H * S * D, S * D, D}; }
@@ -515,15 +532,24 @@ static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *
   splits = (L + kps - 1) / kps;
   if (splits < 1) splits = 1;
   const int64_t nrow_all = B * Hkv * rows_total;
+  View cache = {Hkv * cap * D, cap * D, D};
+  const View kv_src = have_present ? cache : kv;
+  const bool decode_tc =
+      attn_decode_eligible(q->dtype, D, Sq, group, mask != nullptr, at->left_window_size,
+                           at->right_window_size, kv_src.sb, kv_src.sh, kv_src.ss, Hkv, L,
+                           at->is_causal != 0, Sk) &&
+      vv.sb == kv.sb && vv.sh == kv.sh && vv.ss == kv.ss && B * Hkv <= (int64_t)kMaxCounters &&
+      forced_attention_kernel() != 1;
   size_t need = 0;
-  if (splits > 1)
+  if (decode_tc)
+    need = attn_decode_workspace(B, Hkv);
+  else if (splits > 1)
     need = kCounterBytes + (size_t)splits * nrow_all * (D + 2) * 4;
   int rc = workspace_check(ws, ws_bytes, need);
   if (rc < 0) return rc;
   if (rc == 1) return B2_OK;
 
   // 1) build present: copy the past unless it is already in place, append new K/V.
-  View cache = {Hkv * cap * D, cap * D, D};
   if (have_present) {
     if (past_k && !alias) {
       rc = launch_copy<T>(past_k->data, rank4_view(Hkv, P, D), pres_k->data, cache, 0, B, Hkv, P, D, st);
@@ -574,6 +600,9 @@ static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *
     B2_CUDA(cudaMemsetAsync(y->data, 0, (size_t)B * Hq * Sq * D * sizeof(T), st));
     return B2_OK;
   }
+  if (decode_tc)
+    return attn_decode_launch(q->data, qv.sb, qv.sh, p.k, p.v, kview.sh, B, Hkv, group, L,
+                              p.scale, p.softcap, y->data, yv.sb, yv.sh, ws, st);
   const int DP = (int)D + 8;
   const size_t smem = (size_t)2 * 2 * 4 * ATT_TK * DP * sizeof(T) + (size_t)rows_cta * D * 4 +
                       (size_t)4 * rows_cta * ATT_TK * 4 + (size_t)4 * rows_cta * 2 * 4 +

@@ -103,3 +103,57 @@ def test_errors(b2, cuda):
         b2.Attention()(q, k, k)
     with pytest.raises(ValueError, match="same dtype"):
         b2.Attention()(q, k.float(), k.float())
+
+
+# ---------------------------------------------------------------------------
+# Tensor-core decode kernel (FLOAT16, head 128, one new token, GQA group <= 16).
+# ---------------------------------------------------------------------------
+
+def _decode_case(b2, B, Hq, Hkv, P, seed, causal=True, softcap=0.0, cache_extra=8):
+    D = 128
+    q16 = O.f32_to_f16_bits(O.randn(seed, (B, Hq, 1, D), 0, 0.5))
+    k16 = O.f32_to_f16_bits(O.randn(seed + 1, (B, Hkv, P + 1, D), 0, 0.5))
+    v16 = O.f32_to_f16_bits(O.randn(seed + 2, (B, Hkv, P + 1, D), 0, 0.5))
+    cache = b2.KVCache(B, Hkv, P + 1 + cache_extra, D, dtype=torch.float16)
+    # garbage past the valid length must not leak into the result
+    cache.k.fill_(float("nan"))
+    cache.v.fill_(float("nan"))
+    cache.k[:, :, :P] = dev(k16[:, :, :P].copy(), O.FLOAT16)
+    cache.v[:, :, :P] = dev(v16[:, :, :P].copy(), O.FLOAT16)
+    cache.length = P
+    attrs = b2.Attributes(is_causal=causal, softcap=softcap)
+    r = b2.Attention()(dev(q16, O.FLOAT16), dev(k16[:, :, P:].copy(), O.FLOAT16),
+                       dev(v16[:, :, P:].copy(), O.FLOAT16), attrs, cache=cache)
+    torch.cuda.synchronize()
+    q, k, v = O.f16_bits_to_f32(q16), O.f16_bits_to_f32(k16), O.f16_bits_to_f32(v16)
+    ref = O.attention_f32(q, k, v, is_causal=causal, past_len=P, softcap=softcap)
+    return r.Y.float().cpu().numpy(), ref
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,P", [(32, 32, 8, 4096), (2, 16, 1, 1000), (3, 4, 4, 33),
+                                        (1, 8, 2, 0), (5, 12, 3, 31), (2, 8, 8, 700)])
+def test_decode_tensor_core_gqa(b2, cuda, B, Hq, Hkv, P):
+    y, ref = _decode_case(b2, B, Hq, Hkv, P, seed=70 + P % 7)
+    assert rel_l2(y, ref) <= 1e-3, rel_l2(y, ref)
+
+
+def test_decode_tensor_core_softcap_not_causal(b2, cuda):
+    y, ref = _decode_case(b2, 4, 8, 2, 300, seed=81, causal=False, softcap=2.0)
+    assert rel_l2(y, ref) <= 1e-3, rel_l2(y, ref)
+
+
+def test_decode_tensor_core_matches_cuda_core_kernel_and_is_deterministic(b2, cuda, monkeypatch):
+    B, Hq, Hkv, P, D = 6, 32, 8, 1500, 128
+    q = torch.randn(B, Hq, 1, D, device="cuda").half() * 0.5
+    kk = torch.randn(B, Hkv, 1, D, device="cuda").half() * 0.5
+    vv = torch.randn(B, Hkv, 1, D, device="cuda").half() * 0.5
+    pk = torch.randn(B, Hkv, P, D, device="cuda").half() * 0.5
+    pv = torch.randn(B, Hkv, P, D, device="cuda").half() * 0.5
+    attrs = b2.Attributes(is_causal=True)
+    y1 = b2.Attention()(q, kk, vv, attrs, None, pk, pv).Y.float().cpu().numpy()
+    y2 = b2.Attention()(q, kk, vv, attrs, None, pk, pv).Y.float().cpu().numpy()
+    monkeypatch.setenv("ONNXL_B200_ATTN_KERNEL", "cuda")
+    y3 = b2.Attention()(q, kk, vv, attrs, None, pk, pv).Y.float().cpu().numpy()
+    torch.cuda.synchronize()
+    assert np.array_equal(y1, y2)
+    assert rel_l2(y1, y3) <= 1e-3
