@@ -259,6 +259,69 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
       const int64_t kst = kbeg + (int64_t)kt * DT_BK; // first k of the stage
       const uint32_t s_esz = p.s_f16 ? 2u : 4u;
       const uint32_t kst_b = sst ? p.fdiv_block.div((uint32_t)kst) : 0u;
+      if constexpr (MODE == kModeI4H) {
+        // int4 x fp16 scale: the 8 nibbles of a 32-bit word become exact fp16
+        // values with 4 logic ops, 1 shift, 2 subtractions and 2 FMAs (low
+        // nibbles: 1024 + code - bias; high nibbles: (1024 + 16 code) / 16 -
+        // bias), then the correctly rounded product with the fp16 scale -- the
+        // reference's FloatToFloat16Bits((q - 0) * s).  The pairs come out as
+        // columns (0,4) (1,5) (2,6) (3,7) and are stored in that order: the
+        // MMA row of shared position p of an 8-column chunk is column
+        // (p >> 1) + 4 (p & 1), which the epilogue maps back.
+        const bool sgn = p.wdt == kInt4;
+        const uint32_t mlo = sgn ? 0x64086408u : 0x64006400u;
+        const uint32_t mhi = sgn ? 0x64806480u : 0x64006400u;
+        const uint32_t bhi = sgn ? 0xd480d480u : 0xd400d400u; // -(64 + 8) / -64
+        const int nl = cc * 8;
+        // Scale pairs (s0,s4) (s1,s5) (s2,s6) (s3,s7) of the chunk, reloaded
+        // only when the row's scale block changes.
+        int64_t cur_kb = -1;
+        uint32_t sp[4] = {0u, 0u, 0u, 0u};
+        const uint16_t *s16 = reinterpret_cast<const uint16_t *>(p.scale);
+        if (p.slayout == kScaleTensor) {
+          const uint32_t sv = s16[0];
+          sp[0] = sp[1] = sp[2] = sp[3] = sv | (sv << 16);
+        }
+        // No row guard: split ranges are whole 64-row stages, and rows past K
+        // (and columns past N) arrive from TMA as zero codes with zero staged
+        // scales, which dequantize to 0.  Branch-free, the rows interleave.
+        const bool col_ok = n0 + nl < p.N;
+#pragma unroll
+        for (int i = 0; i < DT_BK / kRowStep; ++i) {
+          const int r = r0 + kRowStep * i;
+          const int64_t k = kst + r;
+          if (p.slayout != kScaleTensor) {
+            const int64_t kb = p.slayout == kScaleAxis1 ? 0 : (int64_t)p.fdiv_block.div((uint32_t)k);
+            if (kb != cur_kb) {
+              cur_kb = kb;
+              uint4 v = make_uint4(0, 0, 0, 0);
+              if (sst) v = *reinterpret_cast<const uint4 *>(sst + (size_t)(kb - kst_b) * DT_BM * 2 + nl * 2);
+              else if (col_ok && k < p.K) v = *reinterpret_cast<const uint4 *>(s16 + kb * p.N + n0 + nl);
+              sp[0] = __byte_perm(v.x, v.z, 0x5410);
+              sp[1] = __byte_perm(v.x, v.z, 0x7632);
+              sp[2] = __byte_perm(v.y, v.w, 0x5410);
+              sp[3] = __byte_perm(v.y, v.w, 0x7632);
+            }
+          }
+          uint4 o;
+          {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(raw + r * raw_row_bytes + nl / 2);
+            const uint32_t w8 = w >> 8;
+            uint32_t q0, q1, q2, q3;
+            asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q0) : "r"((w & 0x000f000fu) ^ mlo), "r"(mlo));
+            asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(q1) : "r"((w & 0x00f000f0u) ^ mhi), "r"(0x2c002c00u), "r"(bhi));
+            asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q2) : "r"((w8 & 0x000f000fu) ^ mlo), "r"(mlo));
+            asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(q3) : "r"((w8 & 0x00f000f0u) ^ mhi), "r"(0x2c002c00u), "r"(bhi));
+            asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o.x) : "r"(q0), "r"(sp[0]));
+            asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o.y) : "r"(q1), "r"(sp[1]));
+            asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o.z) : "r"(q2), "r"(sp[2]));
+            asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o.w) : "r"(q3), "r"(sp[3]));
+          }
+          const int blk = nl >> 6, chunk = (nl & 63) >> 3;
+          uint8_t *dst = st + blk * 8192 + r * 128 + ((chunk ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4 *>(dst) = o;
+        }
+      } else {
 #pragma unroll 2
       for (int i = 0; i < DT_BK / kRowStep; ++i) {
         const int r = r0 + kRowStep * i; // k row within the stage
@@ -274,6 +337,7 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
         uint8_t *dst = st + blk * 8192 + r * 128 + ((chunk ^ (r & 7)) << 4);
         *reinterpret_cast<uint4 *>(dst) = o;
       }
+      }
       tc::fence_proxy_async();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&deq[s]);
@@ -284,7 +348,10 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
       const bool ok = tc::mbar_wait(done, 0, 4000000000ull);
       if (!ok) atomicExch(args.status, tc::kTimeoutMma);
       tc::tc_fence_after();
-      const int64_t n = n0 + g * 32 + lane;
+      // MMA row -> weight column (the int4 path stores each 8-column chunk
+      // in the order 0 4 1 5 2 6 3 7)
+      const int pos = g * 32 + lane;
+      const int64_t n = n0 + (MODE == kModeI4H ? (pos & ~7) + (pos & 7) / 2 + (pos & 1) * 4 : pos);
       if (ok && !abort_flag) {
         float *part = p.ksplit > 1 ? p.partials + (int64_t)split * p.M * p.N : nullptr;
         for (int ch = 0; ch < args.bn / 32 + ((args.bn & 31) ? 1 : 0); ++ch) {

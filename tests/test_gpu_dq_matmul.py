@@ -140,6 +140,18 @@ def test_tensor_core_int4_fp16(b2, cuda, monkeypatch, M):
     assert rel_l2(y, ref) <= TOL[O.FLOAT16]
 
 
+@pytest.mark.parametrize("wdt,axis,block,K,N", [
+    (O.INT4, 1, None, 512, 200),    # per-column fp16 scales, N not a multiple of 128
+    (O.UINT4, 0, 96, 384, 256),     # blocks that do not divide the 64-row stage
+    (O.INT4, 0, 32, 256, 136),      # two scale blocks per stage
+])
+def test_tensor_core_int4_scale_layouts(b2, cuda, monkeypatch, wdt, axis, block, K, N):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "tc")
+    for M in (5, 40):
+        y, ref = run_case(b2, M, K, N, wdt, O.FLOAT16, O.FLOAT16, axis=axis, block=block, seed=M + 9)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
 def test_tensor_core_config3_shape_batch32(b2, cuda, monkeypatch):
     monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "tc")
     y, ref = run_case(b2, 32, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=11)
