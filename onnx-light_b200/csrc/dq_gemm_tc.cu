@@ -31,7 +31,10 @@ constexpr int DT_PROD_WARPS = 8; // dequantizing warps (2 .. 9)
 constexpr int DT_THREADS = 64 + DT_PROD_WARPS * 32;
 constexpr uint32_t DT_AOP_BYTES = DT_BM * DT_BK * 2; // 16 KB dequantized operand
 
-enum DqMode : int { kModeI4H = 0, kModeF8 = 1, kModeF4 = 2, kModeGeneric = 3 };
+// kModePre: the weight was dequantized (and cast) once into a 16-bit operand
+// [K, N] in the workspace (large M: every weight tile is used by many
+// activation tiles), and both operands stream in by TMA.
+enum DqMode : int { kModeI4H = 0, kModeF8 = 1, kModeF4 = 2, kModeGeneric = 3, kModePre = 4 };
 
 struct DqTcArgs {
   DqMmParams p;
@@ -201,6 +204,15 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
         }
         uint8_t *st = smem + (size_t)s * args.stage_bytes;
         const int32_t k = (int32_t)(kbeg + (int64_t)kt * DT_BK);
+        if constexpr (MODE == kModePre) {
+          // operand tile [64 k][128 n] as two 64-column boxes with the 128-byte
+          // swizzle: exactly the MN-major layout the dequantizing warps write
+          tc::mbar_expect_tx(&full[s], DT_AOP_BYTES + args.b_bytes);
+          tc::tma_load_2d(st, &map_w, &full[s], (int32_t)n0, k);
+          tc::tma_load_2d(st + 8192, &map_w, &full[s], (int32_t)n0 + 64, k);
+          tc::tma_load_2d(st + DT_AOP_BYTES, &map_a, &full[s], k, (int32_t)m0);
+          continue;
+        }
         const bool raw_tma = MODE != kModeGeneric;
         tc::mbar_expect_tx(&full[s], (raw_tma ? args.raw_bytes : 0u) + args.b_bytes + args.s_bytes);
         tc::tma_load_2d(st + DT_AOP_BYTES, &map_a, &full[s], k, (int32_t)m0);
@@ -219,7 +231,7 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
       const uint32_t id = tc::idesc(1, args.op_bf16, args.op_bf16, 1, 0, DT_BM, (uint32_t)args.bn);
       for (int kt = 0; kt < kt_count; ++kt) {
         const int s = kt % S;
-        if (!tc::mbar_wait(&deq[s], (kt / S) & 1)) {
+        if (!tc::mbar_wait(MODE == kModePre ? &full[s] : &deq[s], (kt / S) & 1)) {
           atomicExch(args.status, tc::kTimeoutFull);
           abort_flag = 1;
           break;
@@ -246,7 +258,7 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
     const int cc = t & 15;   // 8-column chunk (n_local = cc * 8)
     const int r0 = t >> 4;   // first k row, rows r0 + kRowStep i
     const uint32_t raw_row_bytes = MODE == kModeF8 ? 128 : 64;
-    for (int kt = 0; kt < kt_count && !abort_flag; ++kt) {
+    for (int kt = 0; kt < (MODE == kModePre ? 0 : kt_count) && !abort_flag; ++kt) {
       const int s = kt % S;
       if (!tc::mbar_wait(&full[s], (kt / S) & 1)) {
         atomicExch(args.status, tc::kTimeoutFull);
@@ -397,6 +409,23 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
   }
 }
 
+// The 16-bit MMA operand of the whole weight: w16[k][n] = the reference's
+// DequantizeLinear value rounded to its output type and to the Cast type,
+// exactly as the dequantizing warps form it (8 columns per thread).
+template <int MODE>
+__global__ void __launch_bounds__(256) dq_operand_kernel(const DqTcArgs args, uint16_t *w16) {
+  const DqMmParams &p = args.p;
+  const int64_t groups = p.N / 8;
+  const int64_t total = p.K * groups;
+  const int64_t row_bytes = MODE == kModeF8 ? p.N : p.N / 2;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = e / groups, n = (e % groups) * 8;
+    const uint4 o = dequant8<MODE>(args, p.w + k * row_bytes, (int)n, k, n, nullptr);
+    *reinterpret_cast<uint4 *>(w16 + k * p.N + n) = o;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -414,12 +443,15 @@ static int dq_tc_mode(const DqMmParams &p) {
 
 struct TcPlan {
   int bn = 0, stages = 0, ksplit = 1, mode = 0, s_rows = 0;
+  int pre = 0; // 1: dequantize the weight once into the workspace (kModePre)
   uint32_t s_bytes = 0;
   int64_t kchunk = 0;
   uint32_t raw_bytes = 0, b_bytes = 0, stage_bytes = 0;
   size_t smem = 0;
   dim3 grid;
 };
+
+constexpr int64_t kPreM = 2048; // rows of activations from which the weight is dequantized once
 
 static TcPlan tc_plan(const DqMmParams &p) {
   TcPlan t;
@@ -429,13 +461,17 @@ static TcPlan tc_plan(const DqMmParams &p) {
   t.raw_bytes = (t.mode == kModeF8 ? 128u : 64u) * DT_BK;
   if (t.mode == kModeGeneric) t.raw_bytes = 64u * DT_BK; // raw tile unused, keep the ring uniform
   t.b_bytes = (uint32_t)t.bn * 128u;
+  // Large M: each weight tile feeds M / 256 activation tiles, so dequantizing
+  // it per tile would repeat the work that many times; form the operand once.
+  t.pre = p.M >= kPreM && p.N % 8 == 0 && p.N >= 64 ? 1 : 0;
+  if (t.pre) t.raw_bytes = 0;
   // Blocked-along-K scales are staged per stage by TMA: ceil(64 / block) rows
   // of 128 columns (the stage start is block-aligned when block >= 64).
   const uint32_t s_esz = p.s_f16 ? 2u : 4u;
   const bool s_ok = p.slayout == kScaleAxis0Block && t.mode != kModeGeneric &&
                     (p.block % DT_BK == 0 || DT_BK % p.block == 0) &&
                     ((uint64_t)p.N * s_esz) % 16 == 0;
-  t.s_rows = s_ok ? (p.block >= DT_BK ? 1 : (int)(DT_BK / p.block)) : 0;
+  t.s_rows = s_ok && !t.pre ? (p.block >= DT_BK ? 1 : (int)(DT_BK / p.block)) : 0;
   t.s_bytes = (uint32_t)t.s_rows * DT_BM * s_esz;
   t.stage_bytes = DT_AOP_BYTES + t.b_bytes + t.raw_bytes + t.s_bytes;
   t.stage_bytes = (t.stage_bytes + 1023) & ~1023u;
@@ -466,6 +502,8 @@ bool dq_tc_eligible(const DqMmParams &p) {
   if (p.ydt != kFloat16 && p.ydt != kBfloat16) return false;
   // TMA: activation rows K * 2 bytes and packed weight rows must be 16-byte multiples.
   if ((p.K * 2) % 16 != 0) return false;
+  // Large M reads the weight through the dequantized 16-bit operand only.
+  if (p.M >= kPreM && p.N % 8 == 0 && p.N >= 64 && p.K >= DT_BK) return true;
   const int mode = dq_tc_mode(p);
   const int64_t wrow = mode == kModeF8 ? p.N : p.N / 2;
   if (mode != kModeGeneric && ((wrow % 16) != 0 || (p.N % 2) != 0)) return false;
@@ -477,6 +515,7 @@ bool dq_tc_eligible(const DqMmParams &p) {
 size_t dq_tc_workspace(const DqMmParams &p) {
   const TcPlan t = tc_plan(p);
   size_t ws = kCounterBytes;
+  if (t.pre) ws += ((size_t)p.K * p.N * 2 + 1023) & ~(size_t)1023; // 16-bit operand
   if (t.ksplit > 1) ws += (size_t)t.ksplit * p.M * p.N * 4;
   return ws;
 }
@@ -489,9 +528,11 @@ int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st) {
   a.p.ksplit = t.ksplit;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   a.status = reinterpret_cast<int *>(ws + kStatusOffset);
+  uint16_t *w16 = t.pre ? reinterpret_cast<uint16_t *>(ws + kCounterBytes) : nullptr;
+  const size_t pre_bytes = t.pre ? (((size_t)pin.K * pin.N * 2 + 1023) & ~(size_t)1023) : 0;
   if (t.ksplit > 1) {
     a.p.counters = reinterpret_cast<uint32_t *>(ws);
-    a.p.partials = reinterpret_cast<float *>(ws + kCounterBytes);
+    a.p.partials = reinterpret_cast<float *>(ws + kCounterBytes + pre_bytes);
   }
   a.bn = t.bn;
   a.stages = t.stages;
@@ -529,8 +570,9 @@ int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st) {
     const uint64_t dims[2] = {row, (uint64_t)pin.K};
     const uint64_t strides[1] = {row};
     const uint32_t box[2] = {is8 ? 128u : 64u, (uint32_t)DT_BK};
-    if (t.mode == kModeGeneric) {
-      // the generic path reads weights with plain loads; the map is not used
+    if (t.mode == kModeGeneric || t.pre) {
+      // the generic path reads weights with plain loads; the pre path builds
+      // its own map over the operand
       map_w = map_a;
     } else {
       int rc = make_tensor_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, pin.w, dims, strides, box,
@@ -539,6 +581,32 @@ int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st) {
     }
   }
   if (!t.s_bytes) map_s = map_a; // unused
+  if (t.pre) {
+    // 1) the operand, once
+    const int64_t groups = pin.K * (pin.N / 8);
+    const unsigned blocks = (unsigned)std::min<int64_t>((groups + 255) / 256, (int64_t)sm_count() * 16);
+    auto op_kern = t.mode == kModeI4H ? dq_operand_kernel<kModeI4H>
+                   : t.mode == kModeF8 ? dq_operand_kernel<kModeF8>
+                   : t.mode == kModeF4 ? dq_operand_kernel<kModeF4>
+                                       : dq_operand_kernel<kModeGeneric>;
+    op_kern<<<blocks, 256, 0, st>>>(a, w16);
+    B2_LAUNCH_CHECK();
+    // 2) the GEMM on it: [K, N] 16-bit, boxes of 64 n x 64 k with the 128-byte swizzle
+    const uint64_t dims[2] = {(uint64_t)pin.N, (uint64_t)pin.K};
+    const uint64_t strides[1] = {(uint64_t)pin.N * 2};
+    const uint32_t box[2] = {64, (uint32_t)DT_BK};
+    int rc = make_tensor_map(&map_w, a.op_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                             2, w16, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    a.mode = kModePre;
+    a.raw_bytes = 0;
+    a.s_bytes = 0;
+    auto kern = dq_gemm_tc_kernel<kModePre>;
+    B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)t.smem));
+    kern<<<t.grid, DT_THREADS, t.smem, st>>>(map_w, map_a, map_a, a);
+    B2_LAUNCH_CHECK();
+    return B2_OK;
+  }
   auto kern = t.mode == kModeI4H ? dq_gemm_tc_kernel<kModeI4H>
               : t.mode == kModeF8  ? dq_gemm_tc_kernel<kModeF8>
               : t.mode == kModeF4  ? dq_gemm_tc_kernel<kModeF4>

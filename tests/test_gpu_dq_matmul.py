@@ -242,3 +242,20 @@ def test_mma_decode_unaligned_activations_fall_back(b2, cuda):
     y_al = b2.DequantizeMatMul()(a[1:].clone().view(M, K), tw, s, None, axis=0)
     torch.cuda.synchronize()
     assert rel_l2(y_off.float().cpu().numpy(), y_al.float().cpu().numpy()) <= TOL[O.FLOAT16]
+
+
+# ---------------------------------------------------------------------------
+# Large M (prefill): the weight is dequantized once into the workspace and the
+# tcgen05 GEMM streams both operands by TMA.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("wdt,s_dt,act,block,zp,cast", [
+    (O.F8E4M3FN, O.FLOAT, O.BFLOAT16, 32, False, O.BFLOAT16),
+    (O.F4E2M1, O.FLOAT, O.BFLOAT16, 32, False, O.BFLOAT16),
+    (O.INT4, O.FLOAT16, O.FLOAT16, 64, False, 0),
+    (O.UINT8, O.FLOAT16, O.FLOAT16, 32, True, 0),
+])
+def test_prefill_predequantized_gemm(b2, cuda, wdt, s_dt, act, block, zp, cast):
+    y, ref = run_case(b2, 2304, 320, 200, wdt, s_dt, act, axis=0, block=block, zp=zp, cast=cast,
+                      seed=17)
+    assert rel_l2(y, ref) <= TOL[act], rel_l2(y, ref)
