@@ -31,6 +31,13 @@ bool attn_decode_eligible(int dtype, int64_t D, int64_t Sq, int64_t group, bool 
                           int64_t left_window, int64_t right_window, int64_t k_sb, int64_t k_sh,
                           int64_t k_ss, int64_t Hkv, int64_t L, bool causal, int64_t new_tokens);
 size_t attn_decode_workspace(int64_t B, int64_t Hkv);
+// Tensor-core prefill kernel (attention_prefill.cu).
+bool attn_prefill_eligible(int dtype, int64_t D, int64_t Sq, bool mask, int64_t left_window,
+                           int64_t right_window, int64_t k_ss, int64_t L);
+int attn_prefill_launch(int dtype, const void *q, const int64_t *qs, const void *kc,
+                        const void *vc, const int64_t *ks, void *y, const int64_t *ys, int64_t B,
+                        int64_t Hq, int64_t Hkv, int64_t Sq, int64_t L, int64_t past, float scale,
+                        float softcap, int causal, cudaStream_t st);
 int attn_decode_launch(const void *q, int64_t q_sb, int64_t q_sh, const void *kc, const void *vc,
                        int64_t kv_sh, int64_t B, int64_t Hkv, int64_t group, int64_t L, float scale,
                        float softcap, void *y, int64_t y_sb, int64_t y_sh, void *ws,
@@ -540,8 +547,20 @@ static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *
                            at->is_causal != 0, Sk) &&
       vv.sb == kv.sb && vv.sh == kv.sh && vv.ss == kv.ss && B * Hkv <= (int64_t)kMaxCounters &&
       forced_attention_kernel() != 1;
+  const bool prefill_tc =
+      !decode_tc &&
+      attn_prefill_eligible(q->dtype, D, Sq, mask != nullptr, at->left_window_size,
+                            at->right_window_size, kv_src.ss, L) &&
+      vv.sb == kv.sb && vv.sh == kv.sh && vv.ss == kv.ss && forced_attention_kernel() != 1 &&
+      kv_src.sb % 8 == 0 && kv_src.sh % 8 == 0 && qv.sb % 2 == 0 && qv.sh % 2 == 0 &&
+      qv.ss % 2 == 0 && yv.sb % 2 == 0 && yv.sh % 2 == 0 && yv.ss % 2 == 0 &&
+      ((reinterpret_cast<uintptr_t>(q->data) | reinterpret_cast<uintptr_t>(y->data)) & 3) == 0 &&
+      ((reinterpret_cast<uintptr_t>(have_present ? pres_k->data : k->data) |
+        reinterpret_cast<uintptr_t>(have_present ? pres_v->data : v->data)) & 15) == 0;
   size_t need = 0;
-  if (decode_tc)
+  if (prefill_tc)
+    need = 0;
+  else if (decode_tc)
     need = attn_decode_workspace(B, Hkv);
   else if (splits > 1)
     need = kCounterBytes + (size_t)splits * nrow_all * (D + 2) * 4;
@@ -599,6 +618,12 @@ static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *
     // No keys: every row is fully masked and the reference writes zeros.
     B2_CUDA(cudaMemsetAsync(y->data, 0, (size_t)B * Hq * Sq * D * sizeof(T), st));
     return B2_OK;
+  }
+  if (prefill_tc) {
+    const int64_t qs[3] = {qv.sb, qv.sh, qv.ss}, ys[3] = {yv.sb, yv.sh, yv.ss};
+    const int64_t ks[3] = {kview.sb, kview.sh, kview.ss};
+    return attn_prefill_launch(q->dtype, q->data, qs, p.k, p.v, ks, y->data, ys, B, Hq, Hkv, Sq,
+                               L, P, p.scale, p.softcap, p.causal, st);
   }
   if (decode_tc)
     return attn_decode_launch(q->data, qv.sb, qv.sh, p.k, p.v, kview.sh, B, Hkv, group, L,

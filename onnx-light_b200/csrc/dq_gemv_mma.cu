@@ -61,7 +61,13 @@ namespace {
 
 constexpr int GM_TN = 256;                         // columns per tile (128 packed bytes / row)
 constexpr int GM_TK = 128;                         // weight rows per stage
-constexpr int GM_STAGES = 8;                       // ring depth
+#ifndef GM_RING
+#define GM_RING 8
+#endif
+#ifndef GM_CTAS_PER_SM
+#define GM_CTAS_PER_SM 1
+#endif
+constexpr int GM_STAGES = GM_RING;                 // ring depth
 constexpr int GM_QUADS = 4;                        // consumer warps per column half
 constexpr int GM_CONSUMERS = 2 * GM_QUADS;         // consumer warps
 constexpr int GM_THREADS = (GM_CONSUMERS + 1) * 32;
@@ -180,7 +186,7 @@ __device__ __forceinline__ void k16_step(const uint8_t *wst, const uint8_t *ast,
 // (G = 1: all eight warps on every stage, 32 rows each -- lowest latency per
 // stage; G = 4: one warp pair per stage, 128 rows -- fewest epilogues).
 template <int NT, int G>
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     dq_gemv_mma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
                 const __grid_constant__ CUtensorMap map_s, const GmArgs g) {
   using L = GmSmem<NT>;
@@ -470,7 +476,7 @@ MmaPlan mma_plan(const DqMmParams &p) {
   m.ntiles = (int)((p.N + GM_TN - 1) / GM_TN); // the last tile may be ragged (TMA zero-fills)
   m.kunits = (int)((p.K + GM_TK - 1) / GM_TK);
   m.units = m.ntiles * m.kunits;
-  m.grid = std::min(m.units, sm_count());
+  m.grid = std::min(m.units, sm_count() * GM_CTAS_PER_SM);
   // Stages per CTA below about 2 per stage group leave groups idle: put all
   // warps on every stage instead.
   const int per_cta = (m.units + m.grid - 1) / m.grid;

@@ -157,3 +157,90 @@ def test_decode_tensor_core_matches_cuda_core_kernel_and_is_deterministic(b2, cu
     torch.cuda.synchronize()
     assert np.array_equal(y1, y2)
     assert rel_l2(y1, y3) <= 1e-3
+
+
+# ---------------------------------------------------------------------------
+# Tensor-core prefill kernel (FLOAT16 / BFLOAT16, head 128, Sq >= 2, no mask).
+# ---------------------------------------------------------------------------
+
+def _prefill_case(b2, dt, B, Hq, Hkv, S, P, causal, rank3, softcap=0.0, seed=90):
+    D = 128
+    enc = O.f32_to_f16_bits if dt == O.FLOAT16 else O.f32_to_bf16_bits
+    q16 = enc(O.randn(seed, (B, Hq, S, D), 0, 0.5))
+    k16 = enc(O.randn(seed + 1, (B, Hkv, P + S, D), 0, 0.5))
+    v16 = enc(O.randn(seed + 2, (B, Hkv, P + S, D), 0, 0.5))
+    attrs = b2.Attributes(is_causal=causal, softcap=softcap, q_num_heads=Hq, kv_num_heads=Hkv)
+    if rank3:
+        def r3(x):
+            return np.ascontiguousarray(x.transpose(0, 2, 1, 3).reshape(B, x.shape[2], -1))
+        qd, kd, vd = dev(r3(q16), dt), dev(r3(k16[:, :, P:]), dt), dev(r3(v16[:, :, P:]), dt)
+    else:
+        qd, kd, vd = dev(q16, dt), dev(k16[:, :, P:].copy(), dt), dev(v16[:, :, P:].copy(), dt)
+    pk = dev(k16[:, :, :P].copy(), dt) if P else None
+    pv = dev(v16[:, :, :P].copy(), dt) if P else None
+    r = b2.Attention()(qd, kd, vd, attrs, None, pk, pv)
+    torch.cuda.synchronize()
+    y = r.Y.float().cpu().numpy()
+    if rank3:
+        y = y.reshape(B, S, Hq, D).transpose(0, 2, 1, 3)
+    ref = O.attention_f32(UP[dt](q16), UP[dt](k16), UP[dt](v16), is_causal=causal, past_len=P,
+                          softcap=softcap)
+    return y, ref
+
+
+PREFILL_TOL = {O.FLOAT16: 1e-3, O.BFLOAT16: 4e-3}  # bf16: output and P rounding (2^-8)
+
+
+@pytest.mark.parametrize("dt,B,Hq,Hkv,S,P,causal,rank3", [
+    (O.FLOAT16, 2, 8, 2, 130, 0, True, False),
+    (O.BFLOAT16, 1, 4, 4, 64, 0, True, True),
+    (O.FLOAT16, 2, 16, 4, 77, 100, True, False),
+    (O.BFLOAT16, 1, 8, 1, 200, 0, False, False),
+    (O.FLOAT16, 3, 4, 2, 2, 300, True, False),
+    (O.BFLOAT16, 1, 32, 8, 1024, 0, True, True),
+    (O.FLOAT16, 1, 8, 8, 65, 63, False, True),
+])
+def test_prefill_tensor_core(b2, cuda, dt, B, Hq, Hkv, S, P, causal, rank3):
+    y, ref = _prefill_case(b2, dt, B, Hq, Hkv, S, P, causal, rank3, seed=90 + S % 11)
+    assert rel_l2(y, ref) <= PREFILL_TOL[dt], rel_l2(y, ref)
+
+
+def test_prefill_tensor_core_softcap(b2, cuda):
+    y, ref = _prefill_case(b2, O.FLOAT16, 2, 4, 2, 96, 40, True, False, softcap=3.0, seed=97)
+    assert rel_l2(y, ref) <= 1e-3, rel_l2(y, ref)
+
+
+def test_prefill_tensor_core_kv_cache(b2, cuda):
+    """Prefill through a KV cache whose rows past the valid length hold NaN."""
+    B, Hq, Hkv, S, P, D = 2, 8, 2, 150, 70, 128
+    q16 = O.f32_to_f16_bits(O.randn(101, (B, Hq, S, D), 0, 0.5))
+    k16 = O.f32_to_f16_bits(O.randn(102, (B, Hkv, P + S, D), 0, 0.5))
+    v16 = O.f32_to_f16_bits(O.randn(103, (B, Hkv, P + S, D), 0, 0.5))
+    cache = b2.KVCache(B, Hkv, P + S + 40, D, dtype=torch.float16)
+    cache.k.fill_(float("nan"))
+    cache.v.fill_(float("nan"))
+    cache.k[:, :, :P] = dev(k16[:, :, :P].copy(), O.FLOAT16)
+    cache.v[:, :, :P] = dev(v16[:, :, :P].copy(), O.FLOAT16)
+    cache.length = P
+    r = b2.Attention()(dev(q16, O.FLOAT16), dev(k16[:, :, P:].copy(), O.FLOAT16),
+                       dev(v16[:, :, P:].copy(), O.FLOAT16), b2.Attributes(is_causal=True),
+                       cache=cache)
+    torch.cuda.synchronize()
+    ref = oracle_attention(q16, k16, v16, True, P)
+    assert rel_l2(r.Y.float().cpu().numpy(), ref) <= 1e-3
+    assert cache.length == P + S
+
+
+def test_prefill_tensor_core_matches_cuda_core_kernel_and_is_deterministic(b2, cuda, monkeypatch):
+    B, Hq, Hkv, S, D = 2, 16, 4, 300, 128
+    q = torch.randn(B, Hq, S, D, device="cuda").bfloat16() * 0.5
+    kk = torch.randn(B, Hkv, S, D, device="cuda").bfloat16() * 0.5
+    vv = torch.randn(B, Hkv, S, D, device="cuda").bfloat16() * 0.5
+    attrs = b2.Attributes(is_causal=True)
+    y1 = b2.Attention()(q, kk, vv, attrs).Y.float().cpu().numpy()
+    y2 = b2.Attention()(q, kk, vv, attrs).Y.float().cpu().numpy()
+    monkeypatch.setenv("ONNXL_B200_ATTN_KERNEL", "cuda")
+    y3 = b2.Attention()(q, kk, vv, attrs).Y.float().cpu().numpy()
+    torch.cuda.synchronize()
+    assert np.array_equal(y1, y2)
+    assert rel_l2(y1, y3) <= 4e-3
