@@ -136,25 +136,30 @@ __device__ __forceinline__ int cta_of(int u, int U, int G) {
   return (int)(((uint32_t)(u + 1) * (uint32_t)G - 1u) / (uint32_t)U);
 }
 
+// Column (within the warp's 128-column half) of lane row g of m-tile mt;
+// lane row g + 8 holds the next column.  m-tile mt = 2 * chunk + h covers
+// columns 32 * chunk + 4 g + 2 h and + 1 for g = 0..7.
+__device__ __forceinline__ int mt_col(int mt, int g) { return (mt >> 1) * 32 + 4 * g + 2 * (mt & 1); }
+
+__device__ __forceinline__ void ldsm_t4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
 // One k16 step of one consumer warp: rows r0 .. r0+15 of the stage, the 128
-// columns of column half `wn`.  Lane (g, t) holds packed columns
-// c0 = wn*128 + g*16 .. c0+15 of rows r0+2t, r0+2t+1, r0+2t+8, r0+2t+9; m-tile
-// mt of the MMA takes columns c0+2mt (row g: the low nibble of byte mt) and
-// c0+2mt+1 (row g+8: the high nibble), so the byte holding both nibbles feeds
-// one A fragment directly.  D accumulates sum a * magic and O sum a (ones row)
-// for activation rows nt*8 .. nt*8+7.
+// columns (four 16-byte chunks) of column half `wn`.  A transposing ldmatrix
+// of 16-bit elements hands lane (g, t) the 4 columns 32c + 4g .. +3 of rows
+// r0 + 2t and r0 + 2t + 1 (row block 0) or + 8 (row block 1) packed in one
+// register, low half the first row -- the row pair an MMA A register holds.
+// Nibbles 0 and 1 of each half become exact fp16 magic numbers with one logic
+// operation each (1024 + code, 1024 + 16 code); nibbles 2 and 3 after a shift
+// by 8.  D accumulates sum a * magic and O sum a (ones row) for activation
+// rows nt*8 .. nt*8+7.
 template <int NT>
 __device__ __forceinline__ void k16_step(const uint8_t *wst, const uint8_t *ast, int r0, int wn,
-                                         int g, int t, int nt, uint32_t mlo, uint32_t mhi,
-                                         float (&D)[8][4], float (&O)[4]) {
-  const int cb = wn * 64 + g * 8; // logical byte of the lane's 16 columns in a 128-byte row
-  uint2 R[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int rr = r0 + 2 * t + (q & 1) + ((q >> 1) << 3);
-    R[q] = *reinterpret_cast<const uint2 *>(wst + rr * 128 +
-                                            ((((cb >> 4) ^ (rr & 7)) << 4) | (cb & 15)));
-  }
+                                         int lane, int g, int t, int nt, uint32_t mlo,
+                                         uint32_t mhi, float (&D)[8][4], float (&O)[4]) {
   uint32_t B0, B1;
   {
     const int kb = ((r0 & 63) + 2 * t) * 2; // byte within the 64-column activation box
@@ -165,18 +170,26 @@ __device__ __forceinline__ void k16_step(const uint8_t *wst, const uint8_t *ast,
     const int kb2 = kb + 16;
     B1 = *reinterpret_cast<const uint32_t *>(rb + ((((kb2 >> 4) ^ (row & 7)) << 4) | (kb2 & 15)));
   }
+  // ldmatrix source rows: lanes 8i .. 8i+7 address matrix i = (row block
+  // i & 1, chunk i >> 1 of the pair); 128-byte swizzle of the TMA box.
+  const int mi = lane >> 3;
+  const int row = r0 + (mi & 1) * 8 + (lane & 7);
+  const uint32_t rbase = tc::smem_u32(wst + row * 128);
 #pragma unroll
-  for (int mt = 0; mt < 8; ++mt) {
-    const int jb = mt & 3;
-    const uint32_t sel = jb | (jb << 4) | ((jb + 4) << 8) | ((jb + 4) << 12);
-    const uint32_t x01 = (mt >> 2) ? R[0].y : R[0].x, y01 = (mt >> 2) ? R[1].y : R[1].x;
-    const uint32_t x89 = (mt >> 2) ? R[2].y : R[2].x, y89 = (mt >> 2) ? R[3].y : R[3].x;
-    // Byte jb of row k in the low half-word, of row k+1 in the high one.
-    const uint32_t v01 = __byte_perm(x01, y01, sel);
-    const uint32_t v89 = __byte_perm(x89, y89, sel);
-    const uint32_t a0 = (v01 & 0x000f000fu) ^ mlo, a1 = (v01 & 0x00f000f0u) ^ mhi;
-    const uint32_t a2 = (v89 & 0x000f000fu) ^ mlo, a3 = (v89 & 0x00f000f0u) ^ mhi;
-    mma16816(D[mt], a0, a1, a2, a3, B0, B1);
+  for (int pair = 0; pair < 2; ++pair) {
+    const int lch = wn * 4 + pair * 2 + (mi >> 1);
+    uint32_t r[4];
+    ldsm_t4(rbase + ((lch ^ (row & 7)) << 4), r);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint32_t x = r[2 * c], y = r[2 * c + 1]; // row blocks 0 and 1
+      const int mt = (pair * 2 + c) * 2;
+      mma16816(D[mt], (x & 0x000f000fu) ^ mlo, (x & 0x00f000f0u) ^ mhi, (y & 0x000f000fu) ^ mlo,
+               (y & 0x00f000f0u) ^ mhi, B0, B1);
+      const uint32_t xs = x >> 8, ys = y >> 8;
+      mma16816(D[mt + 1], (xs & 0x000f000fu) ^ mlo, (xs & 0x00f000f0u) ^ mhi,
+               (ys & 0x000f000fu) ^ mlo, (ys & 0x00f000f0u) ^ mhi, B0, B1);
+    }
   }
   mma16816(O, GM_ONES, GM_ONES, GM_ONES, GM_ONES, B0, B1);
 }
@@ -185,7 +198,9 @@ __device__ __forceinline__ void k16_step(const uint8_t *wst, const uint8_t *ast,
 // take stages i with i % G == group, each stage's 128 rows cut into 4 / G slabs
 // (G = 1: all eight warps on every stage, 32 rows each -- lowest latency per
 // stage; G = 4: one warp pair per stage, 128 rows -- fewest epilogues).
-template <int NT, int G>
+// KS = k16 steps per scale block inside a slab (the slab's rows / 16 when the
+// block is at least a slab), fixed at compile time so the steps unroll.
+template <int NT, int G, int KS>
 __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     dq_gemv_mma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
                 const __grid_constant__ CUtensorMap map_s, const GmArgs g) {
@@ -263,8 +278,8 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
   const float blo = g.is_signed ? 1032.0f : 1024.0f;
   const float bhi = g.is_signed ? 1152.0f : 1024.0f;
   // scale blocks per slab and k16 steps per scale block
-  const int nsub = (g.block && g.block < kSlabRows) ? kSlabRows / g.block : 1;
-  const int ksub = (kSlabRows / 16) / nsub;
+  constexpr int kSubs = (kSlabRows / 16) / KS;  // scale blocks per slab
+  static_assert(kSubs * KS * 16 == kSlabRows, "slab rows");
   const int slab_row0 = slab * kSlabRows;
   const float scalar = g.srows ? 0.0f : __half2float(__ushort_as_half(__ldg(g.scalar_scale)));
   float acc[8][NT][4];
@@ -295,26 +310,15 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
         const uint8_t *wst = sm + s * GM_W_BYTES;
         const uint8_t *ast = sm + L::kOffA + s * L::kA;
         const uint8_t *sst = sm + L::kOffS + s * GM_SC_BYTES;
-        for (int sub = 0; sub < nsub; ++sub) {
-          const int r0 = slab_row0 + sub * ksub * 16;
-          if (kb * GM_TK + r0 >= g.K) break;
+        // Rows past K read as zeros in every operand (TMA fill), so a
+        // ragged last stage needs no bounds.
+#pragma unroll
+        for (int sub = 0; sub < kSubs; ++sub) {
+          const int r0 = slab_row0 + sub * KS * 16;
           const int srow = (g.block && g.block < GM_TK) ? r0 / g.block : 0;
-          // this scale row's factors for the lane's 16 columns (odd: high nibbles, / 16)
-          float se[16];
-          if (g.srows) {
-            const uint4 *sp = reinterpret_cast<const uint4 *>(sst + srow * GM_TN * 2 +
-                                                              (wn * 128 + gq * 16) * 2);
-            const uint4 v0 = sp[0], v1 = sp[1];
-            const uint32_t w8[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              se[2 * j] = __half2float(__ushort_as_half((uint16_t)(w8[j] & 0xffffu)));
-              se[2 * j + 1] = __half2float(__ushort_as_half((uint16_t)(w8[j] >> 16))) * 0.0625f;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) se[j] = (j & 1) ? scalar * 0.0625f : scalar;
-          }
+          // this scale row's factors are read after the k16 steps, so they
+          // hold no registers during them
+          const uint8_t *srow_p = sst + srow * GM_TN * 2 + wn * 256;
           // Rows 8..15 of the activations (M > 8) take a second pass over the
           // stage, so the registers stay those of one 8-row tile.
 #pragma unroll
@@ -326,17 +330,25 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
               for (int e = 0; e < 4; ++e) D[mt][e] = 0.0f;
 #pragma unroll
             for (int e = 0; e < 4; ++e) O[e] = 0.0f;
-            for (int j = 0; j < ksub; ++j)
-              if (kb * GM_TK + r0 + 16 * j < g.K)
-                k16_step<NT>(wst, ast, r0 + 16 * j, wn, gq, t, nt, mlo, mhi, D, O);
-            // scale block done: acc += s_eff * (D - bias * sum a)
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt)
+            for (int j = 0; j < KS; ++j)
+              k16_step<NT>(wst, ast, r0 + 16 * j, wn, lane, gq, t, nt, mlo, mhi, D, O);
+            // scale block done: acc += s_eff * (D - bias * sum a), the high
+            // nibbles' scale divided by 16
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+              float se0 = scalar, se1 = scalar * 0.0625f;
+              if (g.srows) {
+                const uint32_t w2 = *reinterpret_cast<const uint32_t *>(srow_p + mt_col(mt, gq) * 2);
+                se0 = __half2float(__ushort_as_half((uint16_t)(w2 & 0xffffu)));
+                se1 = __half2float(__ushort_as_half((uint16_t)(w2 >> 16))) * 0.0625f;
+              }
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float c = fmaf(-(e < 2 ? blo : bhi), O[e & 1], D[mt][e]);
-                acc[mt][nt][e] = fmaf(se[2 * mt + (e >> 1)], c, acc[mt][nt][e]);
+                acc[mt][nt][e] = fmaf(e < 2 ? se0 : se1, c, acc[mt][nt][e]);
               }
+            }
           }
         }
       }
@@ -378,7 +390,7 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
       if (quad == 0 && ok) {
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
-          const int col = n0 + wn * 128 + gq * 16 + 2 * mt;
+          const int col = n0 + wn * 128 + mt_col(mt, gq);
           if (col >= g.N) continue; // ragged last tile (N % 256 != 0); N is even
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
@@ -398,7 +410,7 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
       if (quad == 0) {
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
-          const int col = wn * 128 + gq * 16 + 2 * mt;
+          const int col = wn * 128 + mt_col(mt, gq);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             const int m = nt * 8 + 2 * t;
@@ -501,7 +513,7 @@ MmaPlan mma_plan(const DqMmParams &p) {
   return m;
 }
 
-template <int NT, int G>
+template <int NT, int G, int KS>
 int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStream_t st) {
   CUtensorMap map_w, map_a, map_s;
   {
@@ -545,7 +557,7 @@ int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStrea
   a.srows = m.srows;
   a.is_signed = p.wdt == kInt4;
   a.scalar_scale = reinterpret_cast<const uint16_t *>(p.scale);
-  auto kern = dq_gemv_mma<NT, G>;
+  auto kern = dq_gemv_mma<NT, G, KS>;
   const size_t smem = GmSmem<NT>::kDynamic;
   B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   cudaLaunchConfig_t cfg = {};
@@ -599,12 +611,19 @@ size_t dq_mma_workspace(const DqMmParams &p) { return mma_plan(p).ws; }
 int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
   const MmaPlan m = mma_plan(p);
   if (m.ws && workspace == nullptr) B2_FAIL(B2_ERR_WORKSPACE, "workspace of %zu bytes required", m.ws);
-  if (m.groups == 1) {
-    if (m.nt == 1) return launch_mma<1, 1>(p, m, workspace, st);
-    return launch_mma<2, 1>(p, m, workspace, st);
+  if (m.groups == 1) // 32-row slabs: scale blocks are 32 rows or more
+    return m.nt == 1 ? launch_mma<1, 1, 2>(p, m, workspace, st)
+                     : launch_mma<2, 1, 2>(p, m, workspace, st);
+  // 128-row slabs: k16 steps per scale block
+  const int ks = (m.block == 0 || m.block >= GM_TK) ? 8 : m.block / 16;
+  if (m.nt == 1) {
+    if (ks == 2) return launch_mma<1, 4, 2>(p, m, workspace, st);
+    if (ks == 4) return launch_mma<1, 4, 4>(p, m, workspace, st);
+    return launch_mma<1, 4, 8>(p, m, workspace, st);
   }
-  if (m.nt == 1) return launch_mma<1, 4>(p, m, workspace, st);
-  return launch_mma<2, 4>(p, m, workspace, st);
+  if (ks == 2) return launch_mma<2, 4, 2>(p, m, workspace, st);
+  if (ks == 4) return launch_mma<2, 4, 4>(p, m, workspace, st);
+  return launch_mma<2, 4, 8>(p, m, workspace, st);
 }
 
 } // namespace b2
