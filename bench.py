@@ -47,7 +47,7 @@ PROJ = [("q", 4096, 4096, "x"), ("k", 4096, 4096, "x"), ("v", 4096, 4096, "x"),
         ("down", 11008, 4096, "gate")]
 BLOCK = 128
 NCOPIES = 4
-INT4, FLOAT16 = 22, 10
+INT4, FLOAT16, BF16 = 22, 10, 16
 
 
 def load_package():
@@ -351,7 +351,8 @@ def gpu_arm(args):
         want_cpu = not args.no_cpu_baseline
         secondary = {"attention_config4": attention_config4(b2, synth, device, stream, want_cpu),
                      "matmul_integer_config2": matmul_integer_config2(b2, synth, device, stream,
-                                                                      want_cpu)}
+                                                                      want_cpu),
+                     "prefill_config5": prefill_config5(b2, synth, device, stream, want_cpu)}
 
     if rank == 0:
         clocks = clk.summary()
@@ -483,6 +484,87 @@ def matmul_integer_config2(b2, synth, device, stream, cpu):
     return out
 
 
+def prefill_config5(b2, synth, device, stream, cpu):
+    """BASELINE config 5 on one GPU: bf16 activations [4, 8192, 4096] through
+    causal GQA Attention (32 query / 8 KV heads, head 128; K and V [4, 8192,
+    1024]) and then the blocked-dequant MatMuls 4096x11008 and 11008x4096, once
+    with float8e4m3fn weights and once with float4e2m1 weights (block 32 along
+    K, fp32 scales).  Metric: TFLOP/s of the step (attention counted with the
+    causal half, 2*M*K*N per MatMul)."""
+    import torch
+    B, S, Hq, Hkv, D = 4, 8192, 32, 8, 128
+    M, K1, N1 = B * S, 4096, 11008
+    x = synth.convert(synth.randn(5001, (B * S * Hq * D,), 0.0, 0.5, device=device), BF16,
+                      (B, S, Hq * D))
+    kk = synth.convert(synth.randn(5002, (B * S * Hkv * D,), 0.0, 0.5, device=device), BF16,
+                       (B, S, Hkv * D))
+    vv = synth.convert(synth.randn(5003, (B * S * Hkv * D,), 0.0, 0.5, device=device), BF16,
+                       (B, S, Hkv * D))
+    att = b2.Attention()
+    attrs = b2.Attributes(is_causal=True, q_num_heads=Hq, kv_num_heads=Hkv)
+    ao = torch.empty_like(x)
+    h = torch.empty((M, N1), dtype=torch.bfloat16, device=device)
+    y = torch.empty((M, K1), dtype=torch.bfloat16, device=device)
+    mm = b2.DequantizeMatMul()
+    att_flops = 4 * B * Hq * S * S * D // 2
+    mm_flops = 2 * M * K1 * N1
+    peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops_sustained"])
+        src = "measured sustained bf16 (MEASURED_PEAKS.json; the step runs ~20 ms)"
+    except (OSError, KeyError, ValueError):
+        peak, src = 1408.4, "fallback sustained bf16"
+
+    def ev_time(fn, reps=3):
+        with torch.cuda.stream(stream):
+            fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    a2 = ao.view(M, K1)
+    t_att = ev_time(lambda: att(x, kk, vv, attrs, out=ao))
+    out = {"metric": "Prefill block TFLOP/s (config 5: Attention + 2 dequant-MatMuls)",
+           "unit": "TFLOP/s", "dtype": "bf16 activations",
+           "config": {"batch": B, "seq": S, "q_heads": Hq, "kv_heads": Hkv, "head": D,
+                      "causal": True, "matmuls": "4096x11008, 11008x4096", "block_size": 32,
+                      "scales": "fp32"},
+           "attention_ms": round(t_att, 3),
+           "attention_tflops": round(att_flops / (t_att * 1e-3) / 1e12, 1), "formats": {}}
+    for name, dt, lo, hi in (("float8e4m3fn", 17, 0.01, 0.05), ("float4e2m1", 23, 0.05, 0.2)):
+        if dt == 17:
+            w1 = synth.convert(synth.randn(5010, (K1 * N1,), 0.0, 1.0, device=device), dt, (K1, N1))
+            w2 = synth.convert(synth.randn(5011, (N1 * K1,), 0.0, 1.0, device=device), dt, (N1, K1))
+        else:
+            w1 = synth.convert(synth.randint(5010, (K1 * N1,), 0, 15, device=device), dt, (K1, N1))
+            w2 = synth.convert(synth.randint(5011, (N1 * K1,), 0, 15, device=device), dt, (N1, K1))
+        s1 = synth.uniform(5020, (K1 // 32, N1), lo, hi, device=device)
+        s2 = synth.uniform(5021, (N1 // 32, K1), lo, hi, device=device)
+        t1 = ev_time(lambda: mm(a2, w1, s1, None, axis=0, cast_dtype=torch.bfloat16, out=h))
+        t2 = ev_time(lambda: mm(h, w2, s2, None, axis=0, cast_dtype=torch.bfloat16, out=y))
+        step = t_att + t1 + t2
+        tf = (att_flops + 2 * mm_flops) / (step * 1e-3) / 1e12
+        out["formats"][name] = {
+            "value": round(tf, 1), "ms_per_step": round(step, 3),
+            "matmul_ms": [round(t1, 3), round(t2, 3)],
+            "matmul_tflops": [round(mm_flops / (t1 * 1e-3) / 1e12, 1),
+                              round(mm_flops / (t2 * 1e-3) / 1e12, 1)],
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(tf / peak, 4), "peak_source": src}}
+        del w1, w2, s1, s2
+    out["value"] = out["formats"]["float8e4m3fn"]["value"]
+    if cpu:
+        out["cpu_baseline"] = _cpu_prefill_sample()
+    del x, kk, vv, ao, h, y
+    torch.cuda.empty_cache()
+    return out
+
+
 def measured_peak():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -583,6 +665,44 @@ def _cpu_attention_sample():
         return {"value": round(32 / t, 2), "unit": "tokens/s", "cores": O.ref_thread_count(),
                 "kind": "reference",
                 "sample": f"batch 1 of config 4 ({t / 32 * 1e3:.1f} ms), scaled x32 to batch 32"}
+    except Exception as e:
+        return {"value": None, "kind": "error", "sample": repr(e)[:200]}
+
+
+def _cpu_prefill_sample():
+    """Reference Attention (oracle/_ref) on [1, 512, 4096] bf16 scaled by the
+    FLOP ratio to [4, 8192, 4096], plus the reference DequantizeLinear
+    (float8e4m3fn, block 32) and MatMul of 32 rows scaled to 32768 rows."""
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import numpy as np
+        import oracle as O
+        if not O.ref_available():
+            return None
+        S, Hq, Hkv, D = 512, 32, 8, 128
+        b16 = lambda seed, shape: O.f32_to_bf16_bits(O.randn(seed, shape, 0.0, 0.5))
+        q, k, v = b16(1, (1, S, Hq * D)), b16(2, (1, S, Hkv * D)), b16(3, (1, S, Hkv * D))
+        t0 = time.perf_counter()
+        O.ref_attention(q, k, v, O.BFLOAT16, is_causal=True, q_num_heads=Hq, kv_num_heads=Hkv)
+        t_att = (time.perf_counter() - t0) * (4 * (8192 / S) ** 2)
+        K, N, m = 4096, 11008, 32
+        w = O.f32_to_f8e4m3fn(O.randn(4, (K, N), 0.0, 1.0))
+        sc = O.rand_uniform(5, (K // 32, N), 0.01, 0.05).astype(np.float32)
+        a = O.randn(6, (m, K), 0.0, 0.5).astype(np.float32)
+        t0 = time.perf_counter()
+        wd = O.ref_dequantize_linear(w, 17, (K, N), sc, O.FLOAT, (K // 32, N), axis=0)
+        t_dq = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        O.ref_matmul(a, wd, O.FLOAT)
+        t_mm = (time.perf_counter() - t0) * (4 * 8192 / m)
+        step = t_att + 2 * (t_dq + t_mm)
+        flops = 4 * 4 * Hq * 8192 * 8192 * D // 2 + 2 * 2 * 4 * 8192 * K * N
+        return {"value": round(flops / step / 1e12, 6), "unit": "TFLOP/s",
+                "cores": O.ref_thread_count(), "kind": "reference",
+                "sample": f"Attention [1,{S},4096] bf16 ({t_att / (4 * (8192 / S) ** 2):.2f} s, "
+                          f"scaled by FLOPs) + DequantizeLinear fp8 4096x11008 "
+                          f"({t_dq:.2f} s) + fp32 MatMul of {m} rows (scaled to 32768), "
+                          f"the second MatMul taken equal to the first"}
     except Exception as e:
         return {"value": None, "kind": "error", "sample": repr(e)[:200]}
 
