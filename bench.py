@@ -820,9 +820,21 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-4 attention and config-2 MatMulInteger measurements")
+    ap.add_argument("--only", choices=["attention4", "mmi2", "prefill5"],
+                    help="run one secondary measurement alone on cuda:0 (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.only:
+        import torch
+        b2 = load_package()
+        from onnx_light_b200 import synth
+        device = torch.device("cuda", 0)
+        stream = torch.cuda.Stream(device)
+        fn = {"attention4": attention_config4, "mmi2": matmul_integer_config2,
+              "prefill5": prefill_config5}[args.only]
+        print(json.dumps(fn(b2, synth, device, stream, False)), flush=True)
+        return
     if args.impl == "reference":
         reference_arm(args)
     else:

@@ -35,7 +35,13 @@ constexpr int AP_QROWS = 64;          // query rows per CTA (4 warps x 16)
 constexpr int AP_KEYS = 64;           // keys per tile
 constexpr int AP_WARPS = 4;
 constexpr int AP_THREADS = AP_WARPS * 32;
-constexpr int AP_STAGES = 2;
+#ifndef AP_STAGES_N
+#define AP_STAGES_N 2
+#endif
+#ifndef AP_MINB
+#define AP_MINB 3 // CTAs per SM
+#endif
+constexpr int AP_STAGES = AP_STAGES_N;
 constexpr uint32_t AP_HALF = AP_KEYS * 128;       // one 64-dim half of K or V: 8 KB
 constexpr uint32_t AP_STAGE = 4 * AP_HALF;        // K lo, K hi, V lo, V hi: 32 KB
 constexpr uint32_t AP_OFF_BAR = AP_STAGES * AP_STAGE;
@@ -89,17 +95,12 @@ template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float 
     return *reinterpret_cast<const uint32_t *>(&h);
   }
 }
-template <typename T> __device__ __forceinline__ void store1(T *p, float v);
-template <> __device__ __forceinline__ void store1<__half>(__half *p, float v) { *p = __float2half_rn(v); }
-template <> __device__ __forceinline__ void store1<__nv_bfloat16>(__nv_bfloat16 *p, float v) {
-  *p = __float2bfloat16_rn(v);
-}
 __device__ __forceinline__ uint32_t swz(int key, int chunk) {
   return (uint32_t)(key * 128 + ((chunk ^ (key & 7)) << 4));
 }
 
 template <typename T>
-__global__ void __launch_bounds__(AP_THREADS)
+__global__ void __launch_bounds__(AP_THREADS, AP_MINB)
     attn_prefill_mma(const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const ApArgs g) {
   extern __shared__ uint8_t dsm[];

@@ -47,6 +47,7 @@ struct DqTcArgs {
   uint32_t s_bytes;     // scale bytes per stage (0: scales read from global memory)
   int s_rows;           // scale rows per stage
   int op_bf16;          // MMA operand type: 1 bf16, 0 f16
+  int group_m;          // activation tiles per rasterization group (1: plain order)
   int *status;
 };
 
@@ -163,8 +164,21 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
   __shared__ volatile int abort_flag;
   __shared__ bool last_cta;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n0 = (int64_t)blockIdx.x * DT_BM;
-  const int64_t m0 = (int64_t)blockIdx.y * args.bn;
+  // Grouped rasterization: CTAs in launch order cover group_m activation
+  // tiles across every weight tile before the next group, so a wave's tiles
+  // share their operands in L2 instead of sweeping all weights per row tile.
+  int64_t tile_n = blockIdx.x, tile_m = blockIdx.y;
+  if (args.group_m > 1) {
+    const int64_t lin = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+    const int64_t per_group = (int64_t)args.group_m * gridDim.x;
+    const int64_t first_m = lin / per_group * args.group_m;
+    const int64_t gsz = min((int64_t)gridDim.y - first_m, (int64_t)args.group_m);
+    const int64_t r = lin % per_group;
+    tile_m = first_m + r % gsz;
+    tile_n = r / gsz;
+  }
+  const int64_t n0 = tile_n * DT_BM;
+  const int64_t m0 = tile_m * args.bn;
   const int split = blockIdx.z;
   const int64_t kbeg = (int64_t)split * p.kchunk;
   const int64_t kend = min(p.K, kbeg + p.kchunk);
@@ -444,6 +458,7 @@ static int dq_tc_mode(const DqMmParams &p) {
 struct TcPlan {
   int bn = 0, stages = 0, ksplit = 1, mode = 0, s_rows = 0;
   int pre = 0; // 1: dequantize the weight once into the workspace (kModePre)
+  int group_m = 1; // activation tiles per rasterization group
   uint32_t s_bytes = 0;
   int64_t kchunk = 0;
   uint32_t raw_bytes = 0, b_bytes = 0, stage_bytes = 0;
@@ -493,6 +508,13 @@ static TcPlan tc_plan(const DqMmParams &p) {
   t.kchunk = kchunk;
   t.ksplit = (int)((p.K + kchunk - 1) / kchunk);
   t.grid = dim3((unsigned)ntiles, (unsigned)mtiles, (unsigned)t.ksplit);
+  // About 32 MB of activation rows per group (L2 is 126 MB): the group's row
+  // tiles stay resident while the weight tiles stream past them once.
+  t.group_m = 1;
+  if (t.ksplit == 1) {
+    const int64_t tile_bytes = (int64_t)t.bn * p.K * 2;
+    t.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(mtiles, (32ll << 20) / tile_bytes));
+  }
   return t;
 }
 
@@ -543,6 +565,7 @@ int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st) {
   a.s_bytes = t.s_bytes;
   a.s_rows = t.s_rows;
   a.op_bf16 = pin.ydt == kBfloat16;
+  a.group_m = t.group_m;
   CUtensorMap map_a, map_w, map_s;
   if (t.s_bytes) {
     // scales [K / block, N] (FLOAT16 or FLOAT), box 128 columns x s_rows rows

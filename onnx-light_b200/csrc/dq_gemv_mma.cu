@@ -129,6 +129,18 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// d = a * b + c on two fp32 lanes (one packed instruction on sm_100).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\tmov.b64 rc, {%5, %6};\n\t"
+      "fma.rn.f32x2 %0, ra, rb, rc;\n\t}"
+      : "=l"(d)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
 __device__ __forceinline__ int unit_begin(int c, int U, int G) {
   return (int)((uint32_t)c * (uint32_t)U / (uint32_t)G); // units * grid < 2^31 (host check)
 }
@@ -343,11 +355,19 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
                 se0 = __half2float(__ushort_as_half((uint16_t)(w2 & 0xffffu)));
                 se1 = __half2float(__ushort_as_half((uint16_t)(w2 >> 16))) * 0.0625f;
               }
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float c = fmaf(-(e < 2 ? blo : bhi), O[e & 1], D[mt][e]);
-                acc[mt][nt][e] = fmaf(e < 2 ? se0 : se1, c, acc[mt][nt][e]);
-              }
+              // pairs (e = 0, 1) and (2, 3) share the bias and the scale: one
+              // packed fp32x2 FMA per pair (the same IEEE fma per element)
+              const float2 o01 = make_float2(O[0], O[1]);
+              const float2 c01 = ffma2(make_float2(-blo, -blo), o01, make_float2(D[mt][0], D[mt][1]));
+              const float2 c23 = ffma2(make_float2(-bhi, -bhi), o01, make_float2(D[mt][2], D[mt][3]));
+              const float2 a01 = ffma2(make_float2(se0, se0), c01,
+                                       make_float2(acc[mt][nt][0], acc[mt][nt][1]));
+              const float2 a23 = ffma2(make_float2(se1, se1), c23,
+                                       make_float2(acc[mt][nt][2], acc[mt][nt][3]));
+              acc[mt][nt][0] = a01.x;
+              acc[mt][nt][1] = a01.y;
+              acc[mt][nt][2] = a23.x;
+              acc[mt][nt][3] = a23.y;
             }
           }
         }
