@@ -38,8 +38,14 @@ namespace {
 
 constexpr int AD_D = 128;
 constexpr int AD_KEYS = 32;                       // keys per stage
-constexpr int AD_STAGES = 10;
+constexpr int AD_STAGES = 12;
 constexpr int AD_WARPS = 4;                       // consumer warps
+// Stage i is consumed by warp i % AD_WARPS.  With the ring a multiple of the
+// warp count, every fill of a stage goes to the same warp, which has consumed
+// the previous fill before it waits on the next one; a parity wait can then
+// never be satisfied by the fill before last (a warp waiting one phase ahead
+// of a fill still in flight would see its parity as complete).
+static_assert(AD_STAGES % AD_WARPS == 0, "each ring stage must belong to one consumer warp");
 constexpr int AD_THREADS = (AD_WARPS + 1) * 32;
 constexpr uint32_t AD_HALF = AD_KEYS * 64 * 2;    // one 64-dim half of K or V: 4 KB
 constexpr uint32_t AD_STAGE = 4 * AD_HALF;        // K lo, K hi, V lo, V hi: 16 KB

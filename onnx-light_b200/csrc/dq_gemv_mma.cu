@@ -281,6 +281,9 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
 
   // ------------------------------ consumers -------------------------------
   const int wn = warp & 1, quad = warp >> 1;
+  // Stage i goes to group i % G; every fill of a ring slot goes to the same
+  // group, which has consumed the previous fill before waiting on the next.
+  static_assert(GM_STAGES % G == 0, "each ring stage must belong to one stage group");
   constexpr int kSlabs = GM_QUADS / G;        // slabs per stage
   constexpr int kSlabRows = GM_TK / kSlabs;   // rows per slab
   const int grp = quad % G, slab = quad / G;
