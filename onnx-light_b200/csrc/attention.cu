@@ -34,6 +34,13 @@ size_t attn_decode_workspace(int64_t B, int64_t Hkv);
 // Tensor-core prefill kernel (attention_prefill.cu).
 bool attn_prefill_eligible(int dtype, int64_t D, int64_t Sq, bool mask, int64_t left_window,
                            int64_t right_window, int64_t k_ss, int64_t L);
+bool attn_prefill_tc_eligible(int dtype, int64_t D, int64_t Sq, bool mask, int64_t left_window,
+                              int64_t right_window, const int64_t *qs, const int64_t *ks,
+                              const int64_t *ys, int64_t L);
+int attn_prefill_tc_launch(int dtype, const void *q, const int64_t *qs, const void *kc,
+                           const void *vc, const int64_t *ks, void *y, const int64_t *ys,
+                           int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t L, int64_t past,
+                           float scale, float softcap, int causal, cudaStream_t st);
 int attn_prefill_launch(int dtype, const void *q, const int64_t *qs, const void *kc,
                         const void *vc, const int64_t *ks, void *y, const int64_t *ys, int64_t B,
                         int64_t Hq, int64_t Hkv, int64_t Sq, int64_t L, int64_t past, float scale,
@@ -404,9 +411,13 @@ __global__ void kv_copy(const T *__restrict__ src, int64_t s_sb, int64_t s_sh, i
 
 // ONNXL_B200_ATTN_KERNEL=cuda forces the CUDA-core kernel where the tensor-core
 // decode kernel would run (tests compare both); returns 1 in that case.
+// ONNXL_B200_ATTN_KERNEL: "cuda" forces the CUDA-core kernel, "mma" the
+// mma.sync prefill kernel instead of the tcgen05 one (tests compare them).
 static int forced_attention_kernel() {
   const char *e = getenv("ONNXL_B200_ATTN_KERNEL");
-  return (e && !strcmp(e, "cuda")) ? 1 : 0;
+  if (e && !strcmp(e, "cuda")) return 1;
+  if (e && !strcmp(e, "mma")) return 2;
+  return 0;
 }
 
 struct View { int64_t sb, sh, ss; };
@@ -622,6 +633,14 @@ static int attention_t(const b2_tensor *q, const b2_tensor *k, const b2_tensor *
   if (prefill_tc) {
     const int64_t qs[3] = {qv.sb, qv.sh, qv.ss}, ys[3] = {yv.sb, yv.sh, yv.ss};
     const int64_t ks[3] = {kview.sb, kview.sh, kview.ss};
+    // tcgen05 kernel unless forced to the mma.sync one; it needs 16-byte
+    // aligned Q / Y rows (TMA reads of Q, 16-byte stores of Y).
+    const bool aligned16 =
+        ((reinterpret_cast<uintptr_t>(q->data) | reinterpret_cast<uintptr_t>(y->data)) & 15) == 0;
+    if (forced_attention_kernel() != 2 && aligned16 &&
+        attn_prefill_tc_eligible(q->dtype, D, Sq, false, -1, -1, qs, ks, ys, L))
+      return attn_prefill_tc_launch(q->dtype, q->data, qs, p.k, p.v, ks, y->data, ys, B, Hq, Hkv,
+                                    Sq, L, P, p.scale, p.softcap, p.causal, st);
     return attn_prefill_launch(q->dtype, q->data, qs, p.k, p.v, ks, y->data, ys, B, Hq, Hkv, Sq,
                                L, P, p.scale, p.softcap, p.causal, st);
   }

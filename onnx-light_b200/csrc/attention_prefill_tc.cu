@@ -1,0 +1,425 @@
+// Prefill Attention on the 5th-generation tensor cores (tcgen05 + TMEM):
+// FLOAT16 / BFLOAT16, head size 128, GQA, optional causal mask and softcap.
+//
+// Reference: kernel::Attention::operator() / ComputeAttentionRank4
+// (onnx_light/onnx_extensions/kernels/kernels/nn/kernel_attention.cc:427-691,
+// 767-852): per query row i (absolute position past_len + i) and key j,
+// score = q . k * scale, softcap, causal mask j <= past_len + i, softmax with
+// max subtraction, y = softmax . V -- in fp32 after promoting the inputs.
+//
+// One CTA owns 128 query rows of one query head and walks 128-key tiles (up to
+// the diagonal when causal):
+//   warp 4 (TMA)   loads the Q tile once, then K and V tiles through a 2-stage
+//                  ring ([128 keys][64 dims] boxes, 128-byte swizzle);
+//   warp 5 (MMA)   issues S_j = Q . K_j^T into one of two TMEM S buffers
+//                  (M = 128 query rows, N = 128 keys, fp32), and, once the
+//                  softmax warps have written P_{j-1}, O += P_{j-1} . V_{j-1}
+//                  into the TMEM O accumulator (V read MN-major);
+//   warps 0-3      one query row per thread (= its TMEM lane): read the S row,
+//                  online softmax in base 2, write P (rounded to the input
+//                  type) into one of two shared-memory P buffers, and read,
+//                  scale and store O at the end.
+// The running maximum is re-based lazily: only when a row's maximum grows by
+// more than 8 (log2 units) are l and the TMEM O row rescaled, so P stays
+// within 2^8 and most tiles touch O only through the MMA.
+//
+// Every mbarrier is waited phase by phase by the threads that depend on it,
+// and no barrier can run two phases ahead of a waiter (each producer of a
+// phase needs the waiter's previous step first), so the parity waits are
+// exact.  All waits are bounded; a time-out sets the status word and the CTA
+// skips the rest, frees its TMEM and exits.
+#include <type_traits>
+
+#include "b2_common.cuh"
+#include "tc_common.cuh"
+
+namespace b2 {
+
+__device__ int g_attn_prefill_tc_status;
+
+namespace {
+
+constexpr int PT_D = 128;
+constexpr int PT_M = 128;            // query rows per CTA
+constexpr int PT_N = 128;            // keys per tile
+constexpr int PT_SOFT_WARPS = 4;
+constexpr int PT_THREADS = (PT_SOFT_WARPS + 2) * 32;
+constexpr uint32_t PT_HALF = 128 * 128;          // [128 rows][64 elements] bf16: 16 KB
+constexpr uint32_t PT_OFF_Q = 0;                  // 2 halves
+constexpr uint32_t PT_OFF_KV = 2 * PT_HALF;       // 2 stages x (K 2 halves, V 2 halves)
+constexpr uint32_t PT_KV_STAGE = 4 * PT_HALF;
+constexpr uint32_t PT_OFF_P = PT_OFF_KV + 2 * PT_KV_STAGE; // 2 buffers x 2 halves
+constexpr uint32_t PT_OFF_BAR = PT_OFF_P + 4 * PT_HALF;
+constexpr int PT_NBAR = 12;
+constexpr size_t PT_SMEM = PT_OFF_BAR + PT_NBAR * 8 + 16 + 1024;
+constexpr uint32_t PT_TMEM_COLS = 512;            // S0 [0,128), S1 [128,256), O [256,384)
+constexpr uint32_t PT_COL_O = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRebase = 8.0f;                   // lazy re-basing threshold (log2 units)
+
+struct PtArgs {
+  void *y;
+  int64_t y_sb, y_sh, y_ss; // strides (elements) of Y
+  int Hq, group, Sq, L, past;
+  int qtiles;
+  float scale_log2;
+  float softcap;
+  int causal;
+};
+
+template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __half>::value) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+  }
+}
+
+// Scores of 32 consecutive keys of one row in base-2 units: scale (or softcap),
+// then -inf for keys past the valid length or after the row's position.
+__device__ __forceinline__ void score_chunk(const uint32_t (&r)[32], float (&v)[32], const PtArgs &g,
+                                            bool need_mask, int key0, int pos) {
+  if (g.softcap > 0.0f) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      v[e] = g.softcap * tanhf(__uint_as_float(r[e]) * g.scale_log2 / kLog2e / g.softcap) * kLog2e;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]) * g.scale_log2;
+  }
+  if (need_mask) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int key = key0 + e;
+      if (key >= g.L || (g.causal && key > pos)) v[e] = -INFINITY;
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(PT_THREADS, 1)
+    attn_prefill_tc(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                    const __grid_constant__ CUtensorMap map_v, const PtArgs g) {
+  extern __shared__ uint8_t dsm[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + PT_OFF_BAR);
+  uint64_t *q_full = bars;           // 1
+  uint64_t *kv_full = bars + 1;      // 2
+  uint64_t *kv_empty = bars + 3;     // 2
+  uint64_t *s_full = bars + 5;       // 2
+  uint64_t *p_full = bars + 7;       // 2
+  uint64_t *o_done = bars + 9;       // 2
+  uint64_t *mma_done = bars + 11;    // 1: every MMA of the CTA finished
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + PT_NBAR);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = g.qtiles - 1 - (int)(blockIdx.x % g.qtiles); // heavy (late) tiles first
+  const int bh = (int)(blockIdx.x / g.qtiles);
+  const int b = bh / g.Hq, h = bh % g.Hq, kvh = h / g.group;
+  const int q0 = qt * PT_M;
+  const int kend = g.causal ? min(g.L, g.past + q0 + PT_M) : g.L;
+  const int ntiles = (kend + PT_N - 1) / PT_N;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&kv_full[i], 1);
+      tc::mbar_init(&kv_empty[i], 1);
+      tc::mbar_init(&s_full[i], 1);
+      tc::mbar_init(&p_full[i], PT_SOFT_WARPS);
+      tc::mbar_init(&o_done[i], 1);
+    }
+    tc::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 5) {
+    tc::tmem_alloc(tmem_slot, PT_TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------ TMA producer ------------------------------
+    if (tc::elect_one()) {
+      tc::prefetch_tensormap(&map_q);
+      tc::prefetch_tensormap(&map_k);
+      tc::prefetch_tensormap(&map_v);
+      tc::mbar_expect_tx(q_full, 2 * PT_HALF);
+      tc::tma_load_4d(sm + PT_OFF_Q, &map_q, q_full, 0, q0, h, b);
+      tc::tma_load_4d(sm + PT_OFF_Q + PT_HALF, &map_q, q_full, 64, q0, h, b);
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !tc::mbar_wait(&kv_empty[s], ((j - 2) >> 1) & 1)) {
+          atomicExch(&g_attn_prefill_tc_status, tc::kTimeoutEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        issued = j + 1;
+        uint8_t *st = sm + PT_OFF_KV + s * PT_KV_STAGE;
+        const int key0 = j * PT_N;
+        tc::mbar_expect_tx(&kv_full[s], PT_KV_STAGE);
+        tc::tma_load_4d(st, &map_k, &kv_full[s], 0, key0, kvh, b);
+        tc::tma_load_4d(st + PT_HALF, &map_k, &kv_full[s], 64, key0, kvh, b);
+        tc::tma_load_4d(st + 2 * PT_HALF, &map_v, &kv_full[s], 0, key0, kvh, b);
+        tc::tma_load_4d(st + 3 * PT_HALF, &map_v, &kv_full[s], 64, key0, kvh, b);
+      }
+      // No copy may land after the CTA exits: wait (bounded) for the last
+      // fills of both stages and for Q.  On the normal path they are done.
+      for (int j = max(0, issued - 2); j < issued; ++j) tc::mbar_wait(&kv_full[j & 1], (j >> 1) & 1);
+      tc::mbar_wait(q_full, 0);
+    }
+  } else if (warp == 5) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (tc::elect_one()) {
+      const uint32_t fmt = std::is_same<T, __half>::value ? 0u : 1u;
+      const uint32_t id_s = tc::idesc(1, fmt, fmt, 0, 0, PT_M, PT_N);
+      const uint32_t id_o = tc::idesc(1, fmt, fmt, 0, 1, PT_M, PT_D);
+      const uint32_t q_base = tc::smem_u32(sm + PT_OFF_Q);
+      bool ok = tc::mbar_wait(q_full, 0);
+      auto issue_pv = [&](int j) {
+        // O (+)= P_j . V_j: A = P (K-major over keys), B = V (MN-major over dims)
+        if (!tc::mbar_wait(&p_full[j & 1], (j >> 1) & 1)) return false;
+        tc::tc_fence_after();
+        const uint32_t p_base = tc::smem_u32(sm + PT_OFF_P + (j & 1) * 2 * PT_HALF);
+        const uint32_t v_base = tc::smem_u32(sm + PT_OFF_KV + (j & 1) * PT_KV_STAGE + 2 * PT_HALF);
+#pragma unroll
+        for (int kk = 0; kk < PT_N / 16; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(p_base + (kk >> 2) * PT_HALF + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sdesc_sw128(v_base + kk * 16 * 128, PT_HALF, 1024);
+          tc::mma_f16(tmem + PT_COL_O, ad, bd, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::tc_commit(&o_done[j & 1]);
+        tc::tc_commit(&kv_empty[j & 1]);
+        return true;
+      };
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (*abort_flag || !tc::mbar_wait(&kv_full[j & 1], (j >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t k_base = tc::smem_u32(sm + PT_OFF_KV + (j & 1) * PT_KV_STAGE);
+#pragma unroll
+        for (int kk = 0; kk < PT_D / 16; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(q_base + (kk >> 2) * PT_HALF + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sdesc_sw128(k_base + (kk >> 2) * PT_HALF + (kk & 3) * 32, 16, 1024);
+          tc::mma_f16(tmem + (j & 1) * PT_N, ad, bd, id_s, kk > 0 ? 1u : 0u);
+        }
+        tc::tc_commit(&s_full[j & 1]);
+        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok && ntiles > 0 && !issue_pv(ntiles - 1)) ok = false;
+      if (!ok) {
+        atomicExch(&g_attn_prefill_tc_status, tc::kTimeoutFull);
+        *abort_flag = 1;
+      }
+      // TMEM is freed below: wait (bounded) until every issued MMA is done.
+      tc::tc_commit(mma_done);
+      tc::mbar_wait(mma_done, 0);
+    }
+  } else {
+    // ------------------------------ softmax warps -----------------------------
+    // Control flow stays warp-uniform: the TMEM loads and stores are
+    // warp-collective.
+    const int row = warp * 32 + lane;              // query row in the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int pos = g.past + q0 + row;             // absolute position of the row
+    float m_ref = -INFINITY, l_sum = 0.0f;
+    bool ok = true;
+    auto uniform_wait = [&](uint64_t *bar, uint32_t parity) {
+      const bool w = !*abort_flag && tc::mbar_wait(bar, parity);
+      return __all_sync(0xffffffffu, w);
+    };
+    for (int j = 0; j < ntiles; ++j) {
+      if (!uniform_wait(&s_full[j & 1], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc::tc_fence_after();
+      // Two passes over the S row in 32-column chunks (the chunk loops stay
+      // rolled: a fully unrolled 128-column body overflows the instruction
+      // cache and runs an order of magnitude slower).
+      const int key0 = j * PT_N;
+      const bool need_mask = key0 + PT_N > g.L || (g.causal && key0 + PT_N - 1 > g.past + q0);
+      const uint32_t s_col = tmem + lane_off + (j & 1) * PT_N;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < PT_N / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(s_col + c * 32, r);
+        tc::tmem_ld_wait();
+        float v[32];
+        score_chunk(r, v, g, need_mask, key0 + c * 32, pos);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, v[e]);
+      }
+      // Re-base a row when its maximum grew by more than kRebase: l and its O
+      // row (after the previous P.V finished) scale by 2^(m_old - m_new).
+      const bool reb = mx > m_ref + kRebase;
+      float corr = 1.0f;
+      if (reb) {
+        corr = m_ref == -INFINITY ? 0.0f : exp2f(m_ref - mx);
+        l_sum *= corr;
+        m_ref = mx;
+      }
+      if (j >= 1 && __any_sync(0xffffffffu, reb)) {
+        if (!uniform_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < PT_D / 32; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld32(tmem + lane_off + PT_COL_O + c * 32, r);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
+          tc::tmem_st32(tmem + lane_off + PT_COL_O + c * 32, r);
+        }
+        tc::tmem_st_wait();
+      }
+      // P buffer (j & 1) is free once P.V of tile j - 2 is done.
+      if (j >= 2 && !uniform_wait(&o_done[j & 1], ((j - 2) >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      uint8_t *pb = sm + PT_OFF_P + (j & 1) * 2 * PT_HALF;
+      float ls = 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < PT_N / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(s_col + c * 32, r);
+        tc::tmem_ld_wait();
+        float v[32];
+        score_chunk(r, v, g, need_mask, key0 + c * 32, pos);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) { // 16-byte chunks of 8 keys
+          uint32_t w[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float x0 = v[q * 8 + 2 * u], x1 = v[q * 8 + 2 * u + 1];
+            const float p0 = x0 == -INFINITY ? 0.0f : exp2f(x0 - m_ref);
+            const float p1 = x1 == -INFINITY ? 0.0f : exp2f(x1 - m_ref);
+            ls += p0 + p1;
+            w[u] = pack2<T>(p0, p1);
+          }
+          const int kc = c * 4 + q; // 8-key chunk within the tile
+          const int half = kc >> 3, chunk = kc & 7;
+          *reinterpret_cast<uint4 *>(pb + half * PT_HALF + row * 128 + ((chunk ^ (row & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      l_sum += ls;
+      tc::fence_proxy_async();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&p_full[j & 1]);
+    }
+    // y = O / l
+    const int last = ntiles - 1;
+    if (ok && uniform_wait(&o_done[last & 1], (last >> 1) & 1)) {
+      tc::tc_fence_after();
+      const int qrow = q0 + row;
+      const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
+      T *yr = static_cast<T *>(g.y) + (int64_t)b * g.y_sb + (int64_t)h * g.y_sh +
+              (int64_t)qrow * g.y_ss;
+      uint32_t r[32];
+#pragma unroll 1
+      for (int c = 0; c < PT_D / 32; ++c) {
+        tc::tmem_ld32(tmem + lane_off + PT_COL_O + c * 32, r);
+        tc::tmem_ld_wait();
+        if (qrow < g.Sq) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 o;
+            o.x = pack2<T>(__uint_as_float(r[8 * q + 0]) * inv, __uint_as_float(r[8 * q + 1]) * inv);
+            o.y = pack2<T>(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv);
+            o.z = pack2<T>(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv);
+            o.w = pack2<T>(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv);
+            *reinterpret_cast<uint4 *>(yr + c * 32 + q * 8) = o;
+          }
+        }
+      }
+    } else {
+      atomicExch(&g_attn_prefill_tc_status, tc::kTimeoutFull);
+      *abort_flag = 1;
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) tc::tmem_dealloc(tmem, PT_TMEM_COLS);
+}
+
+} // namespace
+
+// Eligible: FLOAT16 / BFLOAT16, head size 128, no mask, no sliding window,
+// 16-byte aligned Q / K / V / Y rows and strides (the caller checks pointers).
+bool attn_prefill_tc_eligible(int dtype, int64_t D, int64_t Sq, bool mask, int64_t left_window,
+                              int64_t right_window, const int64_t *qs, const int64_t *ks,
+                              const int64_t *ys, int64_t L) {
+  if (!(dtype == kFloat16 || dtype == kBfloat16) || D != PT_D || Sq < 2 || mask ||
+      left_window >= 0 || right_window >= 0 || L < 1 || L >= ((int64_t)1 << 30) ||
+      Sq >= ((int64_t)1 << 30))
+    return false;
+  for (int i = 0; i < 3; ++i)
+    if (qs[i] % 8 != 0 || ks[i] % 8 != 0 || ys[i] % 8 != 0) return false;
+  return true;
+}
+
+int attn_prefill_tc_launch(int dtype, const void *q, const int64_t *qs, const void *kc,
+                           const void *vc, const int64_t *ks, void *y, const int64_t *ys,
+                           int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t L, int64_t past,
+                           float scale, float softcap, int causal, cudaStream_t st) {
+  // Q, K, V as 4-D {dim, row, head, batch}; strides in elements {batch, head, row}
+  CUtensorMap map_q, map_k, map_v;
+  const CUtensorMapDataType tdt =
+      dtype == kFloat16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint32_t box[4] = {64, 128, 1, 1};
+  {
+    const uint64_t dims[4] = {(uint64_t)PT_D, (uint64_t)Sq, (uint64_t)Hq, (uint64_t)B};
+    const uint64_t strides[3] = {(uint64_t)qs[2] * 2, (uint64_t)qs[1] * 2, (uint64_t)qs[0] * 2};
+    int rc = make_tensor_map(&map_q, tdt, 4, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[4] = {(uint64_t)PT_D, (uint64_t)L, (uint64_t)Hkv, (uint64_t)B};
+    const uint64_t strides[3] = {(uint64_t)ks[2] * 2, (uint64_t)ks[1] * 2, (uint64_t)ks[0] * 2};
+    int rc = make_tensor_map(&map_k, tdt, 4, kc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tensor_map(&map_v, tdt, 4, vc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  PtArgs a{};
+  a.y = y;
+  a.y_sb = ys[0];
+  a.y_sh = ys[1];
+  a.y_ss = ys[2];
+  a.Hq = (int)Hq;
+  a.group = (int)(Hq / Hkv);
+  a.Sq = (int)Sq;
+  a.L = (int)L;
+  a.past = (int)past;
+  a.qtiles = (int)((Sq + PT_M - 1) / PT_M);
+  a.scale_log2 = scale * kLog2e;
+  a.softcap = softcap;
+  a.causal = causal;
+  const int64_t ctas = (int64_t)a.qtiles * B * Hq;
+  if (ctas >= ((int64_t)1 << 31)) B2_FAIL(B2_ERR_UNSUPPORTED, "b2_attention: too many query tiles");
+  auto kern = dtype == kFloat16 ? attn_prefill_tc<__half> : attn_prefill_tc<__nv_bfloat16>;
+  B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PT_SMEM));
+  kern<<<(unsigned)ctas, PT_THREADS, PT_SMEM, st>>>(map_q, map_k, map_v, a);
+  B2_LAUNCH_CHECK();
+  return B2_OK;
+}
+
+} // namespace b2

@@ -244,3 +244,36 @@ def test_prefill_tensor_core_matches_cuda_core_kernel_and_is_deterministic(b2, c
     torch.cuda.synchronize()
     assert np.array_equal(y1, y2)
     assert rel_l2(y1, y3) <= 4e-3
+
+
+@pytest.mark.parametrize("dt,B,Hq,Hkv,S,P,causal,rank3", [
+    (O.FLOAT16, 2, 8, 2, 130, 0, True, False),
+    (O.BFLOAT16, 1, 8, 1, 200, 0, False, False),
+    (O.FLOAT16, 2, 16, 4, 77, 100, True, False),
+])
+def test_prefill_mma_sync_kernel(b2, cuda, monkeypatch, dt, B, Hq, Hkv, S, P, causal, rank3):
+    """The mma.sync prefill kernel (kept beside the tcgen05 one) against the oracle."""
+    monkeypatch.setenv("ONNXL_B200_ATTN_KERNEL", "mma")
+    y, ref = _prefill_case(b2, dt, B, Hq, Hkv, S, P, causal, rank3, seed=120 + S % 7)
+    assert rel_l2(y, ref) <= PREFILL_TOL[dt], rel_l2(y, ref)
+
+
+def test_prefill_tcgen05_long_causal_gqa(b2, cuda):
+    """Many 128-key tiles (re-basing of the running maximum), ragged Sq and L."""
+    y, ref = _prefill_case(b2, O.BFLOAT16, 1, 8, 2, 1000, 37, True, True, seed=131)
+    assert rel_l2(y, ref) <= PREFILL_TOL[O.BFLOAT16], rel_l2(y, ref)
+
+
+def test_prefill_tcgen05_matches_mma_sync_and_is_deterministic(b2, cuda, monkeypatch):
+    B, Hq, Hkv, S, D = 2, 16, 4, 700, 128
+    q = torch.randn(B, Hq, S, D, device="cuda").half() * 0.5
+    kk = torch.randn(B, Hkv, S, D, device="cuda").half() * 0.5
+    vv = torch.randn(B, Hkv, S, D, device="cuda").half() * 0.5
+    attrs = b2.Attributes(is_causal=True)
+    y1 = b2.Attention()(q, kk, vv, attrs).Y.float().cpu().numpy()
+    y2 = b2.Attention()(q, kk, vv, attrs).Y.float().cpu().numpy()
+    monkeypatch.setenv("ONNXL_B200_ATTN_KERNEL", "mma")
+    y3 = b2.Attention()(q, kk, vv, attrs).Y.float().cpu().numpy()
+    torch.cuda.synchronize()
+    assert np.array_equal(y1, y2)
+    assert rel_l2(y1, y3) <= 1e-3
