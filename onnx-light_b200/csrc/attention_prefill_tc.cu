@@ -9,16 +9,17 @@
 //
 // One CTA owns 128 query rows of one query head and walks 128-key tiles (up to
 // the diagonal when causal):
-//   warp 4 (TMA)   loads the Q tile once, then K and V tiles through a 2-stage
+//   warp 8 (TMA)   loads the Q tile once, then K and V tiles through a 2-stage
 //                  ring ([128 keys][64 dims] boxes, 128-byte swizzle);
-//   warp 5 (MMA)   issues S_j = Q . K_j^T into one of two TMEM S buffers
+//   warp 9 (MMA)   issues S_j = Q . K_j^T into one of two TMEM S buffers
 //                  (M = 128 query rows, N = 128 keys, fp32), and, once the
 //                  softmax warps have written P_{j-1}, O += P_{j-1} . V_{j-1}
 //                  into the TMEM O accumulator (V read MN-major);
-//   warps 0-3      one query row per thread (= its TMEM lane): read the S row,
-//                  online softmax in base 2, write P (rounded to the input
-//                  type) into one of two shared-memory P buffers, and read,
-//                  scale and store O at the end.
+//   warps 0-7      two threads per query row (its TMEM lane), one per 64-
+//                  column half: read S, online softmax in base 2 (row maximum
+//                  and sum combined through shared memory), write P (rounded
+//                  to the input type) into one of two shared-memory P
+//                  buffers, and read, scale and store O at the end.
 // The running maximum is re-based lazily: only when a row's maximum grows by
 // more than 8 (log2 units) are l and the TMEM O row rescaled, so P stays
 // within 2^8 and most tiles touch O only through the MMA.
@@ -42,16 +43,20 @@ namespace {
 constexpr int PT_D = 128;
 constexpr int PT_M = 128;            // query rows per CTA
 constexpr int PT_N = 128;            // keys per tile
-constexpr int PT_SOFT_WARPS = 4;
+constexpr int PT_SOFT_WARPS = 8;                  // two per query row: column halves
+constexpr int PT_TMA_WARP = PT_SOFT_WARPS, PT_MMA_WARP = PT_SOFT_WARPS + 1;
 constexpr int PT_THREADS = (PT_SOFT_WARPS + 2) * 32;
 constexpr uint32_t PT_HALF = 128 * 128;          // [128 rows][64 elements] bf16: 16 KB
 constexpr uint32_t PT_OFF_Q = 0;                  // 2 halves
 constexpr uint32_t PT_OFF_KV = 2 * PT_HALF;       // 2 stages x (K 2 halves, V 2 halves)
 constexpr uint32_t PT_KV_STAGE = 4 * PT_HALF;
 constexpr uint32_t PT_OFF_P = PT_OFF_KV + 2 * PT_KV_STAGE; // 2 buffers x 2 halves
-constexpr uint32_t PT_OFF_BAR = PT_OFF_P + 4 * PT_HALF;
+constexpr uint32_t PT_OFF_RED = PT_OFF_P + 4 * PT_HALF; // [tile parity][half][row] partial maxima
+constexpr uint32_t PT_OFF_BAR = PT_OFF_RED + 2 * 2 * PT_M * 4;
 constexpr int PT_NBAR = 12;
-constexpr size_t PT_SMEM = PT_OFF_BAR + PT_NBAR * 8 + 16 + 1024;
+// No alignment slack: the dynamic shared memory base is 1024-byte aligned
+// (checked at run time; a CTA that finds it otherwise reports and skips).
+constexpr size_t PT_SMEM = PT_OFF_BAR + PT_NBAR * 8 + 16;
 constexpr uint32_t PT_TMEM_COLS = 512;            // S0 [0,128), S1 [128,256), O [256,384)
 constexpr uint32_t PT_COL_O = 256;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -102,9 +107,14 @@ template <typename T>
 __global__ void __launch_bounds__(PT_THREADS, 1)
     attn_prefill_tc(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, const PtArgs g) {
-  extern __shared__ uint8_t dsm[];
-  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t dsm[];
+  if (tc::smem_u32(dsm) & 1023u) { // the layout below needs a 1024-byte aligned base
+    if (threadIdx.x == 0) atomicExch(&g_attn_prefill_tc_status, tc::kTimeoutFull);
+    return;
+  }
+  uint8_t *sm = dsm;
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + PT_OFF_BAR);
+  float *red = reinterpret_cast<float *>(sm + PT_OFF_RED);
   uint64_t *q_full = bars;           // 1
   uint64_t *kv_full = bars + 1;      // 2
   uint64_t *kv_empty = bars + 3;     // 2
@@ -136,7 +146,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == PT_MMA_WARP) {
     tc::tmem_alloc(tmem_slot, PT_TMEM_COLS);
     tc::tmem_relinquish();
   }
@@ -145,7 +155,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == PT_TMA_WARP) {
     // ------------------------------ TMA producer ------------------------------
     if (tc::elect_one()) {
       tc::prefetch_tensormap(&map_q);
@@ -177,7 +187,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       for (int j = max(0, issued - 2); j < issued; ++j) tc::mbar_wait(&kv_full[j & 1], (j >> 1) & 1);
       tc::mbar_wait(q_full, 0);
     }
-  } else if (warp == 5) {
+  } else if (warp == PT_MMA_WARP) {
     // ------------------------------ MMA issuer --------------------------------
     if (tc::elect_one()) {
       const uint32_t fmt = std::is_same<T, __half>::value ? 0u : 1u;
@@ -228,80 +238,89 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     }
   } else {
     // ------------------------------ softmax warps -----------------------------
-    // Control flow stays warp-uniform: the TMEM loads and stores are
-    // warp-collective.
-    const int row = warp * 32 + lane;              // query row in the tile = TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // Two threads per query row (warps w and w + 4 share TMEM lanes 32 (w % 4)
+    // .. + 31), each on one 64-column half of S, P and O; the row maximum and
+    // sum combine through shared memory.  Control flow stays warp-uniform
+    // (the TMEM loads and stores are warp-collective), and every softmax warp
+    // takes every named barrier even after a time-out, so none can hang.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;           // query row in the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int pos = g.past + q0 + row;             // absolute position of the row
-    float m_ref = -INFINITY, l_sum = 0.0f;
+    float m_ref = -INFINITY, l_part = 0.0f;
     bool ok = true;
     auto uniform_wait = [&](uint64_t *bar, uint32_t parity) {
-      const bool w = !*abort_flag && tc::mbar_wait(bar, parity);
+      const bool w = ok && !*abort_flag && tc::mbar_wait(bar, parity);
       return __all_sync(0xffffffffu, w);
     };
+    auto softmax_sync = [] { asm volatile("bar.sync 1, %0;" ::"n"(PT_SOFT_WARPS * 32) : "memory"); };
     for (int j = 0; j < ntiles; ++j) {
-      if (!uniform_wait(&s_full[j & 1], (j >> 1) & 1)) {
-        ok = false;
-        break;
-      }
+      if (!uniform_wait(&s_full[j & 1], (j >> 1) & 1)) ok = false;
       tc::tc_fence_after();
-      // Two passes over the S row in 32-column chunks (the chunk loops stay
-      // rolled: a fully unrolled 128-column body overflows the instruction
-      // cache and runs an order of magnitude slower).
       const int key0 = j * PT_N;
       const bool need_mask = key0 + PT_N > g.L || (g.causal && key0 + PT_N - 1 > g.past + q0);
-      const uint32_t s_col = tmem + lane_off + (j & 1) * PT_N;
+      const uint32_t s_col = tmem + lane_off + (j & 1) * PT_N + half * 64;
+      // pass 1: this half's maximum, then the row's through shared memory
       float mx = -INFINITY;
+      if (ok) {
 #pragma unroll 1
-      for (int c = 0; c < PT_N / 32; ++c) {
-        uint32_t r[32];
-        tc::tmem_ld32(s_col + c * 32, r);
-        tc::tmem_ld_wait();
-        float v[32];
-        score_chunk(r, v, g, need_mask, key0 + c * 32, pos);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld32(s_col + c * 32, r);
+          tc::tmem_ld_wait();
+          float v[32];
+          score_chunk(r, v, g, need_mask, key0 + half * 64 + c * 32, pos);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, v[e]);
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, v[e]);
+        }
       }
+      float *rm = red + (j & 1) * 2 * PT_M;
+      rm[half * PT_M + row] = mx;
+      softmax_sync();
+      mx = fmaxf(mx, rm[(half ^ 1) * PT_M + row]);
+      if (!ok) continue;
       // Re-base a row when its maximum grew by more than kRebase: l and its O
       // row (after the previous P.V finished) scale by 2^(m_old - m_new).
       const bool reb = mx > m_ref + kRebase;
       float corr = 1.0f;
       if (reb) {
         corr = m_ref == -INFINITY ? 0.0f : exp2f(m_ref - mx);
-        l_sum *= corr;
+        l_part *= corr;
         m_ref = mx;
       }
       if (j >= 1 && __any_sync(0xffffffffu, reb)) {
         if (!uniform_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
           ok = false;
-          break;
+          continue;
         }
         tc::tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < PT_D / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t o_col = tmem + lane_off + PT_COL_O + half * 64 + c * 32;
           uint32_t r[32];
-          tc::tmem_ld32(tmem + lane_off + PT_COL_O + c * 32, r);
+          tc::tmem_ld32(o_col, r);
           tc::tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
-          tc::tmem_st32(tmem + lane_off + PT_COL_O + c * 32, r);
+          tc::tmem_st32(o_col, r);
         }
         tc::tmem_st_wait();
       }
       // P buffer (j & 1) is free once P.V of tile j - 2 is done.
       if (j >= 2 && !uniform_wait(&o_done[j & 1], ((j - 2) >> 1) & 1)) {
         ok = false;
-        break;
+        continue;
       }
-      uint8_t *pb = sm + PT_OFF_P + (j & 1) * 2 * PT_HALF;
+      // pass 2: P for this half (its 64 keys are the P buffer's half `half`)
+      uint8_t *pb = sm + PT_OFF_P + (j & 1) * 2 * PT_HALF + half * PT_HALF + row * 128;
       float ls = 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < PT_N / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tc::tmem_ld32(s_col + c * 32, r);
         tc::tmem_ld_wait();
         float v[32];
-        score_chunk(r, v, g, need_mask, key0 + c * 32, pos);
+        score_chunk(r, v, g, need_mask, key0 + half * 64 + c * 32, pos);
 #pragma unroll
         for (int q = 0; q < 4; ++q) { // 16-byte chunks of 8 keys
           uint32_t w[4];
@@ -313,30 +332,34 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
             ls += p0 + p1;
             w[u] = pack2<T>(p0, p1);
           }
-          const int kc = c * 4 + q; // 8-key chunk within the tile
-          const int half = kc >> 3, chunk = kc & 7;
-          *reinterpret_cast<uint4 *>(pb + half * PT_HALF + row * 128 + ((chunk ^ (row & 7)) << 4)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
+          const int chunk = c * 4 + q;
+          *reinterpret_cast<uint4 *>(pb + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-      l_sum += ls;
+      l_part += ls;
       tc::fence_proxy_async();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[j & 1]);
     }
-    // y = O / l
+    // y = O / l, l = the two halves' sums (the reduction slots of tile parity 0
+    // are free: every thread has passed the last tile's barrier)
     const int last = ntiles - 1;
-    if (ok && uniform_wait(&o_done[last & 1], (last >> 1) & 1)) {
+    const bool fin = uniform_wait(&o_done[last & 1], (last >> 1) & 1);
+    softmax_sync();
+    red[half * PT_M + row] = l_part;
+    softmax_sync();
+    const float l_sum = l_part + red[(half ^ 1) * PT_M + row];
+    if (fin) {
       tc::tc_fence_after();
       const int qrow = q0 + row;
       const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
       T *yr = static_cast<T *>(g.y) + (int64_t)b * g.y_sb + (int64_t)h * g.y_sh +
-              (int64_t)qrow * g.y_ss;
+              (int64_t)qrow * g.y_ss + half * 64;
       uint32_t r[32];
 #pragma unroll 1
-      for (int c = 0; c < PT_D / 32; ++c) {
-        tc::tmem_ld32(tmem + lane_off + PT_COL_O + c * 32, r);
+      for (int c = 0; c < 2; ++c) {
+        tc::tmem_ld32(tmem + lane_off + PT_COL_O + half * 64 + c * 32, r);
         tc::tmem_ld_wait();
         if (qrow < g.Sq) {
 #pragma unroll
@@ -357,7 +380,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) tc::tmem_dealloc(tmem, PT_TMEM_COLS);
+  if (warp == PT_MMA_WARP) tc::tmem_dealloc(tmem, PT_TMEM_COLS);
 }
 
 } // namespace
