@@ -512,7 +512,7 @@ def prefill_config5(b2, synth, device, stream, cpu):
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peak = float(json.load(f)["bf16_tflops_sustained"])
-        src = "measured sustained bf16 (MEASURED_PEAKS.json; the step runs ~20 ms)"
+        src = "measured sustained bf16 (MEASURED_PEAKS.json; the block runs about 10 ms)"
     except (OSError, KeyError, ValueError):
         peak, src = 1408.4, "fallback sustained bf16"
 
