@@ -82,25 +82,38 @@ template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float 
   }
 }
 
-// Scores of 32 consecutive keys of one row in base-2 units: scale (or softcap),
-// then -inf for keys past the valid length or after the row's position.
-__device__ __forceinline__ void score_chunk(const uint32_t (&r)[32], float (&v)[32], const PtArgs &g,
-                                            bool need_mask, int key0, int pos) {
+// 32 consecutive scores of one row into v[off .. off + 31]: raw when the
+// scale is positive and there is no softcap (the scale is applied in the
+// exponent), else already in base-2 units (scale or softcap); -inf for keys
+// past the valid length or after the row's position.
+__device__ __forceinline__ void load_scores(const uint32_t (&r)[32], float (&v)[64], int off,
+                                            const PtArgs &g, bool need_mask, int key0, int pos) {
   if (g.softcap > 0.0f) {
 #pragma unroll
     for (int e = 0; e < 32; ++e)
-      v[e] = g.softcap * tanhf(__uint_as_float(r[e]) * g.scale_log2 / kLog2e / g.softcap) * kLog2e;
+      v[off + e] = g.softcap * tanhf(__uint_as_float(r[e]) * g.scale_log2 / kLog2e / g.softcap) * kLog2e;
+  } else if (g.scale_log2 > 0.0f) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[off + e] = __uint_as_float(r[e]);
   } else {
 #pragma unroll
-    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]) * g.scale_log2;
+    for (int e = 0; e < 32; ++e) v[off + e] = __uint_as_float(r[e]) * g.scale_log2;
   }
   if (need_mask) {
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
       const int key = key0 + e;
-      if (key >= g.L || (g.causal && key > pos)) v[e] = -INFINITY;
+      if (key >= g.L || (g.causal && key > pos)) v[off + e] = -INFINITY;
     }
   }
+}
+
+// 2^x with the hardware approximation (relative error about 2^-22; inputs are
+// <= 8 here, and -inf gives 0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 template <typename T>
@@ -248,6 +261,9 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int pos = g.past + q0 + row;             // absolute position of the row
     float m_ref = -INFINITY, l_part = 0.0f;
+    // scores are kept raw and scaled inside the exponent's FMA when the scale
+    // is positive and there is no softcap; otherwise transformed up front
+    const float vk = (g.softcap <= 0.0f && g.scale_log2 > 0.0f) ? g.scale_log2 : 1.0f;
     bool ok = true;
     auto uniform_wait = [&](uint64_t *bar, uint32_t parity) {
       const bool w = ok && !*abort_flag && tc::mbar_wait(bar, parity);
@@ -260,19 +276,21 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       const int key0 = j * PT_N;
       const bool need_mask = key0 + PT_N > g.L || (g.causal && key0 + PT_N - 1 > g.past + q0);
       const uint32_t s_col = tmem + lane_off + (j & 1) * PT_N + half * 64;
-      // pass 1: this half's maximum, then the row's through shared memory
+      // pass 1: the half row's 64 scores stay in registers (v, in units where
+      // p = 2^(v * vk - m)); this half's maximum, then the row's through
+      // shared memory
+      float v[64];
       float mx = -INFINITY;
       if (ok) {
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t r[32];
-          tc::tmem_ld32(s_col + c * 32, r);
-          tc::tmem_ld_wait();
-          float v[32];
-          score_chunk(r, v, g, need_mask, key0 + half * 64 + c * 32, pos);
+        uint32_t r0[32], r1[32];
+        tc::tmem_ld32(s_col, r0);
+        tc::tmem_ld32(s_col + 32, r1);
+        tc::tmem_ld_wait();
+        load_scores(r0, v, 0, g, need_mask, key0 + half * 64, pos);
+        load_scores(r1, v, 32, g, need_mask, key0 + half * 64 + 32, pos);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, v[e]);
-        }
+        for (int e = 0; e < 64; ++e) mx = fmaxf(mx, v[e]);
+        mx *= vk; // vk > 0: the maximum of the scaled scores
       }
       float *rm = red + (j & 1) * 2 * PT_M;
       rm[half * PT_M + row] = mx;
@@ -311,30 +329,22 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
         ok = false;
         continue;
       }
-      // pass 2: P for this half (its 64 keys are the P buffer's half `half`)
+      // pass 2: P for this half (its 64 keys are the P buffer's half `half`);
+      // masked scores are -inf and give 2^-inf = 0
       uint8_t *pb = sm + PT_OFF_P + (j & 1) * 2 * PT_HALF + half * PT_HALF + row * 128;
+      const float nm = -m_ref;
       float ls = 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-        tc::tmem_ld32(s_col + c * 32, r);
-        tc::tmem_ld_wait();
-        float v[32];
-        score_chunk(r, v, g, need_mask, key0 + half * 64 + c * 32, pos);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) { // 16-byte chunks of 8 keys
-          uint32_t w[4];
+      for (int chunk = 0; chunk < 8; ++chunk) { // 16-byte chunks of 8 keys
+        uint32_t w[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float x0 = v[q * 8 + 2 * u], x1 = v[q * 8 + 2 * u + 1];
-            const float p0 = x0 == -INFINITY ? 0.0f : exp2f(x0 - m_ref);
-            const float p1 = x1 == -INFINITY ? 0.0f : exp2f(x1 - m_ref);
-            ls += p0 + p1;
-            w[u] = pack2<T>(p0, p1);
-          }
-          const int chunk = c * 4 + q;
-          *reinterpret_cast<uint4 *>(pb + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int u = 0; u < 4; ++u) {
+          const float p0 = ex2(fmaf(v[chunk * 8 + 2 * u], vk, nm));
+          const float p1 = ex2(fmaf(v[chunk * 8 + 2 * u + 1], vk, nm));
+          ls += p0 + p1;
+          w[u] = pack2<T>(p0, p1);
         }
+        *reinterpret_cast<uint4 *>(pb + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l_part += ls;
       tc::fence_proxy_async();
