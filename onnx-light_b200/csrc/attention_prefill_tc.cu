@@ -7,10 +7,14 @@
 // score = q . k * scale, softcap, causal mask j <= past_len + i, softmax with
 // max subtraction, y = softmax . V -- in fp32 after promoting the inputs.
 //
-// One CTA owns 128 query rows of one query head and walks 128-key tiles (up to
+// One CTA owns 128 query rows -- pk query heads of one GQA group (pk the
+// largest power of two up to 8 dividing the group) x 128 / pk positions, so a
+// K / V tile read from L2 serves pk heads -- and walks 128-key tiles (up to
 // the diagonal when causal):
-//   warp 8 (TMA)   loads the Q tile once, then K and V tiles through a 2-stage
-//                  ring ([128 keys][64 dims] boxes, 128-byte swizzle);
+//   warp 8 (TMA)   loads the Q tile once, then K and V tiles through 2-stage
+//                  rings of their own ([128 keys][64 dims] boxes, 128-byte
+//                  swizzle): a K stage frees when S is done, a V stage when
+//                  P.V is done, so K runs a tile ahead;
 //   warp 9 (MMA)   issues S_j = Q . K_j^T into one of two TMEM S buffers
 //                  (M = 128 query rows, N = 128 keys, fp32), and, once the
 //                  softmax warps have written P_{j-1}, O += P_{j-1} . V_{j-1}
@@ -53,7 +57,7 @@ constexpr uint32_t PT_KV_STAGE = 4 * PT_HALF;
 constexpr uint32_t PT_OFF_P = PT_OFF_KV + 2 * PT_KV_STAGE; // 2 buffers x 2 halves
 constexpr uint32_t PT_OFF_RED = PT_OFF_P + 4 * PT_HALF; // [tile parity][half][row] partial maxima
 constexpr uint32_t PT_OFF_BAR = PT_OFF_RED + 2 * 2 * PT_M * 4;
-constexpr int PT_NBAR = 12;
+constexpr int PT_NBAR = 16;
 // No alignment slack: the dynamic shared memory base is 1024-byte aligned
 // (checked at run time; a CTA that finds it otherwise reports and skips).
 constexpr size_t PT_SMEM = PT_OFF_BAR + PT_NBAR * 8 + 16;
@@ -67,6 +71,7 @@ struct PtArgs {
   int64_t y_sb, y_sh, y_ss; // strides (elements) of Y
   int Hq, group, Sq, L, past;
   int qtiles;
+  int pk, np_, hpacks; // query heads per CTA (of one GQA group), positions per head, packs
   float scale_log2;
   float softcap;
   int causal;
@@ -129,28 +134,35 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + PT_OFF_BAR);
   float *red = reinterpret_cast<float *>(sm + PT_OFF_RED);
   uint64_t *q_full = bars;           // 1
-  uint64_t *kv_full = bars + 1;      // 2
-  uint64_t *kv_empty = bars + 3;     // 2
-  uint64_t *s_full = bars + 5;       // 2
-  uint64_t *p_full = bars + 7;       // 2
-  uint64_t *o_done = bars + 9;       // 2
-  uint64_t *mma_done = bars + 11;    // 1: every MMA of the CTA finished
+  uint64_t *k_full = bars + 1;       // 2: K of a stage landed
+  uint64_t *k_empty = bars + 3;      // 2: S of the stage's tile done (K free)
+  uint64_t *v_full = bars + 5;       // 2
+  uint64_t *v_empty = bars + 7;      // 2: P.V of the stage's tile done (V free)
+  uint64_t *s_full = bars + 9;       // 2
+  uint64_t *p_full = bars + 11;      // 2
+  uint64_t *o_done = bars + 13;      // 2
+  uint64_t *mma_done = bars + 15;    // 1: every MMA of the CTA finished
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + PT_NBAR);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The 128 rows are pk query heads of one GQA group x np_ positions (row r:
+  // head h0 + r / np_, position q0 + r % np_), so every K / V tile serves pk
+  // heads.
   const int qt = g.qtiles - 1 - (int)(blockIdx.x % g.qtiles); // heavy (late) tiles first
-  const int bh = (int)(blockIdx.x / g.qtiles);
-  const int b = bh / g.Hq, h = bh % g.Hq, kvh = h / g.group;
-  const int q0 = qt * PT_M;
-  const int kend = g.causal ? min(g.L, g.past + q0 + PT_M) : g.L;
+  const int bhp = (int)(blockIdx.x / g.qtiles);
+  const int b = bhp / g.hpacks, h0 = (bhp % g.hpacks) * g.pk, kvh = h0 / g.group;
+  const int q0 = qt * g.np_;
+  const int kend = g.causal ? min(g.L, g.past + q0 + g.np_) : g.L;
   const int ntiles = (kend + PT_N - 1) / PT_N;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&kv_full[i], 1);
-      tc::mbar_init(&kv_empty[i], 1);
+      tc::mbar_init(&k_full[i], 1);
+      tc::mbar_init(&k_empty[i], 1);
+      tc::mbar_init(&v_full[i], 1);
+      tc::mbar_init(&v_empty[i], 1);
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&p_full[i], PT_SOFT_WARPS);
       tc::mbar_init(&o_done[i], 1);
@@ -170,35 +182,43 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
 
   if (warp == PT_TMA_WARP) {
     // ------------------------------ TMA producer ------------------------------
-    if (tc::elect_one()) {
-      tc::prefetch_tensormap(&map_q);
-      tc::prefetch_tensormap(&map_k);
-      tc::prefetch_tensormap(&map_v);
-      tc::mbar_expect_tx(q_full, 2 * PT_HALF);
-      tc::tma_load_4d(sm + PT_OFF_Q, &map_q, q_full, 0, q0, h, b);
-      tc::tma_load_4d(sm + PT_OFF_Q + PT_HALF, &map_q, q_full, 64, q0, h, b);
+    // Lane 0 fills the K ring (a stage is free once S of its tile is done),
+    // lane 1 the V ring (free once P.V is done), so the next K tile is on its
+    // way while the softmax and P.V of the current one still run.
+    if (lane < 2) {
+      const bool is_k = lane == 0;
+      const CUtensorMap *map = is_k ? &map_k : &map_v;
+      uint64_t *full = is_k ? k_full : v_full;
+      uint64_t *empty = is_k ? k_empty : v_empty;
+      if (is_k) {
+        tc::prefetch_tensormap(&map_q);
+        tc::prefetch_tensormap(&map_k);
+        tc::mbar_expect_tx(q_full, 2 * PT_HALF);
+        tc::tma_load_4d(sm + PT_OFF_Q, &map_q, q_full, 0, q0, h0, b);
+        tc::tma_load_4d(sm + PT_OFF_Q + PT_HALF, &map_q, q_full, 64, q0, h0, b);
+      } else {
+        tc::prefetch_tensormap(&map_v);
+      }
       int issued = 0;
       for (int j = 0; j < ntiles; ++j) {
         const int s = j & 1;
-        if (j >= 2 && !tc::mbar_wait(&kv_empty[s], ((j - 2) >> 1) & 1)) {
+        if (j >= 2 && !tc::mbar_wait(&empty[s], ((j - 2) >> 1) & 1)) {
           atomicExch(&g_attn_prefill_tc_status, tc::kTimeoutEmpty);
           *abort_flag = 1;
           break;
         }
         if (*abort_flag) break;
         issued = j + 1;
-        uint8_t *st = sm + PT_OFF_KV + s * PT_KV_STAGE;
+        uint8_t *st = sm + PT_OFF_KV + s * PT_KV_STAGE + (is_k ? 0u : 2 * PT_HALF);
         const int key0 = j * PT_N;
-        tc::mbar_expect_tx(&kv_full[s], PT_KV_STAGE);
-        tc::tma_load_4d(st, &map_k, &kv_full[s], 0, key0, kvh, b);
-        tc::tma_load_4d(st + PT_HALF, &map_k, &kv_full[s], 64, key0, kvh, b);
-        tc::tma_load_4d(st + 2 * PT_HALF, &map_v, &kv_full[s], 0, key0, kvh, b);
-        tc::tma_load_4d(st + 3 * PT_HALF, &map_v, &kv_full[s], 64, key0, kvh, b);
+        tc::mbar_expect_tx(&full[s], 2 * PT_HALF);
+        tc::tma_load_4d(st, map, &full[s], 0, key0, kvh, b);
+        tc::tma_load_4d(st + PT_HALF, map, &full[s], 64, key0, kvh, b);
       }
       // No copy may land after the CTA exits: wait (bounded) for the last
-      // fills of both stages and for Q.  On the normal path they are done.
-      for (int j = max(0, issued - 2); j < issued; ++j) tc::mbar_wait(&kv_full[j & 1], (j >> 1) & 1);
-      tc::mbar_wait(q_full, 0);
+      // fills of both stages (and Q).  On the normal path they are done.
+      for (int j = max(0, issued - 2); j < issued; ++j) tc::mbar_wait(&full[j & 1], (j >> 1) & 1);
+      if (is_k) tc::mbar_wait(q_full, 0);
     }
   } else if (warp == PT_MMA_WARP) {
     // ------------------------------ MMA issuer --------------------------------
@@ -211,6 +231,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       auto issue_pv = [&](int j) {
         // O (+)= P_j . V_j: A = P (K-major over keys), B = V (MN-major over dims)
         if (!tc::mbar_wait(&p_full[j & 1], (j >> 1) & 1)) return false;
+        if (!tc::mbar_wait(&v_full[j & 1], (j >> 1) & 1)) return false;
         tc::tc_fence_after();
         const uint32_t p_base = tc::smem_u32(sm + PT_OFF_P + (j & 1) * 2 * PT_HALF);
         const uint32_t v_base = tc::smem_u32(sm + PT_OFF_KV + (j & 1) * PT_KV_STAGE + 2 * PT_HALF);
@@ -221,11 +242,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
           tc::mma_f16(tmem + PT_COL_O, ad, bd, id_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         tc::tc_commit(&o_done[j & 1]);
-        tc::tc_commit(&kv_empty[j & 1]);
+        tc::tc_commit(&v_empty[j & 1]);
         return true;
       };
       for (int j = 0; ok && j < ntiles; ++j) {
-        if (*abort_flag || !tc::mbar_wait(&kv_full[j & 1], (j >> 1) & 1)) {
+        if (*abort_flag || !tc::mbar_wait(&k_full[j & 1], (j >> 1) & 1)) {
           ok = false;
           break;
         }
@@ -238,6 +259,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
           tc::mma_f16(tmem + (j & 1) * PT_N, ad, bd, id_s, kk > 0 ? 1u : 0u);
         }
         tc::tc_commit(&s_full[j & 1]);
+        tc::tc_commit(&k_empty[j & 1]);
         if (j >= 1 && !issue_pv(j - 1)) ok = false;
       }
       if (ok && ntiles > 0 && !issue_pv(ntiles - 1)) ok = false;
@@ -259,7 +281,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;           // query row in the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int pos = g.past + q0 + row;             // absolute position of the row
+    const int pos = g.past + q0 + row % g.np_;     // absolute position of the row
     float m_ref = -INFINITY, l_part = 0.0f;
     // scores are kept raw and scaled inside the exponent's FMA when the scale
     // is positive and there is no softcap; otherwise transformed up front
@@ -362,9 +384,9 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     const float l_sum = l_part + red[(half ^ 1) * PT_M + row];
     if (fin) {
       tc::tc_fence_after();
-      const int qrow = q0 + row;
+      const int qrow = q0 + row % g.np_;
       const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
-      T *yr = static_cast<T *>(g.y) + (int64_t)b * g.y_sb + (int64_t)h * g.y_sh +
+      T *yr = static_cast<T *>(g.y) + (int64_t)b * g.y_sb + (int64_t)(h0 + row / g.np_) * g.y_sh +
               (int64_t)qrow * g.y_ss + half * 64;
       uint32_t r[32];
 #pragma unroll 1
@@ -418,10 +440,17 @@ int attn_prefill_tc_launch(int dtype, const void *q, const int64_t *qs, const vo
   const CUtensorMapDataType tdt =
       dtype == kFloat16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const uint32_t box[4] = {64, 128, 1, 1};
+  // pk = query heads per CTA: the largest power of two up to 8 that divides
+  // the GQA group; the Q box is {64 dims, 128 / pk positions, pk heads}.
+  int pk = 1;
+  const int64_t group = Hq / Hkv;
+  while (pk < 8 && group % (2 * pk) == 0) pk *= 2;
+  const int np = PT_M / pk;
   {
     const uint64_t dims[4] = {(uint64_t)PT_D, (uint64_t)Sq, (uint64_t)Hq, (uint64_t)B};
     const uint64_t strides[3] = {(uint64_t)qs[2] * 2, (uint64_t)qs[1] * 2, (uint64_t)qs[0] * 2};
-    int rc = make_tensor_map(&map_q, tdt, 4, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    const uint32_t qbox[4] = {64, (uint32_t)np, (uint32_t)pk, 1};
+    int rc = make_tensor_map(&map_q, tdt, 4, q, dims, strides, qbox, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
   {
@@ -442,11 +471,14 @@ int attn_prefill_tc_launch(int dtype, const void *q, const int64_t *qs, const vo
   a.Sq = (int)Sq;
   a.L = (int)L;
   a.past = (int)past;
-  a.qtiles = (int)((Sq + PT_M - 1) / PT_M);
+  a.pk = pk;
+  a.np_ = np;
+  a.hpacks = (int)(Hq / pk);
+  a.qtiles = (int)((Sq + np - 1) / np);
   a.scale_log2 = scale * kLog2e;
   a.softcap = softcap;
   a.causal = causal;
-  const int64_t ctas = (int64_t)a.qtiles * B * Hq;
+  const int64_t ctas = (int64_t)a.qtiles * B * a.hpacks;
   if (ctas >= ((int64_t)1 << 31)) B2_FAIL(B2_ERR_UNSUPPORTED, "b2_attention: too many query tiles");
   auto kern = dtype == kFloat16 ? attn_prefill_tc<__half> : attn_prefill_tc<__nv_bfloat16>;
   B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PT_SMEM));
