@@ -130,6 +130,25 @@ B2_API int b2_dequantize_matmul_noalloc(const b2_tensor *a, const b2_tensor *w,
                                         void *stream);
 
 /*
+ * Bounded-wait time-outs recorded by the decode GEMV and attention kernels
+ * since the last reset: 0 when none, else the first code found (1: data never
+ * arrived, 2: a ring slot never freed, 3: an MMA never completed), with the
+ * kernel named in b2_last_error().  Synchronizes the device first; reset != 0
+ * clears the codes.  (The tensor-core GEMMs record theirs in the status word
+ * at the end of the workspace's counter region.)  No counterpart in
+ * onnx-light: its CPU kernels do not wait on other units of work.
+ */
+B2_API int b2_kernel_status(int reset);
+
+/*
+ * Self-test of the time-out path: one kernel thread waits on a barrier that
+ * nothing completes, gives up after limit_ns (at most 2 s) and records code 1;
+ * returns the code read back (1 when the path works).  Nothing faults or
+ * hangs; the context stays usable.  No counterpart in onnx-light.
+ */
+B2_API int b2_selftest_bounded_wait(int64_t limit_ns, void *stream);
+
+/*
  * MatMulInteger: y[i,j] = sum_k (a[i,k] - a_zp[i]) * (b[k,j] - b_zp[j]) in
  * int32, bit-exact.
  * Replaces kernel::MatMulInteger::operator()(a, b, a_zero_point, b_zero_point,

@@ -453,3 +453,17 @@ int attn_decode_launch(const void *q, int64_t q_sb, int64_t q_sh, const void *kc
 }
 
 } // namespace b2
+
+namespace b2 {
+// Host: the time-out code this file's kernels recorded (0: none); reset != 0
+// clears it.  Synchronous (the copy waits for the device).
+int status_read_attn_decode(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_attn_decode_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_attn_decode_status, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+} // namespace b2

@@ -360,3 +360,17 @@ int attn_prefill_launch(int dtype, const void *q, const int64_t *qs, const void 
 }
 
 } // namespace b2
+
+namespace b2 {
+// Host: the time-out code this file's kernels recorded (0: none); reset != 0
+// clears it.  Synchronous (the copy waits for the device).
+int status_read_attn_prefill(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_attn_prefill_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_attn_prefill_status, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+} // namespace b2

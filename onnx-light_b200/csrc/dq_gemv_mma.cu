@@ -650,3 +650,17 @@ int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
 }
 
 } // namespace b2
+
+namespace b2 {
+// Host: the time-out code this file's kernels recorded (0: none); reset != 0
+// clears it.  Synchronous (the copy waits for the device).
+int status_read_gemv_mma(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemv_mma_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_gemv_mma_status, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+} // namespace b2

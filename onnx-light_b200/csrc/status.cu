@@ -1,0 +1,75 @@
+// Surfacing of the kernels' bounded-wait time-outs to the host.
+//
+// Every spin-wait in the device code (mbarrier waits on TMA loads, on MMA
+// commits, on other warps) gives up after a wall-clock limit; the kernel then
+// records a code (1 data never arrived, 2 a ring slot never freed, 3 an MMA
+// never completed) in a status word, skips the rest of its work, frees its
+// TMEM and returns, so the context stays usable.  The decode GEMV and the
+// attention kernels keep that word in device memory of their own; the
+// tensor-core GEMMs keep it at a fixed offset of the caller's workspace.
+// b2_kernel_status() reads the device words; b2_selftest_bounded_wait()
+// makes one wait run out on purpose to check the whole path.
+#include "b2_common.cuh"
+#include "tc_common.cuh"
+
+namespace b2 {
+
+int status_read_gemv_mma(int reset);
+int status_read_attn_decode(int reset);
+int status_read_attn_prefill(int reset);
+int status_read_attn_prefill_tc(int reset);
+
+__device__ int g_selftest_status;
+
+namespace {
+
+// One thread waits on a barrier that nothing completes, gives up after
+// limit_ns and records code 1 (data never arrived).
+__global__ void selftest_bounded_wait(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  tc::mbar_init(&bar, 1);
+  tc::fence_barrier_init();
+  if (!tc::mbar_wait(&bar, 0, limit_ns)) atomicExch(&g_selftest_status, tc::kTimeoutFull);
+}
+
+} // namespace
+
+} // namespace b2
+
+using namespace b2;
+
+extern "C" B2_API int b2_kernel_status(int reset) {
+  B2_CUDA(cudaDeviceSynchronize());
+  struct Src { const char *name; int (*read)(int); };
+  const Src srcs[] = {{"dq_gemv_mma", status_read_gemv_mma},
+                      {"attn_decode_mma", status_read_attn_decode},
+                      {"attn_prefill_mma", status_read_attn_prefill},
+                      {"attn_prefill_tc", status_read_attn_prefill_tc}};
+  int first = 0;
+  for (const Src &s : srcs) {
+    const int v = s.read(reset);
+    if (v < 0) B2_FAIL(B2_ERR_CUDA, "b2_kernel_status: reading the status of %s failed", s.name);
+    if (v && !first) {
+      first = v;
+      set_error(B2_OK, "%s: a bounded wait timed out (code %d: %s)", s.name, v,
+                v == tc::kTimeoutFull ? "data never arrived"
+                : v == tc::kTimeoutEmpty ? "a ring slot never freed" : "an MMA never completed");
+    }
+  }
+  return first;
+}
+
+extern "C" B2_API int b2_selftest_bounded_wait(int64_t limit_ns, void *stream) {
+  if (limit_ns <= 0 || limit_ns > 2000000000ll)
+    B2_FAIL(B2_ERR_INVALID_ARGUMENT, "b2_selftest_bounded_wait: limit must be in (0, 2 s]");
+  const int z = 0;
+  B2_CUDA(cudaMemcpyToSymbol(g_selftest_status, &z, sizeof(int)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  selftest_bounded_wait<<<1, 32, 0, st>>>((uint64_t)limit_ns);
+  B2_LAUNCH_CHECK();
+  B2_CUDA(cudaStreamSynchronize(st));
+  int v = 0;
+  B2_CUDA(cudaMemcpyFromSymbol(&v, g_selftest_status, sizeof(int)));
+  return v;
+}

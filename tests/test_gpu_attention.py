@@ -1,6 +1,8 @@
 """Opset-23 Attention on the GPU: against onnx-light's own outputs (fixtures)
 and the oracle, GQA, causal, softcap, masks, rank-3 inputs, and the contiguous
 KV cache with in-place append.  Tolerance: rel-L2 <= 1e-3 (fp16/bf16)."""
+import ctypes as C
+
 import numpy as np
 import pytest
 import torch
@@ -277,3 +279,20 @@ def test_prefill_tcgen05_matches_mma_sync_and_is_deterministic(b2, cuda, monkeyp
     torch.cuda.synchronize()
     assert np.array_equal(y1, y2)
     assert rel_l2(y1, y3) <= 1e-3
+
+
+# ---------------------------------------------------------------------------
+# Bounded waits: a wait that runs out records a code the host reads back.
+# ---------------------------------------------------------------------------
+
+def test_bounded_wait_times_out_and_reports(b2, cuda):
+    """One kernel thread waits 10 ms on a barrier nothing completes: it gives up,
+    records code 1, and the context stays usable for the next call."""
+    from onnx_light_b200 import _capi
+    lib = _capi.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.b2_selftest_bounded_wait(10_000_000, C.c_void_p(stream)) == 1
+    # the kernels of the tests above finished without any time-out
+    assert lib.b2_kernel_status(1) == 0
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum()) == 8.0
