@@ -148,7 +148,7 @@ __device__ __forceinline__ void store_val(const DqMmParams &p, int64_t m, int64_
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(DT_THREADS, 1)
+__global__ void __launch_bounds__(DT_THREADS, MODE == kModePre ? 1 : 2)
     dq_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_s, const DqTcArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -490,15 +490,18 @@ static TcPlan tc_plan(const DqMmParams &p) {
   t.s_bytes = (uint32_t)t.s_rows * DT_BM * s_esz;
   t.stage_bytes = DT_AOP_BYTES + t.b_bytes + t.raw_bytes + t.s_bytes;
   t.stage_bytes = (t.stage_bytes + 1023) & ~1023u;
-  const size_t budget = 220 * 1024;
+  // Decode-range batches run two CTAs per SM (about 100 KB of ring each), so
+  // two sets of dequantizing warps share an SM and split-K fills both slots;
+  // the prefill (pre-dequantized) GEMM keeps one CTA with a deep ring.
+  const size_t budget = t.pre ? 220 * 1024 : 100 * 1024;
   t.stages = (int)std::min<size_t>(6, budget / t.stage_bytes);
   t.smem = (size_t)t.stages * t.stage_bytes + 1024 + 256;
   const int64_t ntiles = (p.N + DT_BM - 1) / DT_BM, mtiles = (p.M + t.bn - 1) / t.bn;
   const int sms = sm_count();
   int64_t split = 1;
-  if (ntiles * mtiles < sms && ntiles * mtiles <= (int64_t)kMaxCounters) {
+  if (ntiles * mtiles < 2 * sms && ntiles * mtiles <= (int64_t)kMaxCounters) {
     // one CTA per SM (the ring takes most of shared memory): stay within one wave
-    split = sms / (ntiles * mtiles);
+    split = (t.pre ? 1 : 2) * sms / (ntiles * mtiles);
     const int64_t maxsplit = (p.K + 4 * DT_BK - 1) / (4 * DT_BK); // >= 4 stages per split
     if (split > maxsplit) split = maxsplit;
     if (split < 1) split = 1;
