@@ -120,9 +120,10 @@ B2_API int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w, const b2
  * that loads it until the process exits.  Calls whose plan needs more are
  * rejected with B2_ERR_WORKSPACE.  All calls on a device share that array, so
  * calls that overlap on the GPU (other streams or host threads) race; calls
- * on one stream are safe.  The first call on each device resolves the array's
- * device address and should come before any stream capture.  Nothing is
- * allocated.
+ * on one stream are safe.  Every call resolves the array's device address on
+ * the current device; the first call on each device also loads the module
+ * there and should come before any stream capture.  Time-outs of its kernels
+ * are reported by b2_kernel_status().  Nothing is allocated.
  */
 B2_API int b2_dequantize_matmul_noalloc(const b2_tensor *a, const b2_tensor *w,
                                         const b2_tensor *w_scale, const b2_tensor *w_zero_point,
@@ -130,13 +131,15 @@ B2_API int b2_dequantize_matmul_noalloc(const b2_tensor *a, const b2_tensor *w,
                                         void *stream);
 
 /*
- * Bounded-wait time-outs recorded by the decode GEMV and attention kernels
- * since the last reset: 0 when none, else the first code found (1: data never
- * arrived, 2: a ring slot never freed, 3: an MMA never completed), with the
- * kernel named in b2_last_error().  Synchronizes the device first; reset != 0
- * clears the codes.  (The tensor-core GEMMs record theirs in the status word
- * at the end of the workspace's counter region.)  No counterpart in
- * onnx-light: its CPU kernels do not wait on other units of work.
+ * Bounded-wait time-outs recorded by any kernel of this library since the
+ * last reset (decode GEMVs, tensor-core GEMMs, MatMulInteger, attention): 0
+ * when none, else the first code found (1: data never arrived, 2: a ring slot
+ * never freed, 3: an MMA never completed), with the kernel named in
+ * b2_last_error().  A call whose kernel gave up leaves its output unwritten
+ * (or partly written) and is reported only here.  The codes live in device
+ * words of the library, never in a caller's workspace.  Synchronizes the
+ * device first; reset != 0 clears the codes.  No counterpart in onnx-light:
+ * its CPU kernels do not wait on other units of work.
  */
 B2_API int b2_kernel_status(int reset);
 
@@ -147,6 +150,23 @@ B2_API int b2_kernel_status(int reset);
  * hangs; the context stays usable.  No counterpart in onnx-light.
  */
 B2_API int b2_selftest_bounded_wait(int64_t limit_ns, void *stream);
+
+/*
+ * Self-test of the tensor-core dequant GEMM's time-out path, on a real call:
+ * b2_dequantize_matmul's tcgen05 plan for (a, w, w_scale, y) is launched with
+ * no data loads issued, so the first data wait of every CTA runs out after
+ * limit_ns (at most 2 s).  Each CTA records code 1, arrives on its split-K
+ * counter with a give-up mark (the last one resets the counter and skips the
+ * merge) and returns; y is left unwritten.  The workspace (capacity
+ * workspace_bytes) must satisfy b2_dequantize_matmul's size query for the same
+ * tensors; its counters are zero again afterwards, so a following
+ * b2_dequantize_matmul on it computes the right result.  Returns the code read
+ * back (1 when the path works), which b2_kernel_status() then also reports.
+ * Nothing faults or hangs.  No counterpart in onnx-light.
+ */
+B2_API int b2_selftest_gemm_timeout(const b2_tensor *a, const b2_tensor *w,
+                                    const b2_tensor *w_scale, b2_tensor *y, void *workspace,
+                                    size_t workspace_bytes, int64_t limit_ns, void *stream);
 
 /*
  * MatMulInteger: y[i,j] = sum_k (a[i,k] - a_zp[i]) * (b[k,j] - b_zp[j]) in

@@ -43,7 +43,7 @@ ONNX_TO_TORCH = {FLOAT: torch.float32, FLOAT16: torch.float16, BFLOAT16: torch.b
 # Every symbol the header declares (checked by the CPU tests).
 EXPORTS = ("b2_version", "b2_last_error", "b2_dequantize_linear", "b2_dequantize_matmul",
            "b2_dequantize_matmul_noalloc", "b2_matmul_integer", "b2_qlinear_matmul", "b2_attention", "b2_synth_fill",
-           "b2_convert", "b2_kernel_status", "b2_selftest_bounded_wait")
+           "b2_convert", "b2_kernel_status", "b2_selftest_bounded_wait", "b2_selftest_gemm_timeout")
 
 
 class B2Tensor(C.Structure):
@@ -102,6 +102,8 @@ def lib() -> C.CDLL:
                 L.b2_convert.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int64, P]
                 L.b2_kernel_status.argtypes = [C.c_int]
                 L.b2_selftest_bounded_wait.argtypes = [C.c_int64, P]
+                L.b2_selftest_gemm_timeout.argtypes = [T, T, T, T, P, C.c_size_t, C.c_int64, P]
+                L.b2_dequantize_matmul_noalloc.argtypes = [T, T, T, T, C.c_int64, C.c_int32, T, P]
                 _lib = L
     return _lib
 

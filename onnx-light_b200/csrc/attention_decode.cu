@@ -354,10 +354,13 @@ __global__ void __launch_bounds__(AD_THREADS, 1)
     if (!whole) {
       consumers_sync();
       if (threadIdx.x == 0) {
-        const uint32_t prev = atom_add_acq_rel(g.counters + pair, 1u);
-        const bool last = prev + 1 == (uint32_t)(cl - cf + 1);
+        // A CTA whose wait gave up arrives with kAbortMark, and then the last
+        // one does not merge (the partials are not all valid).
+        const uint32_t inc = flags[0] ? kAbortMark + 1u : 1u;
+        const uint32_t now = atom_add_acq_rel(g.counters + pair, inc) + inc;
+        const bool last = (now & (kAbortMark - 1u)) == (uint32_t)(cl - cf + 1);
         if (last) g.counters[pair] = 0u;
-        flags[1] = last ? 1 : 0;
+        flags[1] = last && (now >> 16) == 0u ? 1 : 0;
       }
       consumers_sync();
       if (flags[1] && ok) {

@@ -108,11 +108,36 @@ inline const char *dtype_name(int dt) {
 // kernel ever writes anything else there, so the region stays all-zero across
 // calls of any shape.  Per-call partial results follow the counter region.
 constexpr size_t kCounterBytes = 64 * 1024;
-// The last 16 bytes of the counter region hold a status word that a bounded
-// device-side wait sets when it gives up (0 = no error); counters stop short
-// of it.
+// The last 16 bytes of the counter region are reserved (no kernel writes
+// there); counters stop short of them.  Time-out codes live in per-kernel
+// device words that b2_kernel_status() reads, never in the caller's workspace.
 constexpr size_t kStatusOffset = kCounterBytes - 16;
 constexpr size_t kMaxCounters = kStatusOffset / 4;
+
+// Wall-clock limit of a bounded device-side wait (mbarrier, arrival flag).
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+// Split-K arrival with a give-up mark.  Every contributor of a tile adds 1 to
+// the tile's counter, plus kAbortMark when a bounded wait of its own gave up
+// (its partial sums are then not valid).  The contributor whose arrival
+// completes the count is the last; it resets the counter to zero, so the
+// counters stay all-zero across calls even after a time-out, and it learns
+// whether any contributor gave up (then it must not merge).  Called by one
+// thread, after the caller's own partial stores are ordered before it.
+constexpr uint32_t kAbortMark = 1u << 16;
+__device__ __forceinline__ bool arrive_marked(uint32_t *counter, uint32_t expected, bool gave_up,
+                                              bool *any_gave_up) {
+  __threadfence();
+  const uint32_t inc = gave_up ? kAbortMark + 1u : 1u;
+  const uint32_t now = atomicAdd(counter, inc) + inc;
+  const bool last = (now & (kAbortMark - 1u)) == expected;
+  if (last) {
+    __threadfence();
+    *counter = 0u;
+  }
+  *any_gave_up = (now >> 16) != 0u;
+  return last;
+}
 
 // Workspace protocol shared by every entry point that needs scratch.
 // Returns 1 when the call is a size query (workspace == NULL), 0 when the

@@ -48,8 +48,13 @@ struct DqTcArgs {
   int s_rows;           // scale rows per stage
   int op_bf16;          // MMA operand type: 1 bf16, 0 f16
   int group_m;          // activation tiles per rasterization group (1: plain order)
-  int *status;
+  uint64_t wait_ns;     // limit of every bounded wait (kWaitNs)
+  int no_loads;         // self-test only: issue no TMA, so the first data wait runs out
 };
+
+// Time-out code of the last launch that gave up (0 = none); read and cleared
+// by b2_kernel_status().
+__device__ int g_dq_gemm_tc_status;
 
 // Packs two fp32 values into fp16x2 / bf16x2 bits with the reference's RNE.
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
@@ -162,7 +167,8 @@ __global__ void __launch_bounds__(DT_THREADS, MODE == kModePre ? 1 : 2)
   uint64_t *done = empty + S;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
   __shared__ volatile int abort_flag;
-  __shared__ bool last_cta;
+  __shared__ int issued; // stages the producer filled (for the drain after a give-up)
+  __shared__ bool last_cta, skip_merge;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Grouped rasterization: CTAs in launch order cover group_m activation
   // tiles across every weight tile before the next group, so a wave's tiles
@@ -187,6 +193,7 @@ __global__ void __launch_bounds__(DT_THREADS, MODE == kModePre ? 1 : 2)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
+    issued = 0;
     for (int s = 0; s < S; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&deq[s], DT_PROD_WARPS);
@@ -209,13 +216,15 @@ __global__ void __launch_bounds__(DT_THREADS, MODE == kModePre ? 1 : 2)
       tc::prefetch_tensormap(&map_w);
       tc::prefetch_tensormap(&map_a);
       if (args.s_bytes) tc::prefetch_tensormap(&map_s);
-      for (int kt = 0; kt < kt_count; ++kt) {
+      for (int kt = 0; kt < (args.no_loads ? 0 : kt_count); ++kt) {
         const int s = kt % S;
-        if (kt >= S && !tc::mbar_wait(&empty[s], ((kt / S) - 1) & 1)) {
-          atomicExch(args.status, tc::kTimeoutEmpty);
+        if (kt >= S && !tc::mbar_wait(&empty[s], ((kt / S) - 1) & 1, args.wait_ns)) {
+          atomicExch(&g_dq_gemm_tc_status, tc::kTimeoutEmpty);
           abort_flag = 1;
           break;
         }
+        if (abort_flag) break;
+        issued = kt + 1;
         uint8_t *st = smem + (size_t)s * args.stage_bytes;
         const int32_t k = (int32_t)(kbeg + (int64_t)kt * DT_BK);
         if constexpr (MODE == kModePre) {
@@ -245,8 +254,8 @@ __global__ void __launch_bounds__(DT_THREADS, MODE == kModePre ? 1 : 2)
       const uint32_t id = tc::idesc(1, args.op_bf16, args.op_bf16, 1, 0, DT_BM, (uint32_t)args.bn);
       for (int kt = 0; kt < kt_count; ++kt) {
         const int s = kt % S;
-        if (!tc::mbar_wait(MODE == kModePre ? &full[s] : &deq[s], (kt / S) & 1)) {
-          atomicExch(args.status, tc::kTimeoutFull);
+        if (!tc::mbar_wait(MODE == kModePre ? &full[s] : &deq[s], (kt / S) & 1, args.wait_ns)) {
+          atomicExch(&g_dq_gemm_tc_status, tc::kTimeoutFull);
           abort_flag = 1;
           break;
         }
@@ -274,8 +283,8 @@ __global__ void __launch_bounds__(DT_THREADS, MODE == kModePre ? 1 : 2)
     const uint32_t raw_row_bytes = MODE == kModeF8 ? 128 : 64;
     for (int kt = 0; kt < (MODE == kModePre ? 0 : kt_count) && !abort_flag; ++kt) {
       const int s = kt % S;
-      if (!tc::mbar_wait(&full[s], (kt / S) & 1)) {
-        atomicExch(args.status, tc::kTimeoutFull);
+      if (!tc::mbar_wait(&full[s], (kt / S) & 1, args.wait_ns)) {
+        atomicExch(&g_dq_gemm_tc_status, tc::kTimeoutFull);
         abort_flag = 1;
         break;
       }
@@ -371,8 +380,11 @@ __global__ void __launch_bounds__(DT_THREADS, MODE == kModePre ? 1 : 2)
     // ----- epilogue (warps 2..5: one TMEM lane group each) -----
     if (warp < 6) {
       const int g = warp & 3; // TMEM lane group
-      const bool ok = tc::mbar_wait(done, 0, 4000000000ull);
-      if (!ok) atomicExch(args.status, tc::kTimeoutMma);
+      const bool ok = tc::mbar_wait(done, 0, 2 * args.wait_ns);
+      if (!ok) {
+        atomicExch(&g_dq_gemm_tc_status, tc::kTimeoutMma);
+        abort_flag = 1;
+      }
       tc::tc_fence_after();
       // MMA row -> weight column (the int4 path stores each 8-column chunk
       // in the order 0 4 1 5 2 6 3 7)
@@ -400,20 +412,24 @@ __global__ void __launch_bounds__(DT_THREADS, MODE == kModePre ? 1 : 2)
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) tc::tmem_dealloc(tmem, tmem_cols);
-  if (p.ksplit <= 1 || abort_flag) return;
-  // split-K: the last CTA of this output tile sums the partials in split order
+  if (abort_flag && threadIdx.x == 0) {
+    // A wait gave up: let this CTA's own copies in flight land before it
+    // exits (the last fill of each stage; bounded again).
+    const int n = issued;
+    for (int kt = n > S ? n - S : 0; kt < n; ++kt)
+      tc::mbar_wait(&full[kt % S], (kt / S) & 1, args.wait_ns / 4);
+  }
+  if (p.ksplit <= 1) return;
+  // split-K: the last CTA of this output tile sums the partials in split
+  // order, unless a contributor gave up (its partials are not valid)
   if (threadIdx.x == 0) {
-    __threadfence();
-    uint32_t *ctr = p.counters + (blockIdx.y * gridDim.x + blockIdx.x);
-    const uint32_t prev = atomicAdd(ctr, 1u);
-    last_cta = prev + 1 == (uint32_t)p.ksplit;
-    if (last_cta) {
-      __threadfence();
-      *ctr = 0u;
-    }
+    bool gave_up = false;
+    last_cta = arrive_marked(p.counters + (blockIdx.y * gridDim.x + blockIdx.x),
+                             (uint32_t)p.ksplit, abort_flag != 0, &gave_up);
+    skip_merge = gave_up;
   }
   __syncthreads();
-  if (!last_cta) return;
+  if (!last_cta || skip_merge) return;
   for (int e = threadIdx.x; e < DT_BM * args.bn; e += DT_THREADS) {
     const int64_t m = m0 + e / DT_BM, n = n0 + e % DT_BM;
     if (m >= p.M || n >= p.N) continue;
@@ -545,14 +561,16 @@ size_t dq_tc_workspace(const DqMmParams &p) {
   return ws;
 }
 
-int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st) {
+int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st, uint64_t wait_ns,
+                 bool no_loads) {
   const TcPlan t = tc_plan(pin);
   DqTcArgs a{};
   a.p = pin;
   a.p.kchunk = t.kchunk;
   a.p.ksplit = t.ksplit;
+  a.wait_ns = wait_ns;
+  a.no_loads = no_loads ? 1 : 0;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  a.status = reinterpret_cast<int *>(ws + kStatusOffset);
   uint16_t *w16 = t.pre ? reinterpret_cast<uint16_t *>(ws + kCounterBytes) : nullptr;
   const size_t pre_bytes = t.pre ? (((size_t)pin.K * pin.N * 2 + 1023) & ~(size_t)1023) : 0;
   if (t.ksplit > 1) {
@@ -641,6 +659,18 @@ int dq_tc_launch(const DqMmParams &pin, void *workspace, cudaStream_t st) {
   kern<<<t.grid, DT_THREADS, t.smem, st>>>(map_w, map_a, map_s, a);
   B2_LAUNCH_CHECK();
   return B2_OK;
+}
+
+int dq_tc_ksplit(const DqMmParams &p) { return tc_plan(p).ksplit; }
+
+int status_read_dq_gemm_tc(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dq_gemm_tc_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_dq_gemm_tc_status, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
 }
 
 } // namespace b2

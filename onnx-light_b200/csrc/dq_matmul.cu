@@ -89,6 +89,20 @@ __device__ __forceinline__ void store_out(void *y, int dt, int64_t i, float v) {
 // zero again for the next call.
 // ---------------------------------------------------------------------------
 
+// Time-out code of the last CUDA-core GEMV launch that gave up (0 = none);
+// read and cleared by b2_kernel_status().
+__device__ int g_dq_gemv_status;
+
+int status_read_dq_gemv(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dq_gemv_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_dq_gemv_status, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+
 __device__ __forceinline__ bool arrive_last(uint32_t *counter, int expected) {
   __shared__ bool last;
   __syncthreads(); // all partial stores of this CTA issued
@@ -423,10 +437,12 @@ __global__ void __launch_bounds__(GV_THREADS, MT == 1 ? 2 : 1)
   const int ntiles = (int)((klen + GV_ROWS - 1) / GV_ROWS);
   const int64_t kb0 = p.slayout == kScaleAxis0Block ? kbeg / p.block : 0;
   const int nrows_s = p.slayout == kScaleAxis0Block ? (int)((kend - 1) / p.block - kb0 + 1) : 1;
-  int *status = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(p.counters) + kStatusOffset);
+  int *status = &g_dq_gemv_status;
+  __shared__ int issued; // ring stages the producer filled (for the drain after a give-up)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
+    issued = 0;
     for (int i = 0; i < GV_STAGES; ++i) {
       tc::mbar_init(&full[i], 1);
       tc::mbar_init(&empty[i], GV_CONSUMERS / 32);
@@ -473,6 +489,8 @@ __global__ void __launch_bounds__(GV_THREADS, MT == 1 ? 2 : 1)
           abort_flag = 1;
           break;
         }
+        if (abort_flag) break;
+        issued = t + 1;
         tc::mbar_expect_tx(&full[s], GV_STAGE_BYTES);
         tc::tma_load_2d(ring + s * GV_STAGE_BYTES, &map_w, &full[s], (int32_t)(n0 / 2),
                         (int32_t)(kbeg + (int64_t)t * GV_ROWS));
@@ -562,6 +580,15 @@ __global__ void __launch_bounds__(GV_THREADS, MT == 1 ? 2 : 1)
         acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], 16);
       }
   }
+  __syncthreads();
+  if (abort_flag && threadIdx.x == 0) {
+    // A wait gave up: let the copies in flight (scale rows, the last fill of
+    // each ring stage) land before the ring is reused or the CTA exits.
+    tc::mbar_wait(sbar, 0, kWaitNs / 4);
+    const int n = issued;
+    for (int t = n > GV_STAGES ? n - GV_STAGES : 0; t < n; ++t)
+      tc::mbar_wait(&full[t % GV_STAGES], (t / GV_STAGES) & 1, kWaitNs / 4);
+  }
   __syncthreads(); // the ring is free: reuse it for the cross-warp reduction
   if (warp < GV_CONSUMERS / 32 && r == 0) {
 #pragma unroll
@@ -582,8 +609,17 @@ __global__ void __launch_bounds__(GV_THREADS, MT == 1 ? 2 : 1)
       else store_out(p.y, p.ydt, (int64_t)m * p.N + gn, sum);
     }
   }
-  if (!part || abort_flag) return;
-  if (!arrive_last(p.counters + blockIdx.x, p.ksplit)) return;
+  if (!part) return;
+  // Last contributor merges, unless one of them gave up (partials not valid).
+  __shared__ bool gv_last, gv_skip;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    bool gave_up = false;
+    gv_last = arrive_marked(p.counters + blockIdx.x, (uint32_t)p.ksplit, abort_flag != 0, &gave_up);
+    gv_skip = gave_up;
+  }
+  __syncthreads();
+  if (!gv_last || gv_skip) return;
   for (int e = threadIdx.x; e < MT * GEMV_TN; e += GV_THREADS) {
     const int m = e / GEMV_TN;
     const int64_t gn = n0 + e % GEMV_TN;
@@ -854,4 +890,35 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
   if (p.ydt == kFloat) return launch_simt<float>(p, pl, st);
   if (p.ydt == kFloat16) return launch_simt<__half>(p, pl, st);
   return launch_simt<__nv_bfloat16>(p, pl, st);
+}
+
+// Self-test of the tensor-core GEMM's time-out path (see the header): the
+// planned dq_gemm_tc launch runs with no TMA issued, so its first data wait
+// runs out after limit_ns; every CTA gives up, arrives on its split-K counter
+// with the give-up mark and returns.  Returns the code the kernel recorded.
+extern "C" int b2_selftest_gemm_timeout(const b2_tensor *a, const b2_tensor *w,
+                                        const b2_tensor *w_scale, b2_tensor *y, void *workspace,
+                                        size_t workspace_bytes, int64_t limit_ns, void *stream) {
+  if (limit_ns <= 0 || limit_ns > 2000000000ll)
+    B2_FAIL(B2_ERR_INVALID_ARGUMENT, "b2_selftest_gemm_timeout: limit must be in (0, 2 s]");
+  DqMmParams p{};
+  int rc = dq_mm_validate(a, w, w_scale, nullptr, 0, 0, y, p);
+  if (rc) return rc;
+  if (!dq_tc_eligible(p) || p.M == 0 || p.N == 0 || p.K == 0)
+    B2_FAIL(B2_ERR_UNSUPPORTED, "b2_selftest_gemm_timeout: the tensor-core GEMM does not take this shape");
+  const size_t need = dq_tc_workspace(p);
+  if (workspace == nullptr || workspace_bytes < need)
+    B2_FAIL(B2_ERR_WORKSPACE, "b2_selftest_gemm_timeout: workspace of %zu bytes required", need);
+  p.a = a->data;
+  p.w = static_cast<const uint8_t *>(w->data);
+  p.scale = static_cast<const uint8_t *>(w_scale->data);
+  p.y = y->data;
+  if (status_read_dq_gemm_tc(1) < 0) B2_FAIL(B2_ERR_CUDA, "b2_selftest_gemm_timeout: status reset failed");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = dq_tc_launch(p, workspace, st, (uint64_t)limit_ns, true);
+  if (rc) return rc;
+  B2_CUDA(cudaStreamSynchronize(st));
+  const int v = status_read_dq_gemm_tc(0);
+  if (v < 0) B2_FAIL(B2_ERR_CUDA, "b2_selftest_gemm_timeout: status read failed");
+  return v;
 }

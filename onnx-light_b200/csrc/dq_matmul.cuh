@@ -39,7 +39,12 @@ struct DqMmParams {
 bool dq_tc_eligible(const DqMmParams &p);  // shape/type constraints only
 bool dq_tc_supported(const DqMmParams &p); // eligible and chosen by default
 size_t dq_tc_workspace(const DqMmParams &p);
-int dq_tc_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
+// wait_ns bounds every device-side wait; no_loads (self-test only) issues no
+// TMA, so the first data wait runs out and the time-out path runs.
+int dq_tc_launch(const DqMmParams &p, void *workspace, cudaStream_t stream,
+                 uint64_t wait_ns = kWaitNs, bool no_loads = false);
+int dq_tc_ksplit(const DqMmParams &p); // split-K factor of the plan
+int status_read_dq_gemm_tc(int reset); // time-out word of dq_gemm_tc (-1: read failed)
 
 // Decode path on register-level MMA (dq_gemv_mma.cu): M <= 16, INT4/UINT4
 // weights, FLOAT16 scales, activations and output.

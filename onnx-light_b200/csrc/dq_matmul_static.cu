@@ -16,13 +16,15 @@
 //    cleared on each call, partial sums from the previous call are simply
 //    overwritten, and two calls that overlap on the GPU (different streams,
 //    or different host threads on one device) race on it;
-//  * the first call on each device looks the array's device address up with
-//    cudaGetSymbolAddress (the host-side name of a __device__ array is not a
-//    device address); make that first call before any stream capture;
+//  * each call looks the array's device address up with cudaGetSymbolAddress
+//    on the current device (the host-side name of a __device__ array is not a
+//    device address); the first lookup on a device loads the module there, so
+//    make the first call on each device before any stream capture;
+//  * a kernel whose bounded wait gave up reports it through
+//    b2_kernel_status() (device words of the library, outside this array), so
+//    the per-call clearing of the counters never hides a time-out;
 //  * nothing here allocates: no cudaMalloc, no cudaFree, no library allocator.
 #include "dq_matmul.cuh"
-
-#include <mutex>
 
 namespace b2 {
 
@@ -30,22 +32,15 @@ constexpr size_t kStaticScratchBytes = size_t(8) << 20;
 
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
-// Device address of g_static_scratch on the current device, looked up once
-// per device (with that device current) and cached.
+// Device address of g_static_scratch on the current device, looked up on
+// every call with that device current: the lookup is cheap, and an address
+// cached across calls would go stale after cudaDeviceReset or with a new
+// primary context.
 static int static_scratch(void **out) {
-  static std::mutex mu;
-  static void *addr[64] = {nullptr};
-  int dev = 0;
-  B2_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) B2_FAIL(B2_ERR_CUDA, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void *p = nullptr;
-    B2_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
-    if (p == nullptr) B2_FAIL(B2_ERR_CUDA, "cudaGetSymbolAddress returned a null address");
-    addr[dev] = p;
-  }
-  *out = addr[dev];
+  void *p = nullptr;
+  B2_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+  if (p == nullptr) B2_FAIL(B2_ERR_CUDA, "cudaGetSymbolAddress returned a null address");
+  *out = p;
   return B2_OK;
 }
 

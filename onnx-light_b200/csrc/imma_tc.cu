@@ -20,7 +20,8 @@
 //   warps 2-5  read the accumulator tile from TMEM (tcgen05.ld 32x32b) and
 //              write y.
 // Every wait is bounded; a wait that gives up records the failure in the
-// workspace status word and the CTA skips the rest of its work.
+// device word g_imma_tc_status (read by b2_kernel_status) and the CTA skips
+// the rest of its work, after letting its own copies in flight land.
 #include "imma.cuh"
 #include "tc_common.cuh"
 
@@ -40,8 +41,11 @@ struct ImmaTcArgs {
   const int32_t *rowsum; // [M] sum_k a'
   const int32_t *colsum; // [N] sum_k b, written only when some za' != 0
   uint8_t *a_shift;      // workspace copy of a' (UINT8 A only)
-  int *status;
 };
+
+// Time-out code of the last launch that gave up (0 = none); read and cleared
+// by b2_kernel_status().
+__device__ int g_imma_tc_status;
 
 __device__ __forceinline__ int32_t zp_shifted(const ImmaParams &p, int64_t m) {
   const int32_t za = p.a_zp ? rd_byte(p.adt, p.a_zp, p.a_zp_n > 1 ? m : 0) : 0;
@@ -162,7 +166,8 @@ __global__ void __launch_bounds__(IT_THREADS, 2)
   uint64_t *empty = full + IT_STAGES;
   uint64_t *done = empty + IT_STAGES;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
-  __shared__ int abort_flag;
+  __shared__ volatile int abort_flag;
+  __shared__ int issued; // k stages the producer filled (for the drain after a give-up)
   const ImmaParams &p = args.p;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tile = blockIdx.x, n_tile = blockIdx.y;
@@ -170,6 +175,7 @@ __global__ void __launch_bounds__(IT_THREADS, 2)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
+    issued = 0;
     for (int s = 0; s < IT_STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
@@ -193,10 +199,12 @@ __global__ void __launch_bounds__(IT_THREADS, 2)
       for (int kt = 0; kt < kt_count; ++kt) {
         const int s = kt % IT_STAGES;
         if (kt >= IT_STAGES && !tc::mbar_wait(&empty[s], ((kt / IT_STAGES) - 1) & 1)) {
-          atomicExch(args.status, tc::kTimeoutEmpty);
+          atomicExch(&g_imma_tc_status, tc::kTimeoutEmpty);
           abort_flag = 1;
           break;
         }
+        if (abort_flag) break;
+        issued = kt + 1;
         uint8_t *st = smem + s * IT_STAGE_BYTES;
         tc::mbar_expect_tx(&full[s], IT_STAGE_BYTES);
         tc::tma_load_2d(st, &map_a, &full[s], kt * IT_BK, m_tile * IT_BM);
@@ -214,7 +222,7 @@ __global__ void __launch_bounds__(IT_THREADS, 2)
       for (; kt < kt_count; ++kt) {
         const int s = kt % IT_STAGES;
         if (!tc::mbar_wait(&full[s], (kt / IT_STAGES) & 1)) {
-          atomicExch(args.status, tc::kTimeoutFull);
+          atomicExch(&g_imma_tc_status, tc::kTimeoutFull);
           abort_flag = 1;
           break;
         }
@@ -234,8 +242,11 @@ __global__ void __launch_bounds__(IT_THREADS, 2)
   } else {
     // epilogue warps 2..5 -> TMEM lane groups 2, 3, 0, 1
     const int g = warp & 3;
-    const bool ok = tc::mbar_wait(done, 0, 4000000000ull);
-    if (!ok) atomicExch(args.status, tc::kTimeoutMma);
+    const bool ok = tc::mbar_wait(done, 0, 2 * kWaitNs);
+    if (!ok) {
+      atomicExch(&g_imma_tc_status, tc::kTimeoutMma);
+      abort_flag = 1;
+    }
     tc::tc_fence_after();
     const int64_t m = (int64_t)m_tile * IT_BM + g * 32 + lane;
     if (ok && !abort_flag) {
@@ -252,6 +263,13 @@ __global__ void __launch_bounds__(IT_THREADS, 2)
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) tc::tmem_dealloc(tmem, 256);
+  if (abort_flag && threadIdx.x == 0) {
+    // A wait gave up: let this CTA's own copies in flight land before it
+    // exits (the last fill of each stage; bounded again).
+    const int n = issued;
+    for (int kt = n > IT_STAGES ? n - IT_STAGES : 0; kt < n; ++kt)
+      tc::mbar_wait(&full[kt % IT_STAGES], (kt / IT_STAGES) & 1, kWaitNs / 4);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -276,7 +294,6 @@ int imma_tc_launch(const ImmaParams &p, void *workspace, cudaStream_t st) {
   ImmaTcArgs args{};
   args.p = p;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  args.status = reinterpret_cast<int *>(ws + kStatusOffset);
   size_t off = kCounterBytes;
   if (p.adt == kUint8) {
     args.a_shift = ws + off;
@@ -316,6 +333,16 @@ int imma_tc_launch(const ImmaParams &p, void *workspace, cudaStream_t st) {
   imma_tc_kernel<<<grid, IT_THREADS, IT_SMEM, st>>>(map_a, map_b, args);
   B2_LAUNCH_CHECK();
   return B2_OK;
+}
+
+int status_read_imma_tc(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_imma_tc_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_imma_tc_status, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
 }
 
 } // namespace b2

@@ -3,12 +3,14 @@
 // Every spin-wait in the device code (mbarrier waits on TMA loads, on MMA
 // commits, on other warps) gives up after a wall-clock limit; the kernel then
 // records a code (1 data never arrived, 2 a ring slot never freed, 3 an MMA
-// never completed) in a status word, skips the rest of its work, frees its
-// TMEM and returns, so the context stays usable.  The decode GEMV and the
-// attention kernels keep that word in device memory of their own; the
-// tensor-core GEMMs keep it at a fixed offset of the caller's workspace.
-// b2_kernel_status() reads the device words; b2_selftest_bounded_wait()
-// makes one wait run out on purpose to check the whole path.
+// never completed) in a device word of its own, skips the rest of its work,
+// lets its own copies in flight land, frees its TMEM and returns, so the
+// context stays usable.  A split-K contributor that gave up still arrives on
+// its tile's counter (with a give-up mark), so the counters return to zero
+// and the last contributor does not merge invalid partial sums.
+// b2_kernel_status() reads every kernel's word; b2_selftest_bounded_wait()
+// and b2_selftest_gemm_timeout() make a wait run out on purpose to check the
+// whole path.
 #include "b2_common.cuh"
 #include "tc_common.cuh"
 
@@ -18,6 +20,9 @@ int status_read_gemv_mma(int reset);
 int status_read_attn_decode(int reset);
 int status_read_attn_prefill(int reset);
 int status_read_attn_prefill_tc(int reset);
+int status_read_dq_gemm_tc(int reset);
+int status_read_imma_tc(int reset);
+int status_read_dq_gemv(int reset);
 
 __device__ int g_selftest_status;
 
@@ -45,7 +50,10 @@ extern "C" B2_API int b2_kernel_status(int reset) {
   const Src srcs[] = {{"dq_gemv_mma", status_read_gemv_mma},
                       {"attn_decode_mma", status_read_attn_decode},
                       {"attn_prefill_mma", status_read_attn_prefill},
-                      {"attn_prefill_tc", status_read_attn_prefill_tc}};
+                      {"attn_prefill_tc", status_read_attn_prefill_tc},
+                      {"dq_gemm_tc", status_read_dq_gemm_tc},
+                      {"imma_tc", status_read_imma_tc},
+                      {"dq_gemv_i4h", status_read_dq_gemv}};
   int first = 0;
   for (const Src &s : srcs) {
     const int v = s.read(reset);

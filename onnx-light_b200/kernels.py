@@ -52,18 +52,28 @@ def _ref(d: Optional[Desc]):
 
 
 # ---------------------------------------------------------------------------
-# Workspace: one zero-initialised buffer per device, grown on demand.  The
-# kernels return their split-K counters to zero, so the buffer stays valid.
+# Workspace: one zero-initialised buffer per (device, stream), grown on
+# demand.  The kernels return their split-K counters to zero, so a buffer
+# stays valid from call to call.  Keying by stream keeps the header's rule
+# that calls sharing a workspace must not overlap on the GPU: calls on one
+# stream are ordered, calls on two streams get two buffers.  A buffer is
+# allocated with its stream current, so when a larger one replaces it, torch's
+# caching allocator hands the old memory out again only to later work on that
+# same stream, never while a kernel queued before the swap still reads it.
 # ---------------------------------------------------------------------------
 
 _workspaces: dict = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+def workspace(device: torch.device, nbytes: int, stream=None) -> torch.Tensor:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if stream is None:
+        stream = torch.cuda.current_stream(index)
+    key = (index, stream.cuda_stream)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        with torch.cuda.stream(stream):
+            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf
 

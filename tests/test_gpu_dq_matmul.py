@@ -259,3 +259,60 @@ def test_prefill_predequantized_gemm(b2, cuda, wdt, s_dt, act, block, zp, cast):
     y, ref = run_case(b2, 2304, 320, 200, wdt, s_dt, act, axis=0, block=block, zp=zp, cast=cast,
                       seed=17)
     assert rel_l2(y, ref) <= TOL[act], rel_l2(y, ref)
+
+
+# ---------------------------------------------------------------------------
+# Failure detection: a tensor-core GEMM whose bounded wait runs out reports
+# it, and leaves the caller's workspace valid for the next call.
+# ---------------------------------------------------------------------------
+
+def test_gemm_timeout_is_reported_and_workspace_stays_valid(b2, cuda):
+    import ctypes as C
+    from onnx_light_b200 import _capi as capi
+    lib = capi.lib()
+    M, K, N = 32, 4096, 4096  # tensor-core plan, K split across CTAs
+    w = random_q(41, (K, N), O.INT4)
+    s = scale_raw(O.rand_uniform(42, (K // 128 * N,), 0.002, 0.02), O.FLOAT16)
+    a = O.f32_to_f16_bits(O.randn(43, (M, K)))
+    wq = O.dequantize_linear(w, O.INT4, (K, N), s, O.FLOAT16, (K // 128, N), None, None, 0)
+    ref = O.f16_bits_to_f32(O.matmul(a, wq, O.FLOAT16))
+    tw, ts, ta = to_dev(w), to_dev(s), to_dev(a)
+    y = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+    da = capi.Desc(ta.data_ptr(), capi.FLOAT16, (M, K))
+    dw = capi.Desc(tw.data_ptr(), capi.INT4, (K, N))
+    ds = capi.Desc(ts.data_ptr(), capi.FLOAT16, (K // 128, N))
+    dy = capi.Desc(y.data_ptr(), capi.FLOAT16, (M, N))
+    stream = capi.stream_ptr()
+    need = C.c_size_t(0)
+    capi.check(lib.b2_dequantize_matmul(da.ref, dw.ref, ds.ref, None, 0, 0, dy.ref, None,
+                                        C.byref(need), stream))
+    ws = torch.zeros(need.value, dtype=torch.uint8, device="cuda")
+    assert lib.b2_kernel_status(1) == 0
+    # every CTA's first data wait runs out after 10 ms: code 1 comes back
+    code = lib.b2_selftest_gemm_timeout(da.ref, dw.ref, ds.ref, dy.ref, C.c_void_p(ws.data_ptr()),
+                                        need.value, 10_000_000, stream)
+    assert code == 1
+    assert lib.b2_kernel_status(0) == 1
+    buf = C.create_string_buffer(256)
+    lib.b2_last_error(buf, 256)
+    assert b"dq_gemm_tc" in buf.value
+    assert lib.b2_kernel_status(1) == 1 and lib.b2_kernel_status(0) == 0
+    # the give-up arrivals returned every split-K counter to zero
+    assert int(ws[:65536].count_nonzero()) == 0
+    # so a real call on the same workspace computes the right result
+    cap = C.c_size_t(need.value)
+    capi.check(lib.b2_dequantize_matmul(da.ref, dw.ref, ds.ref, None, 0, 0, dy.ref,
+                                        C.c_void_p(ws.data_ptr()), C.byref(cap), stream))
+    torch.cuda.synchronize()
+    assert rel_l2(y.float().cpu().numpy(), ref) <= TOL[O.FLOAT16]
+    assert lib.b2_kernel_status(0) == 0
+
+
+def test_workspace_is_per_stream(b2, cuda):
+    """Calls on two streams get two workspaces (no shared split-K counters)."""
+    from onnx_light_b200 import kernels
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    w1 = kernels.workspace(torch.device("cuda", 0), 1 << 20, s1)
+    w2 = kernels.workspace(torch.device("cuda", 0), 1 << 20, s2)
+    assert w1.data_ptr() != w2.data_ptr()
+    assert kernels.workspace(torch.device("cuda", 0), 1 << 20, s1).data_ptr() == w1.data_ptr()
