@@ -198,7 +198,7 @@ typedef struct b2_attention_attrs {
   float scale;
   int32_t is_causal;
   float softcap;            /* > 0: softcap * tanh(s / softcap) before the mask */
-  int32_t qk_matmul_output_mode; /* only 0 is accepted (no qk output on this path) */
+  int32_t qk_matmul_output_mode; /* 0..3, used when a qk_matmul_output is requested */
   int64_t q_num_heads;      /* rank-3 inputs only */
   int64_t kv_num_heads;     /* rank-3 inputs only */
   int64_t left_window_size; /* -1 = unbounded */
@@ -216,19 +216,41 @@ typedef struct b2_attention_attrs {
  * Attention (opset 23) with GQA and a contiguous KV cache.
  * Replaces kernel::Attention::operator()(Q, K, V, attrs, attn_mask, past_key,
  * past_value, nonpad_kv_seqlen = nullptr) (kernel_attention.cc:767-852).
- *  q, k, v: FLOAT16 or BFLOAT16, rank 4 [B, H, S, D] or rank 3 [B, S, H*D].
- *  attn_mask: NULL or FLOAT, rank 1-4, broadcast to [B, Hq, Sq, L].
+ *  q, k, v: FLOAT, FLOAT16 or BFLOAT16, rank 4 [B, H, S, D] (v: [B, Hkv, S,
+ *    Dv], Dv may differ from D) or rank 3 [B, S, H*D].
+ *  attn_mask: NULL, FLOAT or BOOL (true keeps a position, false masks it),
+ *    or FLOAT16 / BFLOAT16 when q is half precision; rank 1-4, broadcast to
+ *    [B, Hq, Sq, L]; positions past its last axis are masked.
  *  past_key/past_value: NULL or rank-4 [B, Hkv, past_len, D] (shape), with
  *    data pointing at the cache buffer (see kv_capacity).
  *  present_key/present_value: rank-4 outputs [B, Hkv, past_len+S, D]; may be
  *    NULL when no past is given and the caller does not want them.
- *  y: same dtype as q; rank and layout of q.
+ *  y: same dtype as q; rank and layout of q, head size Dv.
+ * Equivalent to b2_attention_ex with no nonpad_kv_seqlen and no
+ * qk_matmul_output.
  */
 B2_API int b2_attention(const b2_tensor *q, const b2_tensor *k, const b2_tensor *v,
                  const b2_tensor *attn_mask, const b2_tensor *past_key,
                  const b2_tensor *past_value, const b2_attention_attrs *attrs, b2_tensor *y,
                  b2_tensor *present_key, b2_tensor *present_value, void *workspace,
                  size_t *workspace_bytes, void *stream);
+
+/*
+ * Attention with every input and output of the opset-23 node
+ * (kernel::Attention::Run, kernel_attention.cc:855-902): b2_attention plus
+ *  nonpad_kv_seqlen: NULL or INT64 [B]; keys j >= nonpad_kv_seqlen[b] are
+ *    padding, and without a past the causal frontier is offset by
+ *    nonpad_kv_seqlen[b] - Sq (:484-496, 572-582); not with a past cache.
+ *  qk_matmul_output: NULL or [B, Hq, Sq, L] of q's dtype (FLOAT, or the half
+ *    type the reference demotes to): the scores of qk_matmul_output_mode
+ *    0 (scaled Q.K^T), 1 (after softcap), 2 (after the mask) or 3 (softmax).
+ */
+B2_API int b2_attention_ex(const b2_tensor *q, const b2_tensor *k, const b2_tensor *v,
+                    const b2_tensor *attn_mask, const b2_tensor *past_key,
+                    const b2_tensor *past_value, const b2_tensor *nonpad_kv_seqlen,
+                    const b2_attention_attrs *attrs, b2_tensor *y, b2_tensor *present_key,
+                    b2_tensor *present_value, b2_tensor *qk_matmul_output, void *workspace,
+                    size_t *workspace_bytes, void *stream);
 
 /*
  * Seeded synthetic inputs, identical to onnx-light's SplitMix64 generators

@@ -18,12 +18,19 @@
 //   warp 9 (MMA)   issues S_j = Q . K_j^T into one of two TMEM S buffers
 //                  (M = 128 query rows, N = 128 keys, fp32), and, once the
 //                  softmax warps have written P_{j-1}, O += P_{j-1} . V_{j-1}
-//                  into the TMEM O accumulator (V read MN-major);
+//                  into the TMEM O accumulator with P read from TMEM (V read
+//                  MN-major from shared memory);
 //   warps 0-7      two threads per query row (its TMEM lane), one per 64-
 //                  column half: read S, online softmax in base 2 (row maximum
-//                  and sum combined through shared memory), write P (rounded
-//                  to the input type) into one of two shared-memory P
-//                  buffers, and read, scale and store O at the end.
+//                  and sum combined through shared memory), write P over the
+//                  S buffer it came from (tcgen05.st), and read, scale and
+//                  store O at the end.
+// P in the input type: FLOAT16 P carries 11 significant bits, enough for the
+// rel-L2 1e-3 contract.  BFLOAT16 P would carry only 8 (about 1e-3 relative
+// error in O on its own), so it is split into P_hi = bf16(p) and
+// P_lo = bf16(p - P_hi) (16 bits together) and P.V runs as two MMAs per k
+// step, P_hi.V + P_lo.V, the FP32 accumulation of the reference
+// (kernel_attention.cc:670-678) to about 2^-17.
 // The running maximum is re-based lazily: only when a row's maximum grows by
 // more than 8 (log2 units) are l and the TMEM O row rescaled, so P stays
 // within 2^8 and most tiles touch O only through the MMA.
@@ -54,14 +61,15 @@ constexpr uint32_t PT_HALF = 128 * 128;          // [128 rows][64 elements] bf16
 constexpr uint32_t PT_OFF_Q = 0;                  // 2 halves
 constexpr uint32_t PT_OFF_KV = 2 * PT_HALF;       // 2 stages x (K 2 halves, V 2 halves)
 constexpr uint32_t PT_KV_STAGE = 4 * PT_HALF;
-constexpr uint32_t PT_OFF_P = PT_OFF_KV + 2 * PT_KV_STAGE; // 2 buffers x 2 halves
-constexpr uint32_t PT_OFF_RED = PT_OFF_P + 4 * PT_HALF; // [tile parity][half][row] partial maxima
+constexpr uint32_t PT_OFF_RED = PT_OFF_KV + 2 * PT_KV_STAGE; // [tile parity][half][row] partial maxima
 constexpr uint32_t PT_OFF_BAR = PT_OFF_RED + 2 * 2 * PT_M * 4;
 constexpr int PT_NBAR = 16;
 // No alignment slack: the dynamic shared memory base is 1024-byte aligned
 // (checked at run time; a CTA that finds it otherwise reports and skips).
 constexpr size_t PT_SMEM = PT_OFF_BAR + PT_NBAR * 8 + 16;
-constexpr uint32_t PT_TMEM_COLS = 512;            // S0 [0,128), S1 [128,256), O [256,384)
+// TMEM: S0 [0,128), S1 [128,256), O [256,384).  P_j is written over its S
+// buffer: P_hi in columns [0, 64) of it, P_lo (BFLOAT16) in [64, 128).
+constexpr uint32_t PT_TMEM_COLS = 512;
 constexpr uint32_t PT_COL_O = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRebase = 8.0f;                   // lazy re-basing threshold (log2 units)
@@ -228,18 +236,20 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       const uint32_t id_o = tc::idesc(1, fmt, fmt, 0, 1, PT_M, PT_D);
       const uint32_t q_base = tc::smem_u32(sm + PT_OFF_Q);
       bool ok = tc::mbar_wait(q_full, 0);
+      constexpr bool kSplitP = !std::is_same<T, __half>::value;
       auto issue_pv = [&](int j) {
-        // O (+)= P_j . V_j: A = P (K-major over keys), B = V (MN-major over dims)
+        // O (+)= P_j . V_j: A = P from TMEM (over S buffer j & 1), B = V
+        // (MN-major over dims); BFLOAT16 adds P_lo . V_j
         if (!tc::mbar_wait(&p_full[j & 1], (j >> 1) & 1)) return false;
         if (!tc::mbar_wait(&v_full[j & 1], (j >> 1) & 1)) return false;
         tc::tc_fence_after();
-        const uint32_t p_base = tc::smem_u32(sm + PT_OFF_P + (j & 1) * 2 * PT_HALF);
+        const uint32_t p_col = tmem + (uint32_t)(j & 1) * PT_N;
         const uint32_t v_base = tc::smem_u32(sm + PT_OFF_KV + (j & 1) * PT_KV_STAGE + 2 * PT_HALF);
 #pragma unroll
         for (int kk = 0; kk < PT_N / 16; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(p_base + (kk >> 2) * PT_HALF + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = tc::sdesc_sw128(v_base + kk * 16 * 128, PT_HALF, 1024);
-          tc::mma_f16(tmem + PT_COL_O, ad, bd, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_f16_ts(tmem + PT_COL_O, p_col + kk * 8, bd, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          if (kSplitP) tc::mma_f16_ts(tmem + PT_COL_O, p_col + 64 + kk * 8, bd, id_o, 1u);
         }
         tc::tc_commit(&o_done[j & 1]);
         tc::tc_commit(&v_empty[j & 1]);
@@ -247,6 +257,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       };
       for (int j = 0; ok && j < ntiles; ++j) {
         if (*abort_flag || !tc::mbar_wait(&k_full[j & 1], (j >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        // S buffer j & 1 holds P_{j-2} until P.V of tile j - 2 is done.
+        if (j >= 2 && !tc::mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1)) {
           ok = false;
           break;
         }
@@ -346,30 +361,32 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
         }
         tc::tmem_st_wait();
       }
-      // P buffer (j & 1) is free once P.V of tile j - 2 is done.
-      if (j >= 2 && !uniform_wait(&o_done[j & 1], ((j - 2) >> 1) & 1)) {
-        ok = false;
-        continue;
-      }
-      // pass 2: P for this half (its 64 keys are the P buffer's half `half`);
-      // masked scores are -inf and give 2^-inf = 0
-      uint8_t *pb = sm + PT_OFF_P + (j & 1) * 2 * PT_HALF + half * PT_HALF + row * 128;
+      // pass 2: P for this half (keys half * 64 .. + 63) over the S buffer
+      // the scores came from (every thread of the row has read its S half
+      // before the barrier above); masked scores are -inf and give 0
       const float nm = -m_ref;
       float ls = 0.0f;
+      const uint32_t p_col = tmem + lane_off + (j & 1) * PT_N + half * 32;
 #pragma unroll
-      for (int chunk = 0; chunk < 8; ++chunk) { // 16-byte chunks of 8 keys
-        uint32_t w[4];
+      for (int c = 0; c < 2; ++c) { // 32 keys (16 packed columns) at a time
+        uint32_t ph[16];
+        uint32_t pl[std::is_same<T, __half>::value ? 1 : 16];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float p0 = ex2(fmaf(v[chunk * 8 + 2 * u], vk, nm));
-          const float p1 = ex2(fmaf(v[chunk * 8 + 2 * u + 1], vk, nm));
+        for (int u = 0; u < 16; ++u) {
+          const float p0 = ex2(fmaf(v[c * 32 + 2 * u], vk, nm));
+          const float p1 = ex2(fmaf(v[c * 32 + 2 * u + 1], vk, nm));
           ls += p0 + p1;
-          w[u] = pack2<T>(p0, p1);
+          ph[u] = pack2<T>(p0, p1);
+          if constexpr (!std::is_same<T, __half>::value) {
+            const float h0 = __uint_as_float(ph[u] << 16), h1 = __uint_as_float(ph[u] & 0xffff0000u);
+            pl[u] = pack2<T>(p0 - h0, p1 - h1);
+          }
         }
-        *reinterpret_cast<uint4 *>(pb + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tc::tmem_st16(p_col + c * 16, ph);
+        if constexpr (!std::is_same<T, __half>::value) tc::tmem_st16(p_col + 64 + c * 16, pl);
       }
+      tc::tmem_st_wait();
       l_part += ls;
-      tc::fence_proxy_async();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[j & 1]);

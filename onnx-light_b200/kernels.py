@@ -219,6 +219,7 @@ class Result:
     Y: torch.Tensor
     present_key: Optional[torch.Tensor] = None
     present_value: Optional[torch.Tensor] = None
+    qk_matmul_output: Optional[torch.Tensor] = None
 
 
 class KVCache:
@@ -243,13 +244,20 @@ class KVCache:
 
 
 class Attention:
-    """kernel::Attention, opset 23 (kernel_attention.cc:767-902), GQA + contiguous KV cache."""
+    """kernel::Attention, opset 23 (kernel_attention.cc:767-902), GQA + contiguous KV cache.
+
+    ``attn_mask`` may be FLOAT or BOOL (or FLOAT16 / BFLOAT16 with half
+    inputs); ``nonpad_kv_seqlen`` is an INT64 [B] tensor; with
+    ``qk_matmul_output=True`` the result also carries the [B, Hq, Sq, L]
+    scores selected by ``attrs.qk_matmul_output_mode``.
+    """
 
     name = "onnx_kernels:GPU:ai.onnx:Attention"
 
     def __call__(self, Q, K, V, attrs: Optional[Attributes] = None, attn_mask=None,
-                 past_key=None, past_value=None, cache: Optional[KVCache] = None,
-                 present_key=None, present_value=None, out=None) -> Result:
+                 past_key=None, past_value=None, nonpad_kv_seqlen=None,
+                 cache: Optional[KVCache] = None, present_key=None, present_value=None,
+                 qk_matmul_output: bool = False, out=None) -> Result:
         attrs = attrs or Attributes()
         a = capi.B2AttentionAttrs(int(attrs.has_scale), float(attrs.scale), int(attrs.is_causal),
                                   float(attrs.softcap), int(attrs.qk_matmul_output_mode),
@@ -257,24 +265,28 @@ class Attention:
                                   int(attrs.left_window_size), int(attrs.right_window_size), 0)
         qd, kd, vd = _desc(Q), _desc(K), _desc(V)
         md = _desc(attn_mask) if attn_mask is not None else None
+        nd = _desc(nonpad_kv_seqlen) if nonpad_kv_seqlen is not None else None
         rank3 = Q.dim() == 3
         new = K.shape[1] if rank3 else K.shape[2]
         B = Q.shape[0]
         if rank3:
             hkv = attrs.kv_num_heads
             D = K.shape[2] // hkv if hkv > 0 else 0
+            Dv = V.shape[2] // hkv if hkv > 0 else 0
         else:
-            hkv, D = K.shape[1], K.shape[3]
+            hkv, D, Dv = K.shape[1], K.shape[3], V.shape[3]
+        Hq = attrs.q_num_heads if rank3 else Q.shape[1]
+        Sq = Q.shape[1] if rank3 else Q.shape[2]
         pkd = pvd = None
         if cache is not None:
             past = cache.length
             a.kv_capacity = cache.capacity
             if past:
                 pkd = Desc(cache.k.data_ptr(), capi.TORCH_TO_ONNX[cache.k.dtype], (B, hkv, past, D))
-                pvd = Desc(cache.v.data_ptr(), capi.TORCH_TO_ONNX[cache.v.dtype], (B, hkv, past, D))
+                pvd = Desc(cache.v.data_ptr(), capi.TORCH_TO_ONNX[cache.v.dtype], (B, hkv, past, Dv))
             total = past + new
             prk = Desc(cache.k.data_ptr(), capi.TORCH_TO_ONNX[cache.k.dtype], (B, hkv, total, D))
-            prv = Desc(cache.v.data_ptr(), capi.TORCH_TO_ONNX[cache.v.dtype], (B, hkv, total, D))
+            prv = Desc(cache.v.data_ptr(), capi.TORCH_TO_ONNX[cache.v.dtype], (B, hkv, total, Dv))
         else:
             if past_key is not None:
                 pkd, pvd = _desc(past_key), _desc(past_value)
@@ -283,19 +295,22 @@ class Attention:
                 total = new
             if present_key is None and (past_key is not None):
                 present_key = torch.empty((B, hkv, total, D), dtype=Q.dtype, device=Q.device)
-                present_value = torch.empty_like(present_key)
+                present_value = torch.empty((B, hkv, total, Dv), dtype=Q.dtype, device=Q.device)
             prk = _desc(present_key) if present_key is not None else None
             prv = _desc(present_value) if present_value is not None else None
         if out is None:
-            out = torch.empty(Q.shape if not rank3 else Q.shape, dtype=Q.dtype, device=Q.device)
-            if not rank3 and V.shape[3] != Q.shape[3]:
-                out = torch.empty(Q.shape[:3] + (V.shape[3],), dtype=Q.dtype, device=Q.device)
+            shape = (B, Sq, Hq * Dv) if rank3 else (B, Hq, Sq, Dv)
+            out = torch.empty(shape, dtype=Q.dtype, device=Q.device)
         yd = _desc(out)
-        _call_with_workspace(lib().b2_attention,
-                             (qd.ref, kd.ref, vd.ref, _ref(md), _ref(pkd), _ref(pvd), C.byref(a),
-                              yd.ref, _ref(prk), _ref(prv)),
+        qk = None
+        if qk_matmul_output:
+            qk = torch.empty((B, Hq, Sq, total), dtype=Q.dtype, device=Q.device)
+        qkd = _desc(qk) if qk is not None else None
+        _call_with_workspace(lib().b2_attention_ex,
+                             (qd.ref, kd.ref, vd.ref, _ref(md), _ref(pkd), _ref(pvd), _ref(nd),
+                              C.byref(a), yd.ref, _ref(prk), _ref(prv), _ref(qkd)),
                              (stream_ptr(Q.device),), Q.device)
         if cache is not None:
             cache.length = total
-            return Result(out, cache.k[:, :, :total], cache.v[:, :, :total])
-        return Result(out, present_key, present_value)
+            return Result(out, cache.k[:, :, :total], cache.v[:, :, :total], qk)
+        return Result(out, present_key, present_value, qk)

@@ -590,38 +590,48 @@ int orc_qlinear_matmul(const uint8_t *a, int a_dt, const int64_t *as, int an, fl
 /*
  * Attention, rank-4 float32 core (kernel_attention.cc:427-691).
  *
- * Q [B,Hq,Sq,D], K/V [B,Hkv,L,D] where L is the total KV length (past already
- * concatenated by the caller, kernel_attention.cc:469-471), mask optional
- * float [mb,mh,mq,ml] broadcast per :343-370 with positions j >= ml masked
- * (:376-386).  GQA kv_h = h / (Hq/Hkv) (:587); causal j > i + past_len masked
- * (:583-606); softcap applied before the mask (:625-626); max-subtract
+ * Q [B,Hq,Sq,D], K [B,Hkv,L,D], V [B,Hkv,L,Dv] where L is the total KV length
+ * (past already concatenated by the caller, kernel_attention.cc:469-471),
+ * mask optional float [mb,mh,mq,ml] broadcast per :371-394 with positions
+ * j >= ml masked (:396-412; BOOL and half masks are converted to this float
+ * form by the caller, :391-392 and :797-801).  GQA kv_h = h / (Hq/Hkv) (:587);
+ * causal frontier j > i + offset masked, offset = past_len, or
+ * nonpad[b] - Sq when nonpad lengths are given without a past (:572-582);
+ * windows measured from the same offset (:594-597); keys j >= nonpad[b]
+ * masked (:598-599); softcap applied before the mask (:619-620); max-subtract
  * softmax with a fully-masked row producing zeros (:641-661); Y = sum p*V
- * (:670-678).  The extended-exponent rescue for non-finite scores (:33-158)
- * is not restated: it only triggers on overflowing inputs.
+ * (:670-678).  qk (optional, [B,Hq,Sq,L]) receives the scores of qk_mode
+ * 0 (scaled), 1 (after softcap), 2 (after the mask) or 3 (softmax) (:613-668).
+ * The extended-exponent rescue for non-finite scores (:33-158) is not
+ * restated: it only triggers on overflowing inputs.
  */
 int orc_attention_f32(const float *Q, const float *Kc, const float *Vc, int64_t B, int64_t Hq,
                       int64_t Hkv, int64_t Sq, int64_t L, int64_t D, int64_t Dv, float scale,
                       int is_causal, int64_t past_len, float softcap, const float *mask,
                       const int64_t *mask_shape4, int64_t left_window, int64_t right_window,
-                      float *Y) {
+                      const int64_t *nonpad, float *qk, int qk_mode, float *Y) {
   if (Hkv <= 0 || Hq % Hkv) return ORC_EINVAL;
   const int64_t group = Hq / Hkv;
   float *sc = (float *)malloc((size_t)(L ? L : 1) * 4);
   for (int64_t b = 0; b < B; ++b)
     for (int64_t h = 0; h < Hq; ++h) {
       const int64_t kvh = h / group;
+      const int64_t off = (nonpad && past_len == 0) ? nonpad[b] - Sq : past_len;
       const float *q = Q + ((b * Hq + h) * Sq) * D;
       const float *kk = Kc + ((b * Hkv + kvh) * L) * D;
       const float *vv = Vc + ((b * Hkv + kvh) * L) * Dv;
       float *yy = Y + ((b * Hq + h) * Sq) * Dv;
       for (int64_t i = 0; i < Sq; ++i) {
+        float *qkr = qk ? qk + (((b * Hq + h) * Sq) + i) * L : NULL;
         int fully = 1;
         float mx = -INFINITY;
         for (int64_t j = 0; j < L; ++j) {
           float s = 0.0f;
           for (int64_t d = 0; d < D; ++d) s += q[i * D + d] * kk[j * D + d];
           s *= scale;
+          if (qkr && qk_mode == 0) qkr[j] = s;
           if (softcap > 0.0f) s = softcap * tanhf(s / softcap);
+          if (qkr && qk_mode == 1) qkr[j] = s;
           float bias = 0.0f;
           if (mask) {
             const int64_t ml = mask_shape4[3];
@@ -637,13 +647,15 @@ int orc_attention_f32(const float *Q, const float *Kc, const float *Vc, int64_t 
               bias = mask[lin];
             }
           }
-          if (is_causal && j > i + past_len) bias = -INFINITY;
-          const int64_t wd = i + past_len - j;
+          if (is_causal && j > i + off) bias = -INFINITY;
+          const int64_t wd = i + off - j;
           if ((left_window >= 0 && wd > left_window) || (right_window >= 0 && -wd > right_window))
             bias = -INFINITY;
+          if (nonpad && j >= nonpad[b]) bias = -INFINITY;
           fully &= isinf(bias) && bias < 0.0f;
           s += bias;
           sc[j] = s;
+          if (qkr && qk_mode == 2) qkr[j] = s;
           if (s > mx) mx = s;
         }
         float den = 0.0f;
@@ -654,6 +666,8 @@ int orc_attention_f32(const float *Q, const float *Kc, const float *Vc, int64_t 
         }
         const float inv = den != 0.0f ? 1.0f / den : 0.0f;
         for (int64_t j = 0; j < L; ++j) sc[j] *= inv;
+        if (qkr && qk_mode == 3)
+          for (int64_t j = 0; j < L; ++j) qkr[j] = sc[j];
         for (int64_t dv = 0; dv < Dv; ++dv) {
           float acc = 0.0f;
           for (int64_t j = 0; j < L; ++j) acc += sc[j] * vv[j * Dv + dv];

@@ -121,7 +121,7 @@ def _declare_oracle(L):
                                      C.c_float, C.c_int32, C.c_int, P]
     L.orc_attention_f32.argtypes = [P, P, P] + [C.c_int64] * 7 + [C.c_float, C.c_int, C.c_int64,
                                                                    C.c_float, P, I64P, C.c_int64,
-                                                                   C.c_int64, P]
+                                                                   C.c_int64, P, P, C.c_int, P]
     for fn in ("orc_f16_to_f32_n", "orc_f32_to_f16_n", "orc_bf16_to_f32_n", "orc_f32_to_bf16_n",
                "orc_f32_to_f8e4m3fn_n"):
         getattr(L, fn).argtypes = [P, P, C.c_int64]
@@ -287,9 +287,26 @@ def qlinear_matmul(a, a_dt, a_scale: float, a_zp: int, b, b_dt, b_scale: float, 
     return out.view(np.int8) if y_dt == INT8 else out
 
 
+def mask_to_float(mask):
+    """A FLOAT, BOOL (numpy bool) or half-precision (float16 / bfloat16 bits
+    given as ('bf16', uint16 array)) attention mask as the float32 bias the
+    reference kernel adds: BOOL true -> 0, false -> -inf
+    (kernel_attention.cc:391-392); half masks promoted to float32 (:797-801)."""
+    if isinstance(mask, tuple) and mask[0] == "bf16":
+        return bf16_bits_to_f32(mask[1])
+    m = np.asarray(mask)
+    if m.dtype == np.bool_:
+        return np.where(m, np.float32(0.0), np.float32(-np.inf)).astype(np.float32)
+    if m.dtype == np.float16:
+        return m.astype(np.float32)
+    return np.ascontiguousarray(m, np.float32)
+
+
 def attention_f32(q, k, v, scale=None, is_causal=False, past_len=0, softcap=0.0, mask=None,
-                  left_window=-1, right_window=-1):
-    """Rank-4 float32 attention over an already-concatenated KV (B,Hkv,L,D)."""
+                  left_window=-1, right_window=-1, nonpad=None, qk_mode=None):
+    """Rank-4 float32 attention over an already-concatenated KV (B,Hkv,L,D).
+
+    Returns Y, or (Y, qk) when qk_mode (0..3) asks for qk_matmul_output."""
     q = np.ascontiguousarray(q, np.float32)
     k = np.ascontiguousarray(k, np.float32)
     v = np.ascontiguousarray(v, np.float32)
@@ -302,14 +319,16 @@ def attention_f32(q, k, v, scale=None, is_causal=False, past_len=0, softcap=0.0,
     m = None
     ms = (C.c_int64 * 4)(1, 1, 1, 1)
     if mask is not None:
-        m = np.ascontiguousarray(mask, np.float32)
+        m = np.ascontiguousarray(mask_to_float(mask), np.float32)
         shp = [1] * (4 - m.ndim) + list(m.shape)
         ms = (C.c_int64 * 4)(*shp)
+    npd = None if nonpad is None else np.ascontiguousarray(nonpad, np.int64)
+    qk = None if qk_mode is None else np.zeros((B, Hq, Sq, L), np.float32)
     rc = lib().orc_attention_f32(_ptr(q), _ptr(k), _ptr(v), B, Hq, Hkv, Sq, L, D, Dv, scale,
                                  int(is_causal), past_len, softcap, _ptr(m), ms, left_window,
-                                 right_window, _ptr(y))
+                                 right_window, _ptr(npd), _ptr(qk), int(qk_mode or 0), _ptr(y))
     _check(rc, "Attention")
-    return y
+    return y if qk_mode is None else (y, qk)
 
 
 # ---------------------------------------------------------------------------
@@ -402,10 +421,14 @@ def ref_qlinear_matmul(a, a_dt, a_scale, a_zp, b, b_dt, b_scale, b_zp, y_scale, 
 
 
 def ref_attention(q, k, v, dt=FLOAT, scale=None, is_causal=False, softcap=0.0, mask=None,
-                  past_k=None, past_v=None, q_num_heads=0, kv_num_heads=0):
+                  past_k=None, past_v=None, q_num_heads=0, kv_num_heads=0, mask_dt=None,
+                  nonpad=None, left_window=-1, right_window=-1, qk_mode=None):
     """q,k,v: float32 (dt=FLOAT) or uint16 bit patterns (FLOAT16/BFLOAT16), rank 3 or 4.
 
-    Returns (Y, present_key, present_value) in the same storage type."""
+    mask: float32 (mask_dt FLOAT, the default), numpy bool (BOOL) or uint16
+    bits with mask_dt FLOAT16 / BFLOAT16.  Returns (Y, present_key,
+    present_value), plus qk_matmul_output when qk_mode is given, in the
+    storage type of dt."""
     rank = q.ndim
     q = np.ascontiguousarray(q)
     k = np.ascontiguousarray(k)
@@ -416,30 +439,55 @@ def ref_attention(q, k, v, dt=FLOAT, scale=None, is_causal=False, softcap=0.0, m
     store = np.float32 if dt == FLOAT else np.uint16
     if rank == 4:
         ysh = (q.shape[0], q.shape[1], q.shape[2], v.shape[3])
+        sq, hq = q.shape[2], q.shape[1]
+        snew = k.shape[2]
     else:
         ysh = (q.shape[0], q.shape[1], q_num_heads * (v.shape[2] // kv_num_heads))
+        sq, hq = q.shape[1], q_num_heads
+        snew = k.shape[1]
     y = np.empty(ysh, store)
     m = None
     ms, mn = _shape([])
+    mdt = FLOAT
     if mask is not None:
-        m = np.ascontiguousarray(mask, np.float32)
+        m = np.ascontiguousarray(mask)
+        if m.dtype == np.bool_:
+            m, mdt = m.astype(np.uint8), BOOL
+        elif mask_dt in (FLOAT16, BFLOAT16):
+            m, mdt = m.astype(np.uint16), mask_dt
+        else:
+            m = m.astype(np.float32)
         ms, mn = _shape(m.shape)
     pk = pv = None
     ps, _ = _shape([])
+    pvs, _ = _shape([])
     present_k = present_v = None
+    past = 0
     if past_k is not None:
         pk = np.ascontiguousarray(past_k)
         pv = np.ascontiguousarray(past_v)
         ps, _ = _shape(pk.shape)
-        L = pk.shape[2] + (k.shape[2] if rank == 4 else k.shape[1])
+        pvs, _ = _shape(pv.shape)
+        past = pk.shape[2]
+        L = past + snew
         present_k = np.empty((pk.shape[0], pk.shape[1], L, pk.shape[3]), store)
-        present_v = np.empty_like(present_k)
-    _ref_call(ref().ref_attention, _ptr(q), qs, _ptr(k), ks, _ptr(v), vs, rank, dt, _ptr(m), ms,
-              mn, _ptr(pk), _ptr(pv), ps, int(scale is not None),
+        present_v = np.empty((pv.shape[0], pv.shape[1], L, pv.shape[3]), store)
+    npd = None if nonpad is None else np.ascontiguousarray(nonpad, np.int64)
+    qk = None
+    if qk_mode is not None:
+        qk = np.zeros((q.shape[0], hq, sq, past + snew), store)
+    _ref_call(ref().ref_attention, _ptr(q), qs, _ptr(k), ks, _ptr(v), vs, rank, dt, _ptr(m),
+              int(mdt), ms, mn, _ptr(pk), _ptr(pv), ps, pvs, _ptr(npd),
+              C.c_int64(0 if npd is None else npd.size), int(scale is not None),
               C.c_float(0.0 if scale is None else scale), int(is_causal), C.c_float(softcap),
-              C.c_int64(q_num_heads), C.c_int64(kv_num_heads), _ptr(y), C.c_size_t(y.nbytes),
+              C.c_int64(q_num_heads), C.c_int64(kv_num_heads), C.c_int64(left_window),
+              C.c_int64(right_window), int(qk_mode or 0), _ptr(y), C.c_size_t(y.nbytes),
               _ptr(present_k), _ptr(present_v),
-              C.c_size_t(0 if present_k is None else present_k.nbytes))
+              C.c_size_t(0 if present_k is None else present_k.nbytes),
+              C.c_size_t(0 if present_v is None else present_v.nbytes), _ptr(qk),
+              C.c_size_t(0 if qk is None else qk.nbytes))
+    if qk_mode is not None:
+        return y, present_k, present_v, qk
     return y, present_k, present_v
 
 

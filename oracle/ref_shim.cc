@@ -153,19 +153,24 @@ int ref_qlinear_matmul(const void *a, int a_dt, const int64_t *as, int an, const
   }
 }
 
-// kernel::Attention::operator()(Q, K, V, attrs, mask, past_key, past_value, nullptr)
-// (kernel_attention.cc:767-852).  For FLOAT16/BFLOAT16 inputs this mirrors the
-// kernel's own half-precision path (:783-835): every input is promoted with
-// PromoteToFloat32, the float32 kernel runs, and Y / present_key /
-// present_value are demoted with DemoteFromFloat32.  (That path builds a
-// scratch RuntimeContext, which this link-light build does not carry, so
-// the three calls are made here instead.)
+// kernel::Attention::operator()(Q, K, V, attrs, mask, past_key, past_value,
+// nonpad_kv_seqlen) (kernel_attention.cc:767-852).  For FLOAT16/BFLOAT16
+// inputs this mirrors the kernel's own half-precision path (:783-835): every
+// input (a half-precision mask too) is promoted with PromoteToFloat32, the
+// float32 kernel runs, and Y / present_key / present_value /
+// qk_matmul_output are demoted with DemoteFromFloat32.  (That path builds a
+// scratch RuntimeContext, which this link-light build does not carry, so the
+// calls are made here instead.)  Without a node or context all four outputs
+// are produced (:855-861).
 int ref_attention(const void *q, const int64_t *qs, const void *k, const int64_t *ks, const void *v,
-                  const int64_t *vs, int rank, int dt, const float *mask, const int64_t *ms, int mn,
-                  const void *past_k, const void *past_v, const int64_t *ps, int has_scale,
-                  float scale, int is_causal, float softcap, int64_t q_num_heads,
-                  int64_t kv_num_heads, void *y, size_t y_bytes, void *present_k,
-                  void *present_v, size_t present_bytes, char *err, size_t errlen) {
+                  const int64_t *vs, int rank, int dt, const void *mask, int mask_dt,
+                  const int64_t *ms, int mn, const void *past_k, const void *past_v,
+                  const int64_t *ps, const int64_t *pvs, const int64_t *nonpad, int64_t nonpad_n,
+                  int has_scale, float scale, int is_causal, float softcap, int64_t q_num_heads,
+                  int64_t kv_num_heads, int64_t left_window, int64_t right_window, int qk_mode,
+                  void *y, size_t y_bytes, void *present_k, void *present_v,
+                  size_t present_k_bytes, size_t present_v_bytes, void *qk, size_t qk_bytes,
+                  char *err, size_t errlen) {
   try {
     const kernel::KernelContext ctx = Ctx();
     kernel::Attention att(ctx);
@@ -176,28 +181,38 @@ int ref_attention(const void *q, const int64_t *qs, const void *k, const int64_t
     attrs.softcap = softcap;
     attrs.q_num_heads = q_num_heads;
     attrs.kv_num_heads = kv_num_heads;
+    attrs.left_window_size = left_window;
+    attrs.right_window_size = right_window;
+    attrs.qk_matmul_output_mode = qk_mode;
     const bool half = dt != 1;
-    auto up = [&](const void *p, const int64_t *s, int n) {
-      Tensor t = MakeTensor(p, dt, s, n);
-      return half ? PromoteToFloat32(t) : t;
+    auto up = [&](const void *p, const int64_t *s, int n, int t) {
+      Tensor x = MakeTensor(p, t, s, n);
+      return (t == 10 || t == 16) ? PromoteToFloat32(x) : x;
     };
-    Tensor tq = up(q, qs, rank), tk = up(k, ks, rank), tv = up(v, vs, rank);
-    Tensor tm, tpk, tpv;
-    if (mask) tm = MakeTensor(mask, 1, ms, mn);
+    Tensor tq = up(q, qs, rank, dt), tk = up(k, ks, rank, dt), tv = up(v, vs, rank, dt);
+    Tensor tm, tpk, tpv, tnp;
+    // A half-precision mask is promoted only on the half-precision entry
+    // (kernel_attention.cc:797-801); BOOL and FLOAT masks pass unchanged.
+    if (mask) tm = half ? up(mask, ms, mn, mask_dt) : MakeTensor(mask, mask_dt, ms, mn);
     if (past_k) {
-      tpk = up(past_k, ps, 4);
-      tpv = up(past_v, ps, 4);
+      tpk = up(past_k, ps, 4, dt);
+      tpv = up(past_v, pvs, 4, dt);
     }
+    if (nonpad) tnp = MakeTensor(nonpad, 7, &nonpad_n, 1);
     kernel::Attention::Result r =
         att(tq, tk, tv, attrs, mask ? &tm : nullptr, past_k ? &tpk : nullptr,
-            past_v ? &tpv : nullptr, nullptr);
+            past_v ? &tpv : nullptr, nonpad ? &tnp : nullptr);
     Tensor ty = half ? DemoteFromFloat32(r.Y, dt) : r.Y;
     CopyOut(ty, y, y_bytes, nullptr, nullptr);
     if (present_k && r.present_key.size_bytes()) {
       Tensor pk = half ? DemoteFromFloat32(r.present_key, dt) : r.present_key;
       Tensor pv = half ? DemoteFromFloat32(r.present_value, dt) : r.present_value;
-      CopyOut(pk, present_k, present_bytes, nullptr, nullptr);
-      CopyOut(pv, present_v, present_bytes, nullptr, nullptr);
+      CopyOut(pk, present_k, present_k_bytes, nullptr, nullptr);
+      CopyOut(pv, present_v, present_v_bytes, nullptr, nullptr);
+    }
+    if (qk && r.qk_matmul_output.size_bytes()) {
+      Tensor tqk = half ? DemoteFromFloat32(r.qk_matmul_output, dt) : r.qk_matmul_output;
+      CopyOut(tqk, qk, qk_bytes, nullptr, nullptr);
     }
     return 0;
   } catch (const std::exception &e) {

@@ -162,39 +162,109 @@ def main():
         meta["mm"].append(dict(key=k, dt=dt))
 
     # ---------------- Attention ----------------
+    # Optional keys: Sk (new keys, default Sq), Dv (V head size, default D),
+    # mask_dt ("f32" default, "bool", "f16", "bf16") and mask_shape (default
+    # (Sq, P + Sk)), nonpad (nonpad_kv_seqlen per batch), qk (qk_matmul_output
+    # mode), lw / rw (window sizes).
+    F16, BF16 = O.FLOAT16, O.BFLOAT16
     att = [
-        dict(B=2, Hq=8, Hkv=2, Sq=1, P=37, D=64, causal=True, softcap=0.0, mask=False, rank=4, dt=O.FLOAT16),
-        dict(B=1, Hq=4, Hkv=4, Sq=9, P=0, D=32, causal=True, softcap=0.0, mask=False, rank=4, dt=O.FLOAT16),
+        dict(B=2, Hq=8, Hkv=2, Sq=1, P=37, D=64, causal=True, softcap=0.0, mask=False, rank=4, dt=F16),
+        dict(B=1, Hq=4, Hkv=4, Sq=9, P=0, D=32, causal=True, softcap=0.0, mask=False, rank=4, dt=F16),
         dict(B=2, Hq=6, Hkv=3, Sq=5, P=11, D=16, causal=False, softcap=5.0, mask=True, rank=4, dt=O.FLOAT),
-        dict(B=1, Hq=4, Hkv=2, Sq=7, P=0, D=32, causal=True, softcap=0.0, mask=False, rank=3, dt=O.BFLOAT16),
-        dict(B=1, Hq=32, Hkv=8, Sq=1, P=65, D=128, causal=True, softcap=0.0, mask=False, rank=4, dt=O.FLOAT16),
+        dict(B=1, Hq=4, Hkv=2, Sq=7, P=0, D=32, causal=True, softcap=0.0, mask=False, rank=3, dt=BF16),
+        dict(B=1, Hq=32, Hkv=8, Sq=1, P=65, D=128, causal=True, softcap=0.0, mask=False, rank=4, dt=F16),
+        # BOOL mask with fully masked rows, GQA, past
+        dict(B=2, Hq=8, Hkv=2, Sq=4, P=20, D=64, causal=True, softcap=0.0, mask=True, mask_dt="bool",
+             rank=4, dt=F16),
+        # BFLOAT16 mask shorter than the keys (padded with -inf), qk after the mask
+        dict(B=1, Hq=4, Hkv=2, Sq=6, P=0, D=64, causal=False, softcap=0.0, mask=True, mask_dt="bf16",
+             mask_shape=(1, 4, 6, 4), rank=4, dt=BF16, qk=2),
+        # nonpad_kv_seqlen with the causal frontier it offsets, softmax probabilities
+        dict(B=3, Hq=4, Hkv=4, Sq=3, Sk=10, P=0, D=32, causal=True, softcap=0.0, mask=False, rank=4,
+             dt=F16, nonpad=[10, 7, 4], qk=3),
+        # v_head_size != head_size, softcap, windows, raw scores
+        dict(B=2, Hq=6, Hkv=2, Sq=5, P=7, D=32, Dv=16, causal=False, softcap=4.0, mask=False, rank=4,
+             dt=O.FLOAT, lw=3, rw=1, qk=0),
+        # rank-3 with v_head_size != head_size, scores after the softcap
+        dict(B=1, Hq=4, Hkv=2, Sq=5, P=0, D=16, Dv=24, causal=True, softcap=2.0, mask=False, rank=3,
+             dt=O.FLOAT, qk=1),
+        # BFLOAT16 prefill on the tensor-core path (head 128, no mask), rank 4 and rank 3
+        dict(B=1, Hq=8, Hkv=2, Sq=160, P=0, D=128, causal=True, softcap=0.0, mask=False, rank=4, dt=BF16),
+        dict(B=2, Hq=4, Hkv=1, Sq=130, P=0, D=128, causal=True, softcap=0.0, mask=False, rank=3, dt=BF16),
+        # BFLOAT16 decode with a past (CUDA-core decode)
+        dict(B=2, Hq=8, Hkv=2, Sq=1, P=300, D=128, causal=True, softcap=0.0, mask=False, rank=4, dt=BF16),
+        # FLOAT16 decode on the tensor-core path, longer past
+        dict(B=1, Hq=32, Hkv=8, Sq=1, P=257, D=128, causal=True, softcap=0.0, mask=False, rank=4, dt=F16),
+        # FLOAT16 prefill with a past on the tensor-core path
+        dict(B=1, Hq=8, Hkv=2, Sq=64, P=100, D=128, causal=True, softcap=0.0, mask=False, rank=4, dt=F16),
+        # FLOAT16 inputs with a BFLOAT16 mask (any half mask is promoted)
+        dict(B=1, Hq=2, Hkv=1, Sq=5, P=3, D=32, causal=False, softcap=0.0, mask=True, mask_dt="bf16",
+             rank=4, dt=F16),
+        # Scores that overflow FLOAT in query row 0 (the reference's non-finite
+        # rescue, kernel_attention.cc:33-158, makes that row finite), finite in row 1
+        dict(B=1, Hq=1, Hkv=1, Sq=2, P=0, Sk=3, D=8, causal=False, softcap=0.0, mask=False, rank=4,
+             dt=O.FLOAT, overflow=True),
     ]
     for i, c in enumerate(att):
         seed += 10
         B, Hq, Hkv, Sq, P, D = c["B"], c["Hq"], c["Hkv"], c["Sq"], c["P"], c["D"]
+        Sk, Dv = c.get("Sk", Sq), c.get("Dv", D)
         if c["rank"] == 4:
             q = O.randn(seed, (B, Hq, Sq, D), 0, 0.5)
-            k = O.randn(seed + 1, (B, Hkv, Sq, D), 0, 0.5)
-            v = O.randn(seed + 2, (B, Hkv, Sq, D), 0, 0.5)
+            k = O.randn(seed + 1, (B, Hkv, Sk, D), 0, 0.5)
+            v = O.randn(seed + 2, (B, Hkv, Sk, Dv), 0, 0.5)
         else:
             q = O.randn(seed, (B, Sq, Hq * D), 0, 0.5)
-            k = O.randn(seed + 1, (B, Sq, Hkv * D), 0, 0.5)
-            v = O.randn(seed + 2, (B, Sq, Hkv * D), 0, 0.5)
+            k = O.randn(seed + 1, (B, Sk, Hkv * D), 0, 0.5)
+            v = O.randn(seed + 2, (B, Sk, Hkv * Dv), 0, 0.5)
+        if c.get("overflow"):
+            q[:, :, 0, :] = 1e19                      # q0 . k_j overflows FLOAT for every j
+            k = (np.abs(k) + 0.5).astype(np.float32) * np.float32(1e19)
         pk = O.randn(seed + 3, (B, Hkv, P, D), 0, 0.5) if P else None
-        pv = O.randn(seed + 4, (B, Hkv, P, D), 0, 0.5) if P else None
-        mask = O.randn(seed + 5, (Sq, P + Sq), 0, 1.0) if c["mask"] else None
+        pv = O.randn(seed + 4, (B, Hkv, P, Dv), 0, 0.5) if P else None
+        mask, mdt = None, None
+        if c["mask"]:
+            mshape = tuple(c.get("mask_shape", (Sq, P + Sk)))
+            kind = c.get("mask_dt", "f32")
+            mval = O.randn(seed + 5, mshape, 0, 1.0)
+            if kind == "bool":
+                mask = mval > -0.3
+                mask[..., 1, :] = False  # one fully masked query row
+            elif kind == "f16":
+                mask, mdt = O.f32_to_f16_bits(mval), O.FLOAT16
+            elif kind == "bf16":
+                mask, mdt = O.f32_to_bf16_bits(mval), O.BFLOAT16
+            else:
+                mask = mval
         cv = {O.FLOAT: lambda t: t, O.FLOAT16: O.f32_to_f16_bits, O.BFLOAT16: O.f32_to_bf16_bits}[c["dt"]]
         q, k, v = cv(q), cv(k), cv(v)
         if P:
             pk, pv = cv(pk), cv(pv)
-        y, prk, prv = O.ref_attention(q, k, v, dt=c["dt"], is_causal=c["causal"], softcap=c["softcap"],
-                                      mask=mask, past_k=pk, past_v=pv, q_num_heads=Hq, kv_num_heads=Hkv)
+        nonpad = np.array(c["nonpad"], np.int64) if "nonpad" in c else None
+        out = O.ref_attention(q, k, v, dt=c["dt"], is_causal=c["causal"], softcap=c["softcap"],
+                              mask=mask, past_k=pk, past_v=pv, q_num_heads=Hq, kv_num_heads=Hkv,
+                              mask_dt=mdt, nonpad=nonpad, left_window=c.get("lw", -1),
+                              right_window=c.get("rw", -1), qk_mode=c.get("qk"))
+        y, prk, prv = out[:3]
         kk = f"att{i}"
         arrays.update({kk + "_q": q, kk + "_k": k, kk + "_v": v, kk + "_y": y})
         if P:
-            arrays.update({kk + "_pk": pk, kk + "_pv": pv, kk + "_prk": prk, kk + "_prv": prv})
+            arrays.update({kk + "_pk": pk, kk + "_pv": pv})
+            # present = concat(past, new) on axis 2 (kernel_attention.cc:313-339);
+            # large presents are stored only as that check, not as arrays.
+            if prk.nbytes <= (64 << 10):
+                arrays.update({kk + "_prk": prk, kk + "_prv": prv})
+            elif c["rank"] == 4:
+                assert np.array_equal(prk, np.concatenate([pk, k], 2))
+                assert np.array_equal(prv, np.concatenate([pv, v], 2))
+            else:
+                raise AssertionError("large rank-3 presents are not stored")
         if mask is not None:
             arrays[kk + "_mask"] = mask
+        if nonpad is not None:
+            arrays[kk + "_nonpad"] = nonpad
+        if "qk" in c:
+            arrays[kk + "_qk"] = out[3]
         meta["att"].append(dict(key=kk, **c))
 
     arrays["meta"] = np.frombuffer(json.dumps(meta).encode(), np.uint8)

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import oracle as O
-from util import load_fixtures, rel_l2, to_dev
+from util import attention_fixture, load_fixtures, rel_l2, to_dev
 
 pytestmark = pytest.mark.gpu
 META, Z = load_fixtures()
@@ -21,24 +21,78 @@ def dev(raw, dt):
     return to_dev(raw).view(TORCH[dt])
 
 
-@pytest.mark.parametrize("m", META["att"], ids=lambda m: m["key"])
+def as_stored(ref, dt):
+    """The oracle's fp32 result rounded to the output type, as the reference
+    demotes Y (kernel_attention.cc:819-833): half-precision outputs are compared
+    with what onnx-light itself returns, at the contract's rel-L2 1e-3."""
+    if dt == O.FLOAT16:
+        return O.f16_bits_to_f32(O.f32_to_f16_bits(ref))
+    if dt == O.BFLOAT16:
+        return O.bf16_bits_to_f32(O.f32_to_bf16_bits(ref))
+    return ref
+
+
+FINITE = [m for m in META["att"] if not m.get("overflow")]
+
+
+@pytest.mark.parametrize("m", FINITE, ids=lambda m: m["key"])
 def test_matches_reference_fixture(b2, cuda, m):
-    k = m["key"]
+    """Every Attention fixture against onnx-light's own output in its own
+    storage type: rel-L2 <= 1e-3 for FLOAT16 / BFLOAT16 Y (both sides rounded
+    to the half type), 1e-5 for FLOAT; present bit-exact; qk_matmul_output
+    within the same bounds.  Covers BOOL / FLOAT16 / BFLOAT16 masks,
+    nonpad_kv_seqlen, v_head_size != head_size, windows, and the tensor-core
+    decode and prefill kernels in both half types."""
+    f = attention_fixture(m, Z)
     dt = m["dt"]
-    q, kk, v = dev(Z[k + "_q"], dt), dev(Z[k + "_k"], dt), dev(Z[k + "_v"], dt)
+    q, kk, v = dev(f["q"], dt), dev(f["k"], dt), dev(f["v"], dt)
     attrs = b2.Attributes(is_causal=m["causal"], softcap=m["softcap"], q_num_heads=m["Hq"],
-                          kv_num_heads=m["Hkv"])
-    mask = to_dev(Z[k + "_mask"]) if m["mask"] else None
-    pk = dev(Z[k + "_pk"], dt) if m["P"] else None
-    pv = dev(Z[k + "_pv"], dt) if m["P"] else None
-    r = b2.Attention()(q, kk, v, attrs, mask, pk, pv)
+                          kv_num_heads=m["Hkv"], left_window_size=m.get("lw", -1),
+                          right_window_size=m.get("rw", -1),
+                          qk_matmul_output_mode=m.get("qk") or 0)
+    mask = None
+    if f["mask"] is not None:
+        mask = {O.FLOAT: lambda a: to_dev(a), O.BOOL: lambda a: to_dev(a),
+                O.FLOAT16: lambda a: to_dev(a).view(torch.float16),
+                O.BFLOAT16: lambda a: to_dev(a).view(torch.bfloat16)}[f["mask_dt"]](f["mask"])
+    pk = dev(f["pk"], dt) if m["P"] else None
+    pv = dev(f["pv"], dt) if m["P"] else None
+    nonpad = to_dev(f["nonpad"]) if f["nonpad"] is not None else None
+    r = b2.Attention()(q, kk, v, attrs, mask, pk, pv, nonpad_kv_seqlen=nonpad,
+                       qk_matmul_output=f["qk"] is not None)
     torch.cuda.synchronize()
     y = r.Y.float().cpu().numpy()
-    ref = UP[dt](Z[k + "_y"])
-    assert rel_l2(y, ref) <= TOL[dt] * (10 if dt == O.BFLOAT16 else 1)
+    ref = UP[dt](f["y"])
+    assert rel_l2(y, ref) <= TOL[dt], rel_l2(y, ref)
+    if f["qk"] is not None:
+        got = r.qk_matmul_output.float().cpu().numpy()
+        want = UP[dt](f["qk"])
+        fin = np.isfinite(want)
+        assert np.array_equal(np.isfinite(got), fin)
+        assert np.array_equal(got[~fin], want[~fin])  # -inf where masked
+        assert rel_l2(got[fin], want[fin]) <= TOL[dt], rel_l2(got[fin], want[fin])
     if m["P"]:
-        assert np.array_equal(r.present_key.cpu().numpy().view(Z[k + "_prk"].dtype), Z[k + "_prk"])
-        assert np.array_equal(r.present_value.cpu().numpy().view(Z[k + "_prv"].dtype), Z[k + "_prv"])
+        assert np.array_equal(r.present_key.cpu().numpy().view(f["prk"].dtype), f["prk"])
+        assert np.array_equal(r.present_value.cpu().numpy().view(f["prv"].dtype), f["prv"])
+
+
+def test_overflowing_scores_follow_the_oracle_not_the_rescue(b2, cuda):
+    """The documented divergence: onnx-light recomputes a row whose scores
+    overflow FLOAT with an extended exponent (RecomputeCenteredAttentionScores,
+    kernel_attention.cc:33-158) and returns finite values; the GPU kernels do
+    not, and return what the oracle's restatement without the rescue returns
+    (NaN for that row).  Rows without overflow agree with both at 1e-5."""
+    m = next(m for m in META["att"] if m.get("overflow"))
+    f = attention_fixture(m, Z)
+    r = b2.Attention()(dev(f["q"], O.FLOAT), dev(f["k"], O.FLOAT), dev(f["v"], O.FLOAT))
+    torch.cuda.synchronize()
+    y = r.Y.cpu().numpy()
+    ora = O.attention_f32(f["q"], f["k"], f["v"])
+    ref = f["y"]
+    assert np.all(np.isfinite(ref))                     # the reference rescues row 0
+    assert np.all(np.isnan(ora[:, :, 0])) and np.all(np.isnan(y[:, :, 0]))
+    assert rel_l2(y[:, :, 1], ref[:, :, 1]) <= 1e-5
+    assert rel_l2(y[:, :, 1], ora[:, :, 1]) <= 1e-5
 
 
 def oracle_attention(q16, k16, v16, causal, past_len):
@@ -83,7 +137,7 @@ def test_prefill_causal_gqa_rank3(b2, cuda):
     k4 = up(k).reshape(B, S, Hkv, D).transpose(0, 2, 1, 3)
     v4 = up(v).reshape(B, S, Hkv, D).transpose(0, 2, 1, 3)
     ref = O.attention_f32(q4, k4, v4, is_causal=True).transpose(0, 2, 1, 3).reshape(B, S, Hq * D)
-    assert rel_l2(r.Y.float().cpu().numpy(), ref) <= 4e-3  # bf16 output rounding
+    assert rel_l2(r.Y.float().cpu().numpy(), as_stored(ref, O.BFLOAT16)) <= 1e-3
 
 
 def test_fully_masked_rows_are_zero(b2, cuda):
@@ -187,10 +241,10 @@ def _prefill_case(b2, dt, B, Hq, Hkv, S, P, causal, rank3, softcap=0.0, seed=90)
         y = y.reshape(B, S, Hq, D).transpose(0, 2, 1, 3)
     ref = O.attention_f32(UP[dt](q16), UP[dt](k16), UP[dt](v16), is_causal=causal, past_len=P,
                           softcap=softcap)
-    return y, ref
+    return y, as_stored(ref, dt)
 
 
-PREFILL_TOL = {O.FLOAT16: 1e-3, O.BFLOAT16: 4e-3}  # bf16: output and P rounding (2^-8)
+PREFILL_TOL = {O.FLOAT16: 1e-3, O.BFLOAT16: 1e-3}
 
 
 @pytest.mark.parametrize("dt,B,Hq,Hkv,S,P,causal,rank3", [
@@ -245,7 +299,7 @@ def test_prefill_tensor_core_matches_cuda_core_kernel_and_is_deterministic(b2, c
     y3 = b2.Attention()(q, kk, vv, attrs).Y.float().cpu().numpy()
     torch.cuda.synchronize()
     assert np.array_equal(y1, y2)
-    assert rel_l2(y1, y3) <= 4e-3
+    assert rel_l2(y1, y3) <= 1e-3
 
 
 @pytest.mark.parametrize("dt,B,Hq,Hkv,S,P,causal,rank3", [

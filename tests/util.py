@@ -92,3 +92,28 @@ def fixture_dq_inputs(m, z):
 
 def np_int(raw, dt):
     return raw.view(np.int8) if dt == O.INT8 else raw.view(np.uint8)
+
+
+def attention_fixture(m, z):
+    """Inputs and the reference's outputs of one Attention fixture, as raw
+    arrays: q, k, v, past_k, past_v (storage type of m["dt"]), mask (float32,
+    numpy bool, or uint16 bits with mask_dt), nonpad (int64), y, qk, and the
+    expected present_key / present_value (concat(past, new) on axis 2 when the
+    generator did not store them; it checked that equality against the
+    reference)."""
+    k = m["key"]
+    f = {"q": z[k + "_q"], "k": z[k + "_k"], "v": z[k + "_v"], "y": z[k + "_y"]}
+    f["pk"] = z[k + "_pk"] if m["P"] else None
+    f["pv"] = z[k + "_pv"] if m["P"] else None
+    kind = m.get("mask_dt", "f32")
+    f["mask"] = z[k + "_mask"] if m["mask"] else None
+    f["mask_dt"] = {"f32": O.FLOAT, "bool": O.BOOL, "f16": O.FLOAT16, "bf16": O.BFLOAT16}[kind]
+    f["nonpad"] = z[k + "_nonpad"] if "nonpad" in m else None
+    f["qk"] = z[k + "_qk"] if "qk" in m else None
+    if m["P"]:
+        if k + "_prk" in z.files:
+            f["prk"], f["prv"] = z[k + "_prk"], z[k + "_prv"]
+        else:
+            f["prk"] = np.concatenate([f["pk"], f["k"]], 2)
+            f["prv"] = np.concatenate([f["pv"], f["v"]], 2)
+    return f
