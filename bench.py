@@ -70,6 +70,14 @@ def step_bytes(batch: int, shards: int = 1) -> int:
     return total
 
 
+def workload_config(batch: int) -> dict:
+    """The workload both arms run (identical dicts: the reference arm's column
+    slice is reported beside it, not in it)."""
+    return {"workload": "config3: Llama-7B int4 decode layer (q,k,v,o,gate,up,down)",
+            "batch": batch, "block_size": BLOCK, "weights": "int4 [-8, 7]",
+            "scales": "fp16 [0.002, 0.02]", "zero_points": "none", "activations": "fp16 N(0,1)"}
+
+
 def step_flops(batch: int) -> int:
     return sum(2 * batch * K * N for _, K, N, _ in PROJ)
 
@@ -237,6 +245,12 @@ def gpu_arm(args):
         graph_of(args.steps % chunk)
     if args.warmup % chunk:
         graph_of(args.warmup % chunk)
+    # Replay every graph of the timed region once before it (untimed extra
+    # warm-up): the first replay of a graph uploads it to the device, which a
+    # short timed region would otherwise pay inside its first step.
+    with torch.cuda.stream(stream):
+        for n in sorted({chunk, args.steps % chunk} - {0}):
+            graph_of(n).replay()
     play(args.warmup)
     torch.cuda.synchronize()
     if world > 1:
@@ -349,10 +363,16 @@ def gpu_arm(args):
     secondary = None
     if rank == 0 and world == 1 and not args.no_secondary:
         want_cpu = not args.no_cpu_baseline
-        secondary = {"attention_config4": attention_config4(b2, synth, device, stream, want_cpu),
-                     "matmul_integer_config2": matmul_integer_config2(b2, synth, device, stream,
-                                                                      want_cpu),
-                     "prefill_config5": prefill_config5(b2, synth, device, stream, want_cpu)}
+        secondary = {}
+        for bb in (8, 32, 64):
+            secondary[f"decode_config3_b{bb}"] = decode_config3(b2, layers, device, stream, bb,
+                                                                want_cpu)
+        secondary["dq_matmul_config1"] = dq_matmul_config1(b2, synth, device, stream, want_cpu)
+        secondary["dequantize_linear"] = dequantize_standalone(b2, synth, device, stream, want_cpu)
+        secondary["attention_config4"] = attention_config4(b2, synth, device, stream, want_cpu)
+        secondary["matmul_integer_config2"] = matmul_integer_config2(b2, synth, device, stream,
+                                                                     want_cpu)
+        secondary["prefill_config5"] = prefill_config5(b2, synth, device, stream, want_cpu)
 
     if rank == 0:
         clocks = clk.summary()
@@ -362,10 +382,9 @@ def gpu_arm(args):
             "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights, fp16 activations",
             "data": "synthetic (SplitMix64 seeded, generated on device)",
-            "config": {"workload": "config3: Llama-7B int4 decode layer (q,k,v,o,gate,up,down)",
-                       "batch": B, "block_size": BLOCK, "scales": "fp16", "zero_points": "none",
-                       "parallelism": f"column-sharded tp{world}" if world > 1 else "single GPU",
-                       "l2_policy": f"{NCOPIES} weight copies in rotation "
+            "config": workload_config(B),
+            "parallelism": f"column-sharded over {world} GPUs" if world > 1 else "single GPU",
+            "timing": {"l2_policy": f"{NCOPIES} weight copies in rotation "
                                     f"({NCOPIES * step_bytes(B) / 1e6:.0f} MB > 126 MB L2)",
                        "launch": f"CUDA graphs of {chunk} steps"
                                  + (" with NCCL all_gather per projection" if world > 1 else "")},
@@ -381,6 +400,204 @@ def gpu_arm(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _pinned_like(t):
+    import torch
+    return torch.empty(t.shape, dtype=t.dtype).pin_memory()
+
+
+def _e2e(stream, step_fn, h2d, d2h, reps, chunk):
+    """End-to-end ms per step: every step copies its inputs from pinned host
+    memory (h2d: list of (device tensor, pinned host tensor)), runs step_fn
+    (the public API calls) and copies its result back to pinned host memory
+    (d2h: list of (pinned host tensor, device tensor)); the steps are captured
+    in CUDA graphs of `chunk` steps, as a serving loop captures its step.
+    Returns (ms, h2d bytes, d2h bytes); ms = max(wall clock, device time)."""
+    import torch
+
+    def one():
+        for dst, src in h2d:
+            dst.copy_(src, non_blocking=True)
+        step_fn()
+        for dst, src in d2h:
+            dst.copy_(src, non_blocking=True)
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(chunk):
+            one()
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+    n = max(1, reps // chunk)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(n):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3 / (n * chunk)
+    dev = e0.elapsed_time(e1) / (n * chunk)
+    del g
+    hb = sum(src.numel() * src.element_size() for _, src in h2d)
+    db = sum(dst.numel() * dst.element_size() for dst, _ in d2h)
+    return max(wall, dev), hb, db
+
+
+def decode_config3(b2, layers, device, stream, B, cpu):
+    """BASELINE config 3 at batch B (8, 32, 64): the same seven int4
+    projections and weight copies as the headline, activations [B, 4096].
+    The planner takes the register-MMA decode kernel up to 16 rows and the
+    tcgen05 dequant GEMM above."""
+    import torch
+    from onnx_light_b200 import synth
+    mm = b2.DequantizeMatMul()
+    x = synth.convert(synth.randn(2000 + B, (B * 4096,), 0.0, 1.0, device=device), FLOAT16, (B, 4096))
+    acts = {"x": x}
+    for name, K, N, _ in PROJ:
+        acts[name] = torch.empty((B, N), dtype=torch.float16, device=device)
+    state = {"i": 0}
+
+    def step():
+        layer = layers[state["i"] % NCOPIES]
+        state["i"] += 1
+        for name, K, N, src in PROJ:
+            w, sc = layer[name]
+            mm(acts[src], w, sc, None, axis=0, out=acts[name])
+
+    with torch.cuda.stream(stream):
+        for _ in range(NCOPIES):
+            step()
+    torch.cuda.synchronize()
+    ms = _graph_time(stream, step, 256, chunk=NCOPIES * 8)
+    nbytes = step_bytes(B)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    peak, src = measured_peak()
+    x_host = _pinned_like(x)
+    x_host.copy_(x)
+    y_host = _pinned_like(acts["down"])
+    e2e_ms, hb, db = _e2e(stream, step, [(acts["x"], x_host)], [(y_host, acts["down"])], 256,
+                          NCOPIES * 8)
+    out = {"metric": f"int4 dequant-MatMul HBM GB/s (config 3, batch {B})", "value": round(gbs, 1),
+           "unit": "GB/s", "ms_per_step": round(ms, 5),
+           "kernel": "dq_gemv_mma" if B <= 16 else "dq_gemm_tc",
+           "tflops": round(step_flops(B) / (ms * 1e-3) / 1e12, 2),
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 4), "peak_source": src,
+                        "algorithmic_bytes_per_step": nbytes},
+           "e2e": {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                   "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": hb,
+                   "d2h_bytes_per_step": db,
+                   "path": "DequantizeMatMul python API, pinned H2D + 7 calls + D2H per step"}}
+    if cpu:
+        out["cpu_baseline"] = cpu_baseline_sample(B)
+    return out
+
+
+def dq_matmul_config1(b2, synth, device, stream, cpu):
+    """fp32 activations [1, 32, 4096] times an int4 weight
+    [4096, 4096] dequantized with int4 zero points and fp32 scales blocked by
+    32 along K; fp32 output.  The fp32 accumulation contract (rel-L2 1e-5)
+    keeps it on the FP32 pipe: 1.07 GFLOP against 11.8 MB, so the roofline is
+    the slower of the HBM and FP32 times (FP32: 148 SMs x 128 lanes x 2 FLOP x
+    the SM clock)."""
+    import torch
+    K, N, M, bs = 4096, 4096, 32, 32
+    w = synth.packed_randint(1001, (K, N), -8, 7, INT4, device=device)
+    zp = synth.packed_randint(1003, (K // bs, N), -2, 2, INT4, device=device)
+    sc = synth.uniform(1002, (K // bs, N), 0.005, 0.02, device=device)
+    a = synth.randn(1004, (1, M, K), 0.0, 1.0, device=device)
+    y = torch.empty((1, M, N), dtype=torch.float32, device=device)
+    mm = b2.DequantizeMatMul()
+
+    def step():
+        mm(a, w, sc, zp, axis=0, out=y)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    ms = _graph_time(stream, step, 512, chunk=32)
+    nbytes = K * N // 2 + (K // bs) * N * 4 + (K // bs) * N // 2 + M * K * 4 + M * N * 4
+    flops = 2 * M * K * N
+    hbm, hsrc = measured_peak()
+    fp32_tf = 148 * 128 * 2 * 1.965e9 / 1e12
+    t_hbm = nbytes / (hbm * 1e9)
+    t_fp32 = flops / (fp32_tf * 1e12)
+    bound = "fp32" if t_fp32 > t_hbm else "hbm"
+    t_roof = max(t_hbm, t_fp32)
+    a_host, y_host = _pinned_like(a), _pinned_like(y)
+    a_host.copy_(a)
+    e2e_ms, hb, db = _e2e(stream, step, [(a, a_host)], [(y_host, y)], 512, 32)
+    out = {"metric": "DequantizeLinear int4 -> MatMul fp32 (config 1)",
+           "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+           "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "ms_per_call": round(ms, 5),
+           "dtype": "int4 weights, fp32 activations and accumulation",
+           "config": {"M": M, "K": K, "N": N, "block_size": bs, "zero_points": "int4",
+                      "scales": "fp32"},
+           "roofline": {"bound": bound, "achieved": round(flops / (ms * 1e-3) / 1e12, 3),
+                        "peak": round(fp32_tf, 1), "unit": "TFLOP/s",
+                        "frac": round(t_roof / (ms * 1e-3), 4),
+                        "peak_source": "FP32 pipe at the max SM clock (148 x 128 x 2 x 1.965 GHz); "
+                                       f"HBM {hbm} GB/s ({hsrc}) gives {t_hbm * 1e6:.2f} us",
+                        "algorithmic_bytes": nbytes, "flops": flops,
+                        "roofline_us": round(t_roof * 1e6, 2)},
+           "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                   "ms_per_call": round(e2e_ms, 5), "h2d_bytes_per_step": hb,
+                   "d2h_bytes_per_step": db}}
+    if cpu:
+        out["cpu_baseline"] = _cpu_config1_sample()
+    return out
+
+
+def dequantize_standalone(b2, synth, device, stream, cpu):
+    """Standalone DequantizeLinear (bit-exact with the reference) on the
+    config-1 weight (int4 [4096, 4096], int4 zero points, fp32 scales blocked
+    by 32 -> fp32) and the config-5 weight (float8e4m3fn [4096, 11008], fp32
+    scales blocked by 32 -> fp32).  HBM-bound: bytes = packed x + scales + zero
+    points + y."""
+    import torch
+    dq = b2.DequantizeLinear()
+    out = {"metric": "DequantizeLinear HBM GB/s", "unit": "GB/s", "cases": {}}
+    peak, src = measured_peak()
+    K, N = 4096, 4096
+    w = synth.packed_randint(1001, (K, N), -8, 7, INT4, device=device)
+    zp = synth.packed_randint(1003, (K // 32, N), -2, 2, INT4, device=device)
+    sc = synth.uniform(1002, (K // 32, N), 0.005, 0.02, device=device)
+    y1 = torch.empty((K, N), dtype=torch.float32, device=device)
+    K5, N5 = 4096, 11008
+    w5 = synth.convert(synth.randn(5010, (K5 * N5,), 0.0, 1.0, device=device), 17, (K5, N5))
+    s5 = synth.uniform(5020, (K5 // 32, N5), 0.01, 0.05, device=device)
+    y5 = torch.empty((K5, N5), dtype=torch.float32, device=device)
+    cases = [("config1_int4_zp_block32", lambda: dq(w, sc, zp, axis=0, out=y1),
+              K * N // 2 + (K // 32) * N * 4 + (K // 32) * N // 2 + K * N * 4, y1, w.data),
+             ("config5_float8e4m3fn_block32", lambda: dq(w5, s5, None, axis=0, out=y5),
+              K5 * N5 + (K5 // 32) * N5 * 4 + K5 * N5 * 4, y5, w5.data)]
+    for name, fn, nbytes, y, xin in cases:
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        ms = _graph_time(stream, fn, 256, chunk=16)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        x_host, y_host = _pinned_like(xin), _pinned_like(y)
+        x_host.copy_(xin)
+        e2e_ms, hb, db = _e2e(stream, fn, [(xin, x_host)], [(y_host, y)], 32, 8)
+        out["cases"][name] = {
+            "value": round(gbs, 1), "ms_per_call": round(ms, 5),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_source": src,
+                         "algorithmic_bytes": nbytes},
+            "e2e": {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "ms_per_call": round(e2e_ms, 4), "h2d_bytes_per_step": hb,
+                    "d2h_bytes_per_step": db}}
+    out["value"] = out["cases"]["config1_int4_zp_block32"]["value"]
+    if cpu:
+        out["cpu_baseline"] = _cpu_dq_sample()
+    del w5, s5, y5
+    torch.cuda.empty_cache()
+    return out
 
 
 def _graph_time(stream, fn, reps, chunk=64):
@@ -433,8 +650,18 @@ def attention_config4(b2, synth, device, stream, cpu):
     nbytes = 537657344  # KV read incl. the new token + Q/Y + the append
     peak, src = measured_peak()
     gbs = nbytes / (ms * 1e-3) / 1e9
+    hq, hk, hv, hy = _pinned_like(q), _pinned_like(k), _pinned_like(v), _pinned_like(y)
+    hq.copy_(q)
+    hk.copy_(k)
+    hv.copy_(v)
+    e2e_ms, hb, db = _e2e(stream, step, [(q, hq), (k, hk), (v, hv)], [(hy, y)], 256, 32)
     out = {"metric": "GQA Attention decode tokens/s/GPU (config 4)",
            "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 5),
+           "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                   "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": hb,
+                   "d2h_bytes_per_step": db,
+                   "path": "Attention python API with the KV cache resident; the new token's "
+                           "Q/K/V in, Y out"},
            "dtype": "fp16", "config": {"batch": B, "q_heads": Hq, "kv_heads": Hkv, "head": D,
                                         "past": past, "causal": True},
            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
@@ -473,7 +700,14 @@ def matmul_integer_config2(b2, synth, device, stream, cpu):
     except (OSError, KeyError, ValueError):
         peak, src = 4500.0, "nominal 4.5 POPS dense int8"
     tops = ops / (ms * 1e-3) / 1e12
+    ha, hy = _pinned_like(a), _pinned_like(y)
+    ha.copy_(a)
+    e2e_ms, hb, db = _e2e(stream, step, [(a, ha)], [(hy, y)], 64, 8)
     out = {"metric": "MatMulInteger TOP/s (config 2)", "value": round(tops, 2), "unit": "TOP/s",
+           "e2e": {"value": round(ops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOP/s",
+                   "ms_per_call": round(e2e_ms, 4), "h2d_bytes_per_step": hb,
+                   "d2h_bytes_per_step": db,
+                   "path": "MatMulInteger python API, B resident (an initializer), A in, Y out"},
            "ms_per_call": round(ms, 4), "dtype": "u8 x s8 -> s32",
            "config": {"M": M, "K": K, "N": N, "a_zero_point": "scalar 128",
                       "b_zero_point": "per column"},
@@ -558,6 +792,30 @@ def prefill_config5(b2, synth, device, stream, cpu):
                          "unit": "TFLOP/s", "frac": round(tf / peak, 4), "peak_source": src}}
         del w1, w2, s1, s2
     out["value"] = out["formats"]["float8e4m3fn"]["value"]
+    # e2e (float8e4m3fn weights resident as initializers): X, K, V in from
+    # pinned host memory, the block, the block's output back to the host.
+    w1 = synth.convert(synth.randn(5010, (K1 * N1,), 0.0, 1.0, device=device), 17, (K1, N1))
+    w2 = synth.convert(synth.randn(5011, (N1 * K1,), 0.0, 1.0, device=device), 17, (N1, K1))
+    s1 = synth.uniform(5020, (K1 // 32, N1), 0.01, 0.05, device=device)
+    s2 = synth.uniform(5021, (N1 // 32, K1), 0.01, 0.05, device=device)
+
+    def block():
+        att(x, kk, vv, attrs, out=ao)
+        mm(a2, w1, s1, None, axis=0, cast_dtype=torch.bfloat16, out=h)
+        mm(h, w2, s2, None, axis=0, cast_dtype=torch.bfloat16, out=y)
+
+    hx, hk, hv, hy = _pinned_like(x), _pinned_like(kk), _pinned_like(vv), _pinned_like(y)
+    hx.copy_(x)
+    hk.copy_(kk)
+    hv.copy_(vv)
+    with torch.cuda.stream(stream):
+        block()
+    torch.cuda.synchronize()
+    e2e_ms, hb, db = _e2e(stream, block, [(x, hx), (kk, hk), (vv, hv)], [(hy, y)], 3, 1)
+    out["e2e"] = {"value": round((att_flops + 2 * mm_flops) / (e2e_ms * 1e-3) / 1e12, 1),
+                  "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": hb,
+                  "d2h_bytes_per_step": db, "weights": "float8e4m3fn, resident"}
+    del w1, w2, s1, s2, hx, hk, hv, hy
     if cpu:
         out["cpu_baseline"] = _cpu_prefill_sample()
     del x, kk, vv, ao, h, y
@@ -693,16 +951,76 @@ def _cpu_prefill_sample():
         wd = O.ref_dequantize_linear(w, 17, (K, N), sc, O.FLOAT, (K // 32, N), axis=0)
         t_dq = time.perf_counter() - t0
         t0 = time.perf_counter()
-        O.ref_matmul(a, wd, O.FLOAT)
+        h = O.ref_matmul(a, wd, O.FLOAT)
         t_mm = (time.perf_counter() - t0) * (4 * 8192 / m)
-        step = t_att + 2 * (t_dq + t_mm)
+        w2 = O.f32_to_f8e4m3fn(O.randn(7, (N, K), 0.0, 1.0))
+        sc2 = O.rand_uniform(8, (N // 32, K), 0.01, 0.05).astype(np.float32)
+        t0 = time.perf_counter()
+        wd2 = O.ref_dequantize_linear(w2, 17, (N, K), sc2, O.FLOAT, (N // 32, K), axis=0)
+        t_dq2 = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        O.ref_matmul(h, wd2, O.FLOAT)
+        t_mm2 = (time.perf_counter() - t0) * (4 * 8192 / m)
+        step = t_att + t_dq + t_mm + t_dq2 + t_mm2
         flops = 4 * 4 * Hq * 8192 * 8192 * D // 2 + 2 * 2 * 4 * 8192 * K * N
         return {"value": round(flops / step / 1e12, 6), "unit": "TFLOP/s",
                 "cores": O.ref_thread_count(), "kind": "reference",
                 "sample": f"Attention [1,{S},4096] bf16 ({t_att / (4 * (8192 / S) ** 2):.2f} s, "
                           f"scaled by FLOPs) + DequantizeLinear fp8 4096x11008 "
-                          f"({t_dq:.2f} s) + fp32 MatMul of {m} rows (scaled to 32768), "
-                          f"the second MatMul taken equal to the first"}
+                          f"({t_dq:.2f} s) + fp32 MatMul of {m} rows (scaled to 32768), then "
+                          f"DequantizeLinear fp8 11008x4096 ({t_dq2:.2f} s) + MatMul of the "
+                          f"same {m} rows (scaled)"}
+    except Exception as e:
+        return {"value": None, "kind": "error", "sample": repr(e)[:200]}
+
+
+def _cpu_config1_sample():
+    """Reference DequantizeLinear (int4, zp, block 32) + fp32 MatMul of config 1."""
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import numpy as np
+        import oracle as O
+        if not O.ref_available():
+            return None
+        K, N, M, bs = 4096, 4096, 32, 32
+        w = O.pack_bits(O.randint(1, (K * N,), -8, 7), 4)
+        z = O.pack_bits(O.randint(2, (K // bs * N,), -2, 2), 4)
+        sc = O.rand_uniform(3, (K // bs, N), 0.005, 0.02).astype(np.float32)
+        a = O.randn(4, (M, K)).astype(np.float32)
+        run = lambda: O.ref_matmul(a, O.ref_dequantize_linear(w, O.INT4, (K, N), sc, O.FLOAT,
+                                                               (K // bs, N), z, (K // bs, N), 0),
+                                   O.FLOAT)
+        run()
+        t0 = time.perf_counter()
+        run()
+        t = time.perf_counter() - t0
+        return {"value": round(2 * M * K * N / t / 1e12, 6), "unit": "TFLOP/s",
+                "cores": O.ref_thread_count(), "kind": "reference",
+                "sample": f"the whole config-1 chain (DequantizeLinear + MatMul), {t * 1e3:.1f} ms"}
+    except Exception as e:
+        return {"value": None, "kind": "error", "sample": repr(e)[:200]}
+
+
+def _cpu_dq_sample():
+    """Reference DequantizeLinear on the config-1 weight (int4, zp, block 32 -> fp32)."""
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import numpy as np
+        import oracle as O
+        if not O.ref_available():
+            return None
+        K, N, bs = 4096, 4096, 32
+        w = O.pack_bits(O.randint(1, (K * N,), -8, 7), 4)
+        z = O.pack_bits(O.randint(2, (K // bs * N,), -2, 2), 4)
+        sc = O.rand_uniform(3, (K // bs, N), 0.005, 0.02).astype(np.float32)
+        O.ref_dequantize_linear(w, O.INT4, (K, N), sc, O.FLOAT, (K // bs, N), z, (K // bs, N), 0)
+        t0 = time.perf_counter()
+        O.ref_dequantize_linear(w, O.INT4, (K, N), sc, O.FLOAT, (K // bs, N), z, (K // bs, N), 0)
+        t = time.perf_counter() - t0
+        nbytes = K * N // 2 + (K // bs) * N * 4 + (K // bs) * N // 2 + K * N * 4
+        return {"value": round(nbytes / t / 1e9, 4), "unit": "GB/s", "cores": O.ref_thread_count(),
+                "kind": "reference",
+                "sample": f"config-1 weight, {t * 1e3:.1f} ms per call"}
     except Exception as e:
         return {"value": None, "kind": "error", "sample": repr(e)[:200]}
 
@@ -801,8 +1119,10 @@ def reference_arm(args):
         "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights, fp16 activations",
         "data": "synthetic (SplitMix64 seeded)",
-        "config": {"workload": "config3: Llama-7B int4 decode layer (q,k,v,o,gate,up,down)",
-                   "batch": B, "block_size": BLOCK},
+        "config": workload_config(B),
+        "parallelism": f"{cores} host threads",
+        "sample_slice": {"per_step": "one projection, q k v o gate up down in turn",
+                         "columns": {n: c for n, _, c, _, _ in slices}},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores,
                          "kind": "reference", "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,

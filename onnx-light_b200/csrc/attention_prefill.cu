@@ -12,13 +12,14 @@
 // the key range in tiles of 64 (only up to the diagonal when causal):
 //   S[16 x 64] = Q[16 x 128] . K^T   (mma.sync m16n8k16, fp32 accumulation)
 //   online softmax of S in fp32 registers (base 2, running max / sum)
-//   O[16 x 128] += P[16 x 64] . V    (P rounded to the input type)
+//   O[16 x 128] += P[16 x 64] . V    (P rounded to FLOAT16, or to BFLOAT16
+//                                     plus its BFLOAT16 remainder)
 // K and V tiles ([64 keys][128 dims], two 64-dim halves with the 128-byte
 // swizzle, 32 KB per tile) arrive by TMA through a 2-stage ring; a 4-D tensor
 // map {dim, key, kv_head, batch} reads both the rank-4 [B, H, S, D] and the
 // rank-3 [B, S, H*D] layouts without a repack.  Keys past the valid length
 // read as zeros and are masked.  P is the only value rounded on the way
-// (2^-11 relative for fp16, 2^-8 for bf16).
+// (2^-11 relative for fp16; about 2^-17 for bf16 with the remainder term).
 #include <type_traits>
 
 #include "b2_common.cuh"
@@ -258,6 +259,19 @@ __global__ void __launch_bounds__(AP_THREADS, AP_MINB)
         const uint32_t pa1 = pack2<T>(sc[2 * kt][2], sc[2 * kt][3]);
         const uint32_t pa2 = pack2<T>(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
         const uint32_t pa3 = pack2<T>(sc[2 * kt + 1][2], sc[2 * kt + 1][3]);
+        // BFLOAT16: the remainder p - bf16(p) as a second operand, so P
+        // carries 16 significant bits (as in the tcgen05 kernel)
+        constexpr bool kSplit = !std::is_same<T, __half>::value;
+        uint32_t pl0 = 0, pl1 = 0, pl2 = 0, pl3 = 0;
+        if constexpr (kSplit) {
+          auto rem = [](uint32_t hi, float lo_v, float hi_v) {
+            return pack2<T>(lo_v - __uint_as_float(hi << 16), hi_v - __uint_as_float(hi & 0xffff0000u));
+          };
+          pl0 = rem(pa0, sc[2 * kt][0], sc[2 * kt][1]);
+          pl1 = rem(pa1, sc[2 * kt][2], sc[2 * kt][3]);
+          pl2 = rem(pa2, sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
+          pl3 = rem(pa3, sc[2 * kt + 1][2], sc[2 * kt + 1][3]);
+        }
 #pragma unroll
         for (int nd = 0; nd < 8; ++nd) {
           const int key = kt * 16 + (mi & 1) * 8 + mr;
@@ -266,6 +280,10 @@ __global__ void __launch_bounds__(AP_THREADS, AP_MINB)
           ldsm_x4_t(vbase + (dim >= 64 ? AP_HALF : 0) + swz(key, (dim & 63) >> 3), b0, b1, b2, b3);
           mma<T>(o[2 * nd], pa0, pa1, pa2, pa3, b0, b1);
           mma<T>(o[2 * nd + 1], pa0, pa1, pa2, pa3, b2, b3);
+          if constexpr (kSplit) {
+            mma<T>(o[2 * nd], pl0, pl1, pl2, pl3, b0, b1);
+            mma<T>(o[2 * nd + 1], pl0, pl1, pl2, pl3, b2, b3);
+          }
         }
       }
     }

@@ -506,10 +506,11 @@ static TcPlan tc_plan(const DqMmParams &p) {
   t.s_bytes = (uint32_t)t.s_rows * DT_BM * s_esz;
   t.stage_bytes = DT_AOP_BYTES + t.b_bytes + t.raw_bytes + t.s_bytes;
   t.stage_bytes = (t.stage_bytes + 1023) & ~1023u;
-  // Decode-range batches run two CTAs per SM (about 100 KB of ring each), so
-  // two sets of dequantizing warps share an SM and split-K fills both slots;
-  // the prefill (pre-dequantized) GEMM keeps one CTA with a deep ring.
-  const size_t budget = t.pre ? 220 * 1024 : 100 * 1024;
+  // Decode-range batches (bn <= 64) run two CTAs per SM (about 100 KB of ring
+  // each), so two sets of dequantizing warps share an SM and split-K fills
+  // both slots; wider activation tiles (a stage of 35 KB or more) keep one CTA
+  // with a deeper ring, as does the prefill (pre-dequantized) GEMM.
+  const size_t budget = (t.pre || t.bn > 64) ? 220 * 1024 : 100 * 1024;
   t.stages = (int)std::min<size_t>(6, budget / t.stage_bytes);
   t.smem = (size_t)t.stages * t.stage_bytes + 1024 + 256;
   const int64_t ntiles = (p.N + DT_BM - 1) / DT_BM, mtiles = (p.M + t.bn - 1) / t.bn;
