@@ -146,6 +146,170 @@ __global__ void __launch_bounds__(256) dq_kernel(const DqParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Row kernel: the common layouts, where each group of 8 consecutive elements
+// shares (o, k) -- per-tensor scale, or per-axis / blocked along an axis whose
+// inner extent is a multiple of 8 (a weight [K, N] quantized along K, N % 8 ==
+// 0).  A group then needs one scale (per-tensor, per-axis) or 8 consecutive
+// scales (blocked: one vector load) and the same for the zero points, so
+// nothing is decoded per element but the value itself.  Each thread handles
+// two groups per iteration to keep more bytes in flight.  Same arithmetic as
+// dq_kernel: x86 NaN rules, fp32 (q - zp) * s, RNE to fp16 when the scale is.
+// ---------------------------------------------------------------------------
+enum RowKind : int { kRowI4 = 0, kRowU4, kRowF4, kRowI8, kRowU8, kRowF8E4M3FN };
+
+template <int XK>
+__device__ __forceinline__ void dec8_row(const uint8_t *p, int64_t i0, float (&v)[8]) {
+  if constexpr (XK == kRowI4 || XK == kRowU4 || XK == kRowF4) {
+    const uint32_t w = __ldg(reinterpret_cast<const uint32_t *>(p + (i0 >> 1)));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if constexpr (XK == kRowI4) v[j] = (float)((int32_t)(w << (28 - 4 * j)) >> 28);
+      else if constexpr (XK == kRowU4) v[j] = (float)((w >> (4 * j)) & 0xfu);
+      else v[j] = dec_f4e2m1((w >> (4 * j)) & 0xfu);
+    }
+  } else {
+    const uint2 w = __ldg(reinterpret_cast<const uint2 *>(p + i0));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t b = ((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xffu;
+      if constexpr (XK == kRowI8) v[j] = (float)(int8_t)b;
+      else if constexpr (XK == kRowU8) v[j] = (float)b;
+      else v[j] = dec_f8e4m3fn(b);
+    }
+  }
+}
+
+template <int XK>
+__device__ __forceinline__ float dec1_row(const uint8_t *p, int64_t i) {
+  if constexpr (XK == kRowI4) return (float)((int32_t)((uint32_t)p[i >> 1] << (28 - 4 * (i & 1))) >> 28);
+  else if constexpr (XK == kRowU4) return (float)((p[i >> 1] >> (4 * (i & 1))) & 0xfu);
+  else if constexpr (XK == kRowF4) return dec_f4e2m1((p[i >> 1] >> (4 * (i & 1))) & 0xfu);
+  else if constexpr (XK == kRowI8) return (float)(int8_t)p[i];
+  else if constexpr (XK == kRowU8) return (float)p[i];
+  else return dec_f8e4m3fn(p[i]);
+}
+
+template <int XK, bool F16>
+__global__ void __launch_bounds__(256) dq_rows_kernel(const DqParams p) {
+  const int64_t ngroups = p.n / 8; // full groups; a ragged tail (per-tensor only) below
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t0 < ngroups; t0 += 2 * stride) {
+    float v[2][8], s[2][8], z[2][8];
+    int64_t gi[2];
+    bool live[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      gi[u] = t0 + u * stride;
+      live[u] = gi[u] < ngroups;
+      if (!live[u]) continue;
+      const int64_t i0 = gi[u] * 8;
+      dec8_row<XK>(p.x, i0, v[u]);
+      if (p.layout == 0) {
+        const float sc = F16 ? f16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t *>(p.scale)))
+                             : __ldg(reinterpret_cast<const float *>(p.scale));
+        const float zz = p.zp ? dec1_row<XK>(p.zp, 0) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          s[u][j] = sc;
+          z[u][j] = zz;
+        }
+        continue;
+      }
+      // (o, k, in) of the group's first element; in % 8 == 0
+      const uint32_t ii = (uint32_t)i0;
+      const uint32_t q1 = p.div_inner.div(ii);
+      const uint32_t in = ii - q1 * (uint32_t)p.inner;
+      const uint32_t q2 = p.div_alen.div(q1);
+      const uint32_t k = q1 - q2 * (uint32_t)p.alen;
+      if (p.layout == 1) {
+        const float sc = F16 ? f16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t *>(p.scale) + k))
+                             : __ldg(reinterpret_cast<const float *>(p.scale) + k);
+        const float zz = p.zp ? dec1_row<XK>(p.zp, k) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          s[u][j] = sc;
+          z[u][j] = zz;
+        }
+        continue;
+      }
+      const int64_t si = ((int64_t)q2 * p.s_alen + p.div_block.div(k)) * p.inner + in;
+      if (F16) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(p.scale) + si));
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[u][2 * j] = f16_bits_to_f32((uint16_t)(ww[j] & 0xffffu));
+          s[u][2 * j + 1] = f16_bits_to_f32((uint16_t)(ww[j] >> 16));
+        }
+      } else {
+        const float4 a = __ldg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p.scale) + si));
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p.scale) + si + 4));
+        s[u][0] = a.x; s[u][1] = a.y; s[u][2] = a.z; s[u][3] = a.w;
+        s[u][4] = b.x; s[u][5] = b.y; s[u][6] = b.z; s[u][7] = b.w;
+      }
+      if (p.zp) dec8_row<XK>(p.zp, si, z[u]);
+      else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) z[u][j] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!live[u]) continue;
+      float r[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = x86_mul(x86_sub(v[u][j], z[u][j]), s[u][j]);
+      if (F16) {
+        uint4 w;
+        w.x = (uint32_t)f32_to_f16_bits(r[0]) | ((uint32_t)f32_to_f16_bits(r[1]) << 16);
+        w.y = (uint32_t)f32_to_f16_bits(r[2]) | ((uint32_t)f32_to_f16_bits(r[3]) << 16);
+        w.z = (uint32_t)f32_to_f16_bits(r[4]) | ((uint32_t)f32_to_f16_bits(r[5]) << 16);
+        w.w = (uint32_t)f32_to_f16_bits(r[6]) | ((uint32_t)f32_to_f16_bits(r[7]) << 16);
+        __stcs(reinterpret_cast<uint4 *>(p.y) + gi[u], w);
+      } else {
+        float4 *dst = reinterpret_cast<float4 *>(p.y) + 2 * gi[u];
+        __stcs(dst, make_float4(r[0], r[1], r[2], r[3]));
+        __stcs(dst + 1, make_float4(r[4], r[5], r[6], r[7]));
+      }
+    }
+  }
+  // ragged tail of a per-tensor call (n % 8 elements), one thread each
+  if (blockIdx.x == 0 && threadIdx.x < (p.n & 7)) {
+    const int64_t i = (p.n & ~(int64_t)7) + threadIdx.x;
+    const float sc = F16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t *>(p.scale)[0])
+                         : reinterpret_cast<const float *>(p.scale)[0];
+    const float zz = p.zp ? dec1_row<XK>(p.zp, 0) : 0.0f;
+    store1(p, i, x86_mul(x86_sub(dec1_row<XK>(p.x, i), zz), sc));
+  }
+}
+
+// Row kernel variant for this call, or nullptr (then dq_kernel runs).
+static void (*row_kernel(const DqParams &p))(DqParams) {
+  if (!p.use32) return nullptr;
+  if (p.layout != 0 && (p.inner % 8 != 0 || p.n % 8 != 0)) return nullptr;
+  const uintptr_t sa = reinterpret_cast<uintptr_t>(p.scale), za = reinterpret_cast<uintptr_t>(p.zp);
+  if (p.layout == 2 && ((sa & 15u) || (za & 7u))) return nullptr; // vector loads of 8 scales / zps
+  int xk;
+  switch (p.xdt) {
+  case kInt4: xk = kRowI4; break;
+  case kUint4: xk = kRowU4; break;
+  case kF4E2M1: xk = kRowF4; break;
+  case kInt8: xk = kRowI8; break;
+  case kUint8: xk = kRowU8; break;
+  case kF8E4M3FN: xk = kRowF8E4M3FN; break;
+  default: return nullptr;
+  }
+  static void (*const table[6][2])(DqParams) = {
+      {dq_rows_kernel<kRowI4, false>, dq_rows_kernel<kRowI4, true>},
+      {dq_rows_kernel<kRowU4, false>, dq_rows_kernel<kRowU4, true>},
+      {dq_rows_kernel<kRowF4, false>, dq_rows_kernel<kRowF4, true>},
+      {dq_rows_kernel<kRowI8, false>, dq_rows_kernel<kRowI8, true>},
+      {dq_rows_kernel<kRowU8, false>, dq_rows_kernel<kRowU8, true>},
+      {dq_rows_kernel<kRowF8E4M3FN, false>, dq_rows_kernel<kRowF8E4M3FN, true>}};
+  return table[xk][p.f16 ? 1 : 0];
+}
+
 static bool dq_supported(int dt) {
   return dt == kUint8 || dt == kInt8 || dt == kUint16 || dt == kInt16 || dt == kInt32 || is_f8(dt) ||
          dt == kUint4 || dt == kInt4 || dt == kUint2 || dt == kInt2 || dt == kF4E2M1 ||
@@ -249,6 +413,16 @@ int dq_launch(const DqParams &p, cudaStream_t stream) {
   if (p.n == 0) return B2_OK;
   const int64_t nvec = (p.n + 7) / 8;
   const int threads = 256;
+  if (auto rk = row_kernel(p)) {
+    // two groups of 8 per thread and iteration; 8 CTAs of 256 per SM
+    int64_t blocks = (nvec + 2 * threads - 1) / (2 * threads);
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    rk<<<(unsigned)blocks, threads, 0, stream>>>(p);
+    B2_LAUNCH_CHECK();
+    return B2_OK;
+  }
   int64_t blocks = (nvec + threads - 1) / threads;
   const int64_t cap = (int64_t)sm_count() * 16;
   if (blocks > cap) blocks = cap;
