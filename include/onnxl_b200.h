@@ -135,8 +135,10 @@ B2_API int b2_dequantize_matmul_noalloc(const b2_tensor *a, const b2_tensor *w,
  * last reset (decode GEMVs, tensor-core GEMMs, MatMulInteger, attention): 0
  * when none, else the first code found (1: data never arrived, 2: a ring slot
  * never freed, 3: an MMA never completed), with the kernel named in
- * b2_last_error().  A call whose kernel gave up leaves its output unwritten
- * (or partly written) and is reported only here.  The codes live in device
+ * b2_last_error(); 4 when b2_rotary_embedding met a position_ids value
+ * outside its cos/sin cache (the reference throws there; those outputs are 0).
+ * A call whose kernel gave up leaves its output unwritten (or partly written)
+ * and is reported only here.  The codes live in device
  * words of the library, never in a caller's workspace.  Synchronizes the
  * device first; reset != 0 clears the codes.  No counterpart in onnx-light:
  * its CPU kernels do not wait on other units of work.
@@ -251,6 +253,43 @@ B2_API int b2_attention_ex(const b2_tensor *q, const b2_tensor *k, const b2_tens
                     const b2_attention_attrs *attrs, b2_tensor *y, b2_tensor *present_key,
                     b2_tensor *present_value, b2_tensor *qk_matmul_output, void *workspace,
                     size_t *workspace_bytes, void *stream);
+
+/*
+ * RMSNormalization (opset 23): y = x / sqrt(mean(x^2 over axes [axis, rank)) +
+ * epsilon) * scale, scale broadcast against the trailing axes.
+ * Replaces kernel::RMSNormalization::operator()(x, scale, axis, epsilon)
+ * (kernel_rmsnormalization.cc:83-214): sum of squares in double, rms in float,
+ * x / rms in float; FLOAT16 / BFLOAT16 round the normalized value to their type
+ * before the scale multiplies it.  x, scale, y: FLOAT, FLOAT16 or BFLOAT16 (one
+ * dtype); axis may be negative.
+ */
+B2_API int b2_rms_normalization(const b2_tensor *x, const b2_tensor *scale, int64_t axis,
+                                float epsilon, b2_tensor *y, void *stream);
+
+/*
+ * RotaryEmbedding (opset 23).
+ * Replaces kernel::RotaryEmbedding::operator()(X, cos_cache, sin_cache,
+ * position_ids, attrs) (kernel_rotary_embedding.cc:47-218).
+ *  x: FLOAT / FLOAT16 / BFLOAT16, rank 4 [B, H, S, D] or rank 3 [B, S, H*D]
+ *     (num_heads required); cos/sin: x's dtype, [max_pos, rot/2] with
+ *     position_ids (INT64 [B, S]) or [B, S, rot/2] without (position_ids NULL);
+ *  rotary_embedding_dim: 0 = D; interleaved: pairs (2i, 2i+1) instead of
+ *     (i, i + rot/2).  Channels past rot/2 pairs are copied.  Bit-exact.
+ *  A position outside the cache writes 0 and is reported by b2_kernel_status.
+ */
+B2_API int b2_rotary_embedding(const b2_tensor *x, const b2_tensor *cos_cache,
+                               const b2_tensor *sin_cache, const b2_tensor *position_ids,
+                               int32_t interleaved, int64_t rotary_embedding_dim,
+                               int64_t num_heads, b2_tensor *y, void *stream);
+
+/*
+ * SwiGLU: y = a * sigmoid(alpha * a) * b, a and b of one shape.
+ * Replaces kernel::SwiGLU::operator()(a, b, alpha) (kernel_swiglu.cc:13-20,
+ * 58-112).  FLOAT, DOUBLE, FLOAT16 or BFLOAT16.  The exponential is CUDA's
+ * expf / exp (within 2 ulps of the host library's).
+ */
+B2_API int b2_swiglu(const b2_tensor *a, const b2_tensor *b, float alpha, b2_tensor *y,
+                     void *stream);
 
 /*
  * Seeded synthetic inputs, identical to onnx-light's SplitMix64 generators

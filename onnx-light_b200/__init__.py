@@ -2,11 +2,13 @@
 
 Drop-in GPU implementations of onnx-light's DequantizeLinear, MatMulInteger,
 QLinearMatMul, the fused DequantizeLinear -> MatMul weight-only pattern and
-opset-23 Attention (GQA, contiguous KV cache), exposed through the C ABI in
+opset-23 Attention (GQA, contiguous KV cache), plus the decoder-layer operators
+around them (RMSNormalization, RotaryEmbedding, SwiGLU), exposed through the C ABI in
 include/onnxl_b200.h and mirrored here with the reference's class names.
 """
 from ._capi import version  # noqa: F401
 from .dispatch import (KernelDispatchTable, RegisterB200KernelFunctions,  # noqa: F401
                        default_table)
 from .kernels import (Attention, Attributes, DequantizeLinear, DequantizeMatMul,  # noqa: F401
-                      KVCache, MatMulInteger, QLinearMatMul, QTensor, Result)
+                      KVCache, MatMulInteger, QLinearMatMul, QTensor, Result, RMSNormalization,
+                      RotaryEmbedding, SwiGLU)

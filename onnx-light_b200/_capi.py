@@ -43,7 +43,8 @@ ONNX_TO_TORCH = {FLOAT: torch.float32, FLOAT16: torch.float16, BFLOAT16: torch.b
 # Every symbol the header declares (checked by the CPU tests).
 EXPORTS = ("b2_version", "b2_last_error", "b2_dequantize_linear", "b2_dequantize_matmul",
            "b2_dequantize_matmul_noalloc", "b2_matmul_integer", "b2_qlinear_matmul", "b2_attention", "b2_attention_ex", "b2_synth_fill",
-           "b2_convert", "b2_kernel_status", "b2_selftest_bounded_wait", "b2_selftest_gemm_timeout")
+           "b2_convert", "b2_kernel_status", "b2_selftest_bounded_wait", "b2_selftest_gemm_timeout",
+           "b2_rms_normalization", "b2_rotary_embedding", "b2_swiglu")
 
 
 class B2Tensor(C.Structure):
@@ -99,6 +100,9 @@ def lib() -> C.CDLL:
                                            P, SZ, P]
                 L.b2_attention_ex.argtypes = [T, T, T, T, T, T, T, C.POINTER(B2AttentionAttrs), T,
                                               T, T, T, P, SZ, P]
+                L.b2_rms_normalization.argtypes = [T, T, C.c_int64, C.c_float, T, P]
+                L.b2_rotary_embedding.argtypes = [T, T, T, T, C.c_int32, C.c_int64, C.c_int64, T, P]
+                L.b2_swiglu.argtypes = [T, T, C.c_float, T, P]
                 L.b2_synth_fill.argtypes = [C.c_int32, C.c_uint64, C.c_int64, C.c_double,
                                             C.c_double, P, P]
                 L.b2_convert.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int64, P]

@@ -6,6 +6,9 @@
 //   MatMulInteger     kernel_matmul_integer.cc:236-250   -> b2_matmul_integer
 //   QLinearMatMul     kernel_qlinearmatmul.cc:269-284    -> b2_qlinear_matmul
 //   Attention         kernel_attention.cc:855-902        -> b2_attention_ex
+//   RMSNormalization  kernel_rmsnormalization.cc:216-223 -> b2_rms_normalization
+//   RotaryEmbedding   kernel_rotary_embedding.cc:220-240 -> b2_rotary_embedding
+//   SwiGLU            kernel_swiglu.cc:119-127           -> b2_swiglu
 //   b200:DequantizeMatMul (DequantizeLinear -> [Cast] -> MatMul) -> b2_dequantize_matmul
 // A negative status becomes std::invalid_argument (the reference's
 // EXT_ENFORCE_INVALID) for invalid arguments and dtypes, std::runtime_error
@@ -146,10 +149,16 @@ protected:
   }
   const Tensor *OnDevice(const Tensor *t) { return t ? &OnDevice(*t) : nullptr; }
 
-  // Runs `call(workspace, &bytes)` once as a size query and once for real.
+  // Runs `call(workspace, &bytes)` once as a size query and once for real
+  // (with no workspace at all when the plan needs none: a NULL workspace with
+  // a size pointer is a size query, header of onnxl_b200.h).
   template <class F> void WithWorkspace(F call) {
     size_t need = 0;
     Check(call(nullptr, &need));
+    if (need == 0) {
+      Check(call(nullptr, nullptr));
+      return;
+    }
     if (need > workspace_bytes_) {
       DeviceGuard g(device_);
       if (workspace_) workspace_.reset();
@@ -328,6 +337,75 @@ public:
   }
 };
 
+// RMSNormalization (kernel_rmsnormalization.cc:216-223): X, scale; axis
+// (default -1), epsilon (default 1e-5).
+class CudaRMSNormalization final : public GpuKernel {
+public:
+  using GpuKernel::GpuKernel;
+  void Run(RuntimeContext &rt) override {
+    const NodeProto &node = *node_;
+    ort::RequireInputCount(node, 2);
+    ort::RequireOutputCount(node, 1);
+    Bind(rt);
+    const Tensor &x = OnDevice(ort::GetInput(node, 0, rt));
+    const Tensor &s = OnDevice(ort::GetInput(node, 1, rt));
+    Tensor y = MakeDeviceTensor(x.data_type, x.shape, device_);
+    Desc dx(x), ds(s), dy(y);
+    Check(b2_rms_normalization(dx.ptr(), ds.ptr(), ort::GetAttributeIntOrDefault(node, "axis", -1),
+                               ort::GetAttributeFloatOrDefault(node, "epsilon", 1e-5f), dy.ptr(),
+                               stream()));
+    ort::SetOutput(node, 0, std::move(y), rt);
+  }
+};
+
+// RotaryEmbedding (kernel_rotary_embedding.cc:220-240): X, cos_cache,
+// sin_cache [, position_ids]; interleaved, rotary_embedding_dim, num_heads.
+class CudaRotaryEmbedding final : public GpuKernel {
+public:
+  using GpuKernel::GpuKernel;
+  void Run(RuntimeContext &rt) override {
+    const NodeProto &node = *node_;
+    if (node.input_size() < 3 || node.input_size() > 4)
+      throw std::invalid_argument("RunNode: op '" + std::string(node.op_type()) +
+                                  "' expects between 3 and 4 input(s), got " +
+                                  std::to_string(node.input_size()) + ".");
+    ort::RequireOutputCount(node, 1);
+    Bind(rt);
+    const Tensor &x = OnDevice(ort::GetInput(node, 0, rt));
+    const Tensor &c = OnDevice(ort::GetInput(node, 1, rt));
+    const Tensor &s = OnDevice(ort::GetInput(node, 2, rt));
+    const Tensor *pos = OnDevice(ort::GetOptionalInput(node, 3, rt));
+    Tensor y = MakeDeviceTensor(x.data_type, x.shape, device_);
+    Desc dx(x), dc(c), ds(s), dy(y);
+    std::unique_ptr<Desc> dp(pos ? new Desc(*pos) : nullptr);
+    Check(b2_rotary_embedding(
+        dx.ptr(), dc.ptr(), ds.ptr(), dp ? dp->ptr() : nullptr,
+        ort::GetAttributeIntOrDefault(node, "interleaved", 0) != 0,
+        ort::GetAttributeIntOrDefault(node, "rotary_embedding_dim", 0),
+        ort::GetAttributeIntOrDefault(node, "num_heads", 0), dy.ptr(), stream()));
+    ort::SetOutput(node, 0, std::move(y), rt);
+  }
+};
+
+// SwiGLU (kernel_swiglu.cc:119-127): A, B; alpha (default 1).
+class CudaSwiGLU final : public GpuKernel {
+public:
+  using GpuKernel::GpuKernel;
+  void Run(RuntimeContext &rt) override {
+    const NodeProto &node = *node_;
+    ort::RequireInputCount(node, 2);
+    ort::RequireOutputCount(node, 1);
+    Bind(rt);
+    const Tensor &a = OnDevice(ort::GetInput(node, 0, rt));
+    const Tensor &b = OnDevice(ort::GetInput(node, 1, rt));
+    Tensor y = MakeDeviceTensor(a.data_type, a.shape, device_);
+    Desc da(a), db(b), dy(y);
+    Check(b2_swiglu(da.ptr(), db.ptr(), ort::GetAttributeFloatOrDefault(node, "alpha", 1.0f),
+                    dy.ptr(), stream()));
+    ort::SetOutput(node, 0, std::move(y), rt);
+  }
+};
+
 // b200:DequantizeMatMul(A, W, W_scale [, W_zero_point]) with attributes axis
 // (of the DequantizeLinear, default 0 for a [K, N] weight) and cast_to (the
 // ONNX dtype of a Cast between the two nodes, 0 for none).
@@ -424,6 +502,9 @@ int RegisterB200KernelFunctions(int device_count, bool overwrite) {
       {"", "MatMulInteger", Factory<CudaMatMulInteger>()},
       {"", "QLinearMatMul", Factory<CudaQLinearMatMul>()},
       {"", "Attention", Factory<CudaAttention>()},
+      {"", "RMSNormalization", Factory<CudaRMSNormalization>()},
+      {"", "RotaryEmbedding", Factory<CudaRotaryEmbedding>()},
+      {"", "SwiGLU", Factory<CudaSwiGLU>()},
       {"b200", "DequantizeMatMul", Factory<CudaDequantizeMatMul>()},
   };
   int stored = 0;

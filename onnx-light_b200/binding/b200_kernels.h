@@ -32,9 +32,10 @@ namespace onnxl_b200::binding {
 namespace ort = onnx_light::core::runtime;
 
 /// Registers the GPU kernels for Device::kGPU0 .. kGPU0 + device_count - 1:
-/// ai.onnx DequantizeLinear, MatMulInteger, QLinearMatMul, Attention and the
-/// fused node b200:DequantizeMatMul (DequantizeLinear -> [Cast] -> MatMul; a
-/// pattern pass rewrites the node pair into it).  With overwrite == false an
+/// ai.onnx DequantizeLinear, MatMulInteger, QLinearMatMul, Attention,
+/// RMSNormalization, RotaryEmbedding, SwiGLU and the fused node
+/// b200:DequantizeMatMul (DequantizeLinear -> [Cast] -> MatMul; a pattern pass
+/// rewrites the node pair into it).  With overwrite == false an
 /// existing entry is kept, like the reference's built-in registration.
 /// Returns the number of entries stored.
 int RegisterB200KernelFunctions(int device_count, bool overwrite = false);

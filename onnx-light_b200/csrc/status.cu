@@ -23,6 +23,7 @@ int status_read_attn_prefill_tc(int reset);
 int status_read_dq_gemm_tc(int reset);
 int status_read_imma_tc(int reset);
 int status_read_dq_gemv(int reset);
+int status_read_rotary(int reset);
 
 __device__ int g_selftest_status;
 
@@ -46,23 +47,31 @@ using namespace b2;
 
 extern "C" B2_API int b2_kernel_status(int reset) {
   B2_CUDA(cudaDeviceSynchronize());
-  struct Src { const char *name; int (*read)(int); };
-  const Src srcs[] = {{"dq_gemv_mma", status_read_gemv_mma},
-                      {"attn_decode_mma", status_read_attn_decode},
-                      {"attn_prefill_mma", status_read_attn_prefill},
-                      {"attn_prefill_tc", status_read_attn_prefill_tc},
-                      {"dq_gemm_tc", status_read_dq_gemm_tc},
-                      {"imma_tc", status_read_imma_tc},
-                      {"dq_gemv_i4h", status_read_dq_gemv}};
+  // code: the kernels' time-out codes (1..3), or kOutOfRange for an input
+  // value a device kernel could not reject on the host
+  constexpr int kOutOfRange = 4;
+  struct Src { const char *name; int (*read)(int); int code; };
+  const Src srcs[] = {{"dq_gemv_mma", status_read_gemv_mma, 0},
+                      {"attn_decode_mma", status_read_attn_decode, 0},
+                      {"attn_prefill_mma", status_read_attn_prefill, 0},
+                      {"attn_prefill_tc", status_read_attn_prefill_tc, 0},
+                      {"dq_gemm_tc", status_read_dq_gemm_tc, 0},
+                      {"imma_tc", status_read_imma_tc, 0},
+                      {"dq_gemv_i4h", status_read_dq_gemv, 0},
+                      {"kernel::RotaryEmbedding", status_read_rotary, kOutOfRange}};
   int first = 0;
   for (const Src &s : srcs) {
     const int v = s.read(reset);
     if (v < 0) B2_FAIL(B2_ERR_CUDA, "b2_kernel_status: reading the status of %s failed", s.name);
     if (v && !first) {
-      first = v;
-      set_error(B2_OK, "%s: a bounded wait timed out (code %d: %s)", s.name, v,
-                v == tc::kTimeoutFull ? "data never arrived"
-                : v == tc::kTimeoutEmpty ? "a ring slot never freed" : "an MMA never completed");
+      first = s.code ? s.code : v;
+      if (s.code == kOutOfRange)
+        set_error(B2_OK, "%s: position_ids value out of range (those outputs were written as 0)",
+                  s.name);
+      else
+        set_error(B2_OK, "%s: a bounded wait timed out (code %d: %s)", s.name, v,
+                  v == tc::kTimeoutFull ? "data never arrived"
+                  : v == tc::kTimeoutEmpty ? "a ring slot never freed" : "an MMA never completed");
     }
   }
   return first;

@@ -11,17 +11,21 @@ which case the existing entry wins and the call returns False (:97-109).
 ``onnx_kernels::RegisterKernelFunctions``
 (onnx_light/onnx_extensions/kernels/kernel_dispatch_table.cc:374-488): it
 registers the B200 kernels for ``Device::kGPU0 + i`` with overwrite=False, so an
-override installed earlier by another library keeps precedence.  On the C++
-side the same registrations bind KernelBase subclasses that call the C ABI
-(see INTEGRATION.md); this table lets the Python tests exercise the same
-resolution rules.
+override installed earlier by another library keeps precedence.
+
+This module is the registry of the Python host API (a Python program that
+drives the kernels by name) and of the CPU tests of the resolution rules.
+onnx-light sessions do not read it: they resolve through the compiled
+registration of onnx-light_b200/binding (``onnxl_b200::binding::
+RegisterB200KernelFunctions``, KernelBase subclasses over the C ABI), which
+registers the same operators under the same keys.
 """
 from __future__ import annotations
 
 from typing import Callable, Dict, Optional
 
 from .kernels import (Attention, DequantizeLinear, DequantizeMatMul, MatMulInteger,
-                      QLinearMatMul)
+                      QLinearMatMul, RMSNormalization, RotaryEmbedding, SwiGLU)
 
 K_DEFAULT_ONNX_DOMAIN = "ai.onnx"
 DEVICE_CPU = -1
@@ -95,6 +99,9 @@ def RegisterB200KernelFunctions(table: Optional[KernelDispatchTable] = None,
         ("", "MatMulInteger"): MatMulInteger,
         ("", "QLinearMatMul"): QLinearMatMul,
         ("", "Attention"): Attention,
+        ("", "RMSNormalization"): RMSNormalization,
+        ("", "RotaryEmbedding"): RotaryEmbedding,
+        ("", "SwiGLU"): SwiGLU,
         (FUSED_DOMAIN, "DequantizeMatMul"): DequantizeMatMul,
     }
     for i in range(num_gpus):

@@ -314,3 +314,51 @@ class Attention:
             cache.length = total
             return Result(out, cache.k[:, :, :total], cache.v[:, :, :total], qk)
         return Result(out, present_key, present_value, qk)
+
+
+class RMSNormalization:
+    """kernel::RMSNormalization, opset 23 (kernel_rmsnormalization.cc:83-228)."""
+
+    name = "onnx_kernels:GPU:ai.onnx:RMSNormalization"
+
+    def __call__(self, x: torch.Tensor, scale: torch.Tensor, axis: int = -1,
+                 epsilon: float = 1e-5, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty_like(x)
+        xd, sd, yd = _desc(x), _desc(scale), _desc(out)
+        check(lib().b2_rms_normalization(xd.ref, sd.ref, int(axis), float(epsilon), yd.ref,
+                                         stream_ptr(x.device)))
+        return out
+
+
+class RotaryEmbedding:
+    """kernel::RotaryEmbedding, opset 23 (kernel_rotary_embedding.cc:47-242)."""
+
+    name = "onnx_kernels:GPU:ai.onnx:RotaryEmbedding"
+
+    def __call__(self, x: torch.Tensor, cos_cache: torch.Tensor, sin_cache: torch.Tensor,
+                 position_ids: Optional[torch.Tensor] = None, interleaved: bool = False,
+                 rotary_embedding_dim: int = 0, num_heads: int = 0,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty_like(x)
+        xd, cd, sd, yd = _desc(x), _desc(cos_cache), _desc(sin_cache), _desc(out)
+        pd = _desc(position_ids) if position_ids is not None else None
+        check(lib().b2_rotary_embedding(xd.ref, cd.ref, sd.ref, _ref(pd), int(bool(interleaved)),
+                                        int(rotary_embedding_dim), int(num_heads), yd.ref,
+                                        stream_ptr(x.device)))
+        return out
+
+
+class SwiGLU:
+    """kernel::SwiGLU (kernel_swiglu.cc:58-129): a * sigmoid(alpha a) * b."""
+
+    name = "onnx_kernels:GPU:ai.onnx:SwiGLU"
+
+    def __call__(self, a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty_like(a)
+        ad, bd, yd = _desc(a), _desc(b), _desc(out)
+        check(lib().b2_swiglu(ad.ref, bd.ref, float(alpha), yd.ref, stream_ptr(a.device)))
+        return out

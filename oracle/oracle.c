@@ -679,6 +679,73 @@ int orc_attention_f32(const float *Q, const float *Kc, const float *Vc, int64_t 
   return ORC_OK;
 }
 
+/*
+ * RMSNormalization on float rows (kernel_rmsnormalization.cc:83-214): for each
+ * of `outer` rows of `norm` values, sum of squares in double (increasing
+ * index), mean in double, rms = sqrtf((float)mean + eps), n = x / rms; half
+ * types (half_dt 10 / 16) round n to their type first (:200-205); y = n * s
+ * with the scale already expanded to one value per normalized element.  The
+ * caller rounds y to the output type.
+ */
+void orc_rms_norm_f32(const float *x, const float *s, int64_t outer, int64_t norm, float eps,
+                      int half_dt, float *y) {
+  for (int64_t o = 0; o < outer; ++o) {
+    const float *xr = x + o * norm;
+    double sq = 0.0;
+    for (int64_t i = 0; i < norm; ++i) sq += (double)xr[i] * (double)xr[i];
+    const double mean = norm > 0 ? sq / (double)norm : 0.0;
+    const float rms = sqrtf((float)mean + eps);
+    for (int64_t i = 0; i < norm; ++i) {
+      float n = xr[i] / rms;
+      if (half_dt == 10) n = orc_f16_to_f32(orc_f32_to_f16(n));
+      else if (half_dt == 16) n = orc_bf16_to_f32(orc_f32_to_bf16(n));
+      y[o * norm + i] = n * s[i];
+    }
+  }
+}
+
+/*
+ * RotaryEmbedding on float data (kernel_rotary_embedding.cc:151-218): x in the
+ * canonical [B, H, S, D] order or, with rank3, stored [B, S, H, D]; cos / sin
+ * rows of `half` values picked by pos[b * S + s] (pos != NULL) or by
+ * (b * S + s); pairs (i, i + half) or, interleaved, (2i, 2i + 1);
+ * y1 = c x1 - s x2, y2 = s x1 + c x2; channels from 2 * half on are copied.
+ * Returns ORC_EINVAL for a position outside [0, cache_rows) (the reference
+ * throws there).
+ */
+int orc_rotary_f32(const float *x, const float *cs, const float *sn, const int64_t *pos,
+                   int64_t B, int64_t H, int64_t S, int64_t D, int64_t half, int rank3,
+                   int interleaved, int64_t cache_rows, float *y) {
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t h = 0; h < H; ++h)
+      for (int64_t s = 0; s < S; ++s) {
+        const int64_t base = rank3 ? ((b * S + s) * H + h) * D : ((b * H + h) * S + s) * D;
+        int64_t row = b * S + s;
+        if (pos) {
+          row = pos[b * S + s];
+          if (row < 0 || row >= cache_rows) return ORC_EINVAL;
+        }
+        const float *cr = cs + row * half, *sr = sn + row * half;
+        for (int64_t i = 0; i < half; ++i) {
+          const int64_t i1 = interleaved ? base + 2 * i : base + i;
+          const int64_t i2 = interleaved ? base + 2 * i + 1 : base + half + i;
+          const float x1 = x[i1], x2 = x[i2], c = cr[i], sv = sr[i];
+          y[i1] = c * x1 - sv * x2;
+          y[i2] = sv * x1 + c * x2;
+        }
+        for (int64_t i = 2 * half; i < D; ++i) y[base + i] = x[base + i];
+      }
+  return ORC_OK;
+}
+
+/* SwiGLU on floats (kernel_swiglu.cc:13-20): a * (1 / (1 + exp(-alpha a))) * b. */
+void orc_swiglu_f32(const float *a, const float *b, int64_t n, float alpha, float *y) {
+  for (int64_t i = 0; i < n; ++i) {
+    const float sg = 1.0f / (1.0f + expf(-alpha * a[i]));
+    y[i] = a[i] * sg * b[i];
+  }
+}
+
 /* Bulk conversions used by the Python wrapper. */
 void orc_f16_to_f32_n(const uint16_t *in, float *out, int64_t n) {
   for (int64_t i = 0; i < n; ++i) out[i] = orc_f16_to_f32(in[i]);

@@ -122,6 +122,9 @@ def _declare_oracle(L):
     L.orc_attention_f32.argtypes = [P, P, P] + [C.c_int64] * 7 + [C.c_float, C.c_int, C.c_int64,
                                                                    C.c_float, P, I64P, C.c_int64,
                                                                    C.c_int64, P, P, C.c_int, P]
+    L.orc_rms_norm_f32.argtypes = [P, P, C.c_int64, C.c_int64, C.c_float, C.c_int, P]
+    L.orc_rotary_f32.argtypes = [P, P, P, P] + [C.c_int64] * 5 + [C.c_int, C.c_int, C.c_int64, P]
+    L.orc_swiglu_f32.argtypes = [P, P, C.c_int64, C.c_float, P]
     for fn in ("orc_f16_to_f32_n", "orc_f32_to_f16_n", "orc_bf16_to_f32_n", "orc_f32_to_bf16_n",
                "orc_f32_to_f8e4m3fn_n"):
         getattr(L, fn).argtypes = [P, P, C.c_int64]
@@ -331,6 +334,66 @@ def attention_f32(q, k, v, scale=None, is_causal=False, past_len=0, softcap=0.0,
     return y if qk_mode is None else (y, qk)
 
 
+def _up(raw, dt):
+    if dt == FLOAT16:
+        return f16_bits_to_f32(raw)
+    if dt == BFLOAT16:
+        return bf16_bits_to_f32(raw)
+    return np.ascontiguousarray(raw, np.float32)
+
+
+def _down(v, dt):
+    if dt == FLOAT16:
+        return f32_to_f16_bits(v)
+    if dt == BFLOAT16:
+        return f32_to_bf16_bits(v)
+    return v.astype(np.float32)
+
+
+def rms_normalization(x, scale, dt=FLOAT, axis=-1, epsilon=1e-5):
+    """RMSNormalization of x (float32, or uint16 bits of dt) with the scale
+    broadcast against the normalized axes; returns the output in x's storage."""
+    xf, sf = _up(x, dt), _up(scale, dt)
+    if axis < 0:
+        axis += xf.ndim
+    norm_shape = xf.shape[axis:]
+    outer = int(np.prod(xf.shape[:axis])) if axis else 1
+    norm = int(np.prod(norm_shape)) if norm_shape else 1
+    s_full = np.ascontiguousarray(np.broadcast_to(sf, norm_shape), np.float32).ravel()
+    y = np.empty(xf.size, np.float32)
+    lib().orc_rms_norm_f32(_ptr(np.ascontiguousarray(xf).ravel()), _ptr(s_full), outer, norm,
+                           C.c_float(epsilon), int(dt if dt != FLOAT else 0), _ptr(y))
+    return _down(y.reshape(xf.shape), dt)
+
+
+def rotary_embedding(x, cos, sin, dt=FLOAT, position_ids=None, interleaved=False,
+                     rotary_embedding_dim=0, num_heads=0):
+    xf, cf, sf = _up(x, dt), _up(cos, dt), _up(sin, dt)
+    rank3 = xf.ndim == 3
+    if rank3:
+        B, S, hid = xf.shape
+        H, D = num_heads, hid // num_heads
+    else:
+        B, H, S, D = xf.shape
+    rot = rotary_embedding_dim or D
+    pos = None if position_ids is None else np.ascontiguousarray(position_ids, np.int64)
+    y = np.empty_like(np.ascontiguousarray(xf))
+    rc = lib().orc_rotary_f32(_ptr(np.ascontiguousarray(xf)), _ptr(np.ascontiguousarray(cf)),
+                              _ptr(np.ascontiguousarray(sf)), _ptr(pos), B, H, S, D, rot // 2,
+                              int(rank3), int(bool(interleaved)),
+                              cf.shape[0] if pos is not None else 0, _ptr(y))
+    _check(rc, "RotaryEmbedding")
+    return _down(y, dt)
+
+
+def swiglu(a, b, dt=FLOAT, alpha=1.0):
+    af, bf = _up(a, dt), _up(b, dt)
+    y = np.empty(af.size, np.float32)
+    lib().orc_swiglu_f32(_ptr(np.ascontiguousarray(af).ravel()), _ptr(np.ascontiguousarray(bf).ravel()),
+                         af.size, C.c_float(alpha), _ptr(y))
+    return _down(y.reshape(af.shape), dt)
+
+
 # ---------------------------------------------------------------------------
 # onnx-light's own kernels (oracle/_ref)
 # ---------------------------------------------------------------------------
@@ -489,6 +552,39 @@ def ref_attention(q, k, v, dt=FLOAT, scale=None, is_causal=False, softcap=0.0, m
     if qk_mode is not None:
         return y, present_k, present_v, qk
     return y, present_k, present_v
+
+
+def ref_rms_normalization(x, scale, dt=FLOAT, axis=-1, epsilon=1e-5):
+    x, scale = np.ascontiguousarray(x), np.ascontiguousarray(scale)
+    xs, xn = _shape(x.shape)
+    ss, sn = _shape(scale.shape)
+    y = np.empty_like(x)
+    _ref_call(ref().ref_rms_normalization, _ptr(x), xs, xn, dt, _ptr(scale), ss, sn,
+              C.c_int64(axis), C.c_float(epsilon), _ptr(y), C.c_size_t(y.nbytes))
+    return y
+
+
+def ref_rotary_embedding(x, cos, sin, dt=FLOAT, position_ids=None, interleaved=False,
+                         rotary_embedding_dim=0, num_heads=0):
+    x, cos, sin = np.ascontiguousarray(x), np.ascontiguousarray(cos), np.ascontiguousarray(sin)
+    xs, xn = _shape(x.shape)
+    cs, cn = _shape(cos.shape)
+    pos = None if position_ids is None else np.ascontiguousarray(position_ids, np.int64)
+    ps, pn = _shape([] if pos is None else pos.shape)
+    y = np.empty_like(x)
+    _ref_call(ref().ref_rotary_embedding, _ptr(x), xs, xn, dt, _ptr(cos), _ptr(sin), cs, cn,
+              _ptr(pos), ps, pn, int(bool(interleaved)), C.c_int64(rotary_embedding_dim),
+              C.c_int64(num_heads), _ptr(y), C.c_size_t(y.nbytes))
+    return y
+
+
+def ref_swiglu(a, b, dt=FLOAT, alpha=1.0):
+    a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
+    sh, nd = _shape(a.shape)
+    y = np.empty_like(a)
+    _ref_call(ref().ref_swiglu, _ptr(a), _ptr(b), sh, nd, dt, C.c_float(alpha), _ptr(y),
+              C.c_size_t(y.nbytes))
+    return y
 
 
 def ref_thread_count() -> int:

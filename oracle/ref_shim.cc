@@ -221,6 +221,64 @@ int ref_attention(const void *q, const int64_t *qs, const void *k, const int64_t
   }
 }
 
+// kernel::RMSNormalization::operator()(x, scale, axis, epsilon)
+// (kernel_rmsnormalization.cc:68-214).
+int ref_rms_normalization(const void *x, const int64_t *xs, int xn, int dt, const void *scale,
+                          const int64_t *ss, int sn, int64_t axis, float epsilon, void *y,
+                          size_t y_bytes, char *err, size_t errlen) {
+  try {
+    kernel::RMSNormalization k(Ctx());
+    Tensor r = k(MakeTensor(x, dt, xs, xn), MakeTensor(scale, dt, ss, sn), axis, epsilon);
+    CopyOut(r, y, y_bytes, nullptr, nullptr);
+    return 0;
+  } catch (const std::exception &e) {
+    Fail(e, err, errlen);
+    return -1;
+  }
+}
+
+// kernel::RotaryEmbedding::operator()(X, cos_cache, sin_cache, position_ids,
+// attrs) (kernel_rotary_embedding.cc:47-218).
+int ref_rotary_embedding(const void *x, const int64_t *xs, int xn, int dt, const void *c,
+                         const void *s, const int64_t *cs, int cn, const int64_t *pos,
+                         const int64_t *ps, int pn, int interleaved, int64_t rotary_dim,
+                         int64_t num_heads, void *y, size_t y_bytes, char *err, size_t errlen) {
+  try {
+    kernel::RotaryEmbedding k(Ctx());
+    kernel::RotaryEmbedding::Attributes attrs;
+    attrs.interleaved = interleaved != 0;
+    attrs.rotary_embedding_dim = rotary_dim;
+    attrs.num_heads = num_heads;
+    Tensor tp;
+    if (pos) tp = MakeTensor(pos, 7, ps, pn);
+    // FLOAT16 / BFLOAT16 mirror the kernel's own half path (:65-88): promote,
+    // run in float32, demote (its scratch RuntimeContext is not carried here).
+    const bool half = dt != 1;
+    auto up = [&](Tensor t) { return half ? PromoteToFloat32(t) : t; };
+    Tensor r = k(up(MakeTensor(x, dt, xs, xn)), up(MakeTensor(c, dt, cs, cn)),
+                 up(MakeTensor(s, dt, cs, cn)), tp, attrs);
+    CopyOut(half ? DemoteFromFloat32(r, dt) : r, y, y_bytes, nullptr, nullptr);
+    return 0;
+  } catch (const std::exception &e) {
+    Fail(e, err, errlen);
+    return -1;
+  }
+}
+
+// kernel::SwiGLU::operator()(a, b, alpha) (kernel_swiglu.cc:58-85).
+int ref_swiglu(const void *a, const void *b, const int64_t *shp, int nd, int dt, float alpha, void *y,
+               size_t y_bytes, char *err, size_t errlen) {
+  try {
+    kernel::SwiGLU k(Ctx());
+    Tensor r = k(MakeTensor(a, dt, shp, nd), MakeTensor(b, dt, shp, nd), alpha);
+    CopyOut(r, y, y_bytes, nullptr, nullptr);
+    return 0;
+  } catch (const std::exception &e) {
+    Fail(e, err, errlen);
+    return -1;
+  }
+}
+
 // FloatToFloat8E4M3FNBits (cast_float8.cc:27-80), exposed so that the
 // restatement's encoder can be compared against it.
 uint8_t ref_f32_to_f8e4m3fn(float v) { return onnx_light::core::runtime::FloatToFloat8E4M3FNBits(v); }

@@ -267,6 +267,51 @@ def main():
             arrays[kk + "_qk"] = out[3]
         meta["att"].append(dict(key=kk, **c))
 
+    # ---------------- decoder-layer operators ----------------
+    meta["dec"] = []
+    cvt = {O.FLOAT: lambda t: t.astype(np.float32), O.FLOAT16: O.f32_to_f16_bits,
+           O.BFLOAT16: O.f32_to_bf16_bits}
+    rms = [((2, 7, 4096), (4096,), -1, O.FLOAT, 1e-5), ((3, 64), (), -1, O.FLOAT16, 1e-6),
+           ((2, 3, 40), (1, 40), 1, O.BFLOAT16, 1e-5), ((5, 256), (5, 256), 0, O.FLOAT, 1e-3)]
+    for i, (xs, ss, axis, dt, eps) in enumerate(rms):
+        seed += 10
+        x = cvt[dt](O.randn(seed, xs))
+        sc = cvt[dt](O.rand_uniform(seed + 1, ss, 0.5, 1.5) if ss else np.float32(1.25))
+        y = O.ref_rms_normalization(x, np.asarray(sc), dt, axis, eps)
+        k = f"rms{i}"
+        arrays.update({k + "_x": x, k + "_s": np.asarray(sc), k + "_y": y})
+        meta["dec"].append(dict(key=k, op="RMSNormalization", dt=dt, axis=axis, eps=eps))
+    rot = [((2, 4, 9, 64), None, False, 0, 0, O.FLOAT), ((2, 9, 4 * 64), (2, 9), True, 0, 4, O.FLOAT16),
+           ((1, 2, 7, 128), (1, 7), False, 64, 0, O.BFLOAT16), ((3, 5, 2 * 32), (3, 5), False, 0, 2, O.FLOAT)]
+    for i, (xs, ps, inter, rdim, nh, dt) in enumerate(rot):
+        seed += 10
+        x = cvt[dt](O.randn(seed, xs))
+        D = xs[3] if len(xs) == 4 else xs[2] // nh
+        half = (rdim or D) // 2
+        B, S = xs[0], (xs[2] if len(xs) == 4 else xs[1])
+        if ps is None:
+            cs_shape, pos = (B, S, half), None
+        else:
+            cs_shape, pos = (32, half), O.randint(seed + 3, (B * S,), 0, 31).reshape(B, S)
+        c = cvt[dt](O.rand_uniform(seed + 1, cs_shape, -1.0, 1.0))
+        sn = cvt[dt](O.rand_uniform(seed + 2, cs_shape, -1.0, 1.0))
+        y = O.ref_rotary_embedding(x, c, sn, dt, pos, inter, rdim, nh)
+        k = f"rot{i}"
+        arrays.update({k + "_x": x, k + "_c": c, k + "_s": sn, k + "_y": y})
+        if pos is not None:
+            arrays[k + "_p"] = pos
+        meta["dec"].append(dict(key=k, op="RotaryEmbedding", dt=dt, interleaved=inter, rdim=rdim,
+                                num_heads=nh, pos=pos is not None))
+    for i, (sh, dt, alpha) in enumerate([((4, 11008), O.FLOAT, 1.0), ((3, 1000), O.FLOAT16, 1.702),
+                                         ((2, 515), O.BFLOAT16, 1.0)]):
+        seed += 10
+        a_ = cvt[dt](O.randn(seed, sh))
+        b_ = cvt[dt](O.randn(seed + 1, sh))
+        y = O.ref_swiglu(a_, b_, dt, alpha)
+        k = f"swi{i}"
+        arrays.update({k + "_a": a_, k + "_b": b_, k + "_y": y})
+        meta["dec"].append(dict(key=k, op="SwiGLU", dt=dt, alpha=alpha))
+
     arrays["meta"] = np.frombuffer(json.dumps(meta).encode(), np.uint8)
     np.savez_compressed(OUT, **arrays)
     print(f"wrote {OUT}: {sum(len(v) for v in meta.values())} cases, {os.path.getsize(OUT)} bytes")

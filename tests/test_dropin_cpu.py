@@ -15,7 +15,7 @@ pytestmark = pytest.mark.skipif(not __import__("os").path.exists(dropin.HARNESS)
 @pytest.fixture(scope="module")
 def registered():
     stored = dropin.lib().h_register(2)
-    assert stored in (0, 10)  # 5 operators x 2 devices, 0 when already registered
+    assert stored in (0, 16)  # 8 operators x 2 devices, 0 when already registered
     return True
 
 
@@ -29,7 +29,8 @@ def key(domain, op, dev):
 def test_registration_is_device_keyed(registered):
     for dev in (0, 1):
         for dom, op in (("", "DequantizeLinear"), ("", "MatMulInteger"), ("", "QLinearMatMul"),
-                        ("", "Attention"), ("b200", "DequantizeMatMul")):
+                        ("", "Attention"), ("", "RMSNormalization"), ("", "RotaryEmbedding"),
+                        ("", "SwiGLU"), ("b200", "DequantizeMatMul")):
             found, k = key(dom, op, dev)
             assert found == 1, k
             assert k == f"{dom or 'ai.onnx'}:{op}:{dev}"

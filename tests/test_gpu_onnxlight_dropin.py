@@ -131,3 +131,15 @@ def test_invalid_node_raises_reference_style_error(registered):
         dropin.run_node("", "DequantizeLinear",
                         [dev_in(x, O.UINT8, (4, 4)), dev_in(s, O.FLOAT, (3,))], 1,
                         attrs={"axis": 0}, out_bytes=[64])
+
+
+def test_rms_normalization_node_bit_exact(registered):
+    m = next(m for m in META["dec"] if m["op"] == "RMSNormalization" and m["dt"] == O.FLOAT16)
+    k = m["key"]
+    x, s = to_dev(Z[k + "_x"]), to_dev(np.ascontiguousarray(Z[k + "_s"]))
+    xs = Z[k + "_x"].shape
+    (dt, shape, buf), = dropin.run_node(
+        "", "RMSNormalization", [dev_in(x, O.FLOAT16, xs), dev_in(s, O.FLOAT16, Z[k + "_s"].shape)], 1,
+        attrs={"axis": m["axis"], "epsilon": float(m["eps"])}, out_bytes=[Z[k + "_y"].nbytes])
+    assert dt == O.FLOAT16 and shape == xs
+    assert np.array_equal(buf[:Z[k + "_y"].nbytes].cpu().numpy().view(np.uint16), Z[k + "_y"].ravel())

@@ -161,3 +161,19 @@ def test_live_matmul_integer_config2_slice():
     got = O.matmul_integer(a, O.UINT8, b, O.INT8, az, bz)
     ref = O.ref_matmul_integer(a, O.UINT8, b, O.INT8, az, bz, a_zp_shape=[], b_zp_shape=[64])
     np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("m", META["dec"], ids=lambda m: m["key"])
+def test_decoder_ops_match_reference_fixture(m):
+    """RMSNormalization, RotaryEmbedding and SwiGLU: the restatement is
+    bit-exact with onnx-light's own output."""
+    k, dt = m["key"], m["dt"]
+    if m["op"] == "RMSNormalization":
+        y = O.rms_normalization(Z[k + "_x"], Z[k + "_s"], dt, m["axis"], m["eps"])
+    elif m["op"] == "RotaryEmbedding":
+        y = O.rotary_embedding(Z[k + "_x"], Z[k + "_c"], Z[k + "_s"], dt,
+                               Z[k + "_p"] if m["pos"] else None, m["interleaved"], m["rdim"],
+                               m["num_heads"])
+    else:
+        y = O.swiglu(Z[k + "_a"], Z[k + "_b"], dt, m["alpha"])
+    np.testing.assert_array_equal(np.asarray(y).view(np.uint8), Z[k + "_y"].view(np.uint8))
