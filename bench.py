@@ -189,14 +189,22 @@ def gpu_arm(args):
     mm = b2.DequantizeMatMul()
     stream = torch.cuda.Stream(device)
 
-    # Buffers: full activations per projection output, local slice outputs, gather buffers.
+    # Buffers: the full activation of every projection output and, sharded,
+    # this rank's column slice.  Sharded, the full outputs are peer buffers:
+    # b2_allgather_cols stores each rank's slice into every rank's copy over
+    # NVLink (sharding.PeerGroup), one kernel per projection.
     acts = {"x": x0}
     loc = {}
-    gat = {}
+    peers = None
+    if world > 1:
+        from onnx_light_b200.sharding import PeerGroup
+        peers = PeerGroup()
     for name, K, N, _ in PROJ:
-        acts[name] = torch.empty((B, N), dtype=torch.float16, device=device)
-        loc[name] = torch.empty((B, N // world), dtype=torch.float16, device=device)
-        gat[name] = torch.empty((world, B, N // world), dtype=torch.float16, device=device)
+        if world == 1:
+            acts[name] = torch.empty((B, N), dtype=torch.float16, device=device)
+        else:
+            acts[name] = peers.buffer(name, (B, N), torch.float16)
+            loc[name] = torch.empty((B, N // world), dtype=torch.float16, device=device)
 
     def run_step(layer):
         for name, K, N, src in PROJ:
@@ -205,8 +213,7 @@ def gpu_arm(args):
                 mm(acts[src], w, s, None, axis=0, out=acts[name])
             else:
                 mm(acts[src], w, s, None, axis=0, out=loc[name])
-                dist.all_gather_into_tensor(gat[name].view(-1), loc[name].view(-1))
-                acts[name].copy_(gat[name].permute(1, 0, 2).reshape(B, N))
+                peers.gather(name, loc[name])
 
     def run_steps(n, offset):
         for i in range(n):
@@ -218,7 +225,7 @@ def gpu_arm(args):
         run_steps(NCOPIES, 0)
     torch.cuda.synchronize()
 
-    # The steps run as CUDA graphs of up to CHUNK steps each (NCCL calls
+    # The steps run as CUDA graphs of up to CHUNK steps each (the peer gathers
     # captured too when sharded), so the device time measured is the steps'
     # own and never the host's launch rate.  K steps = K // CHUNK replays of the
     # chunk graph + one graph of the remainder.
@@ -320,7 +327,9 @@ def gpu_arm(args):
     # back to pinned host memory inside every step; the calls are captured in
     # CUDA graphs the way a serving loop captures its decode step.
     e2e = None
-    if rank == 0 and world == 1:
+    if world > 1:
+        dist.barrier()  # rank 0 timed the projections alone; line the ranks up again
+    if rank == 0 or world > 1:  # sharded: every rank takes part (the gathers wait for all)
         x_host = x0.cpu().pin_memory()
         y_host = torch.empty((B, 4096), dtype=torch.float16).pin_memory()
 
@@ -348,12 +357,35 @@ def gpu_arm(args):
         wall = (time.perf_counter() - t0) / (reps_e2e * chunk)
         dev_ms = e0.elapsed_time(e1) / (reps_e2e * chunk)
         e2e_ms = max(wall * 1e3, dev_ms)
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
         e2e = {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": B * 4096 * 2,
                "d2h_bytes_per_step": B * 4096 * 2,
                "path": "DequantizeMatMul python API -> b2_dequantize_matmul, pinned H2D + "
-                       "7 calls + D2H per step, captured in CUDA graphs"}
+                       "7 calls + D2H per step, captured in CUDA graphs"
+                       + (" (+ b2_allgather_cols per call, max over ranks)" if world > 1 else "")}
         del ge
+        del ge
+
+    # Sharded: the gathered full output of a step against the unsharded
+    # projection computed on this rank (rel-L2, contract 1e-3).
+    gather_check = None
+    if world > 1:
+        with torch.cuda.stream(stream):
+            run_step(layers[0])
+        torch.cuda.synchronize()
+        full = make_layer(b2, synth, 0, 0, 1, device)
+        ref_q = mm(x0, full["q"][0], full["q"][1], None, axis=0)
+        torch.cuda.synchronize()
+        err = float(((acts["q"].float() - ref_q.float()).norm() / ref_q.float().norm()).item())
+        t = torch.tensor([err], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gather_check = {"projection": "q", "rel_l2_max_over_ranks": float(t.item()),
+                        "ok": float(t.item()) <= 1e-3}
+        del full, ref_q
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -387,9 +419,11 @@ def gpu_arm(args):
             "timing": {"l2_policy": f"{NCOPIES} weight copies in rotation "
                                     f"({NCOPIES * step_bytes(B) / 1e6:.0f} MB > 126 MB L2)",
                        "launch": f"CUDA graphs of {chunk} steps"
-                                 + (" with NCCL all_gather per projection" if world > 1 else "")},
+                                 + (" with a peer-store all-gather (b2_allgather_cols) per "
+                                    "projection" if world > 1 else "")},
             "tflops": round(step_flops(B) / (ms * 1e-3) / 1e12, 3),
-            "gpu_launches": 7 * args.steps,
+            "gpu_launches": (7 if world == 1 else 14) * args.steps,
+            "gather_check": gather_check,
             "clocks": clocks,
             "roofline": roof,
             "cpu_baseline": cpu,
@@ -398,6 +432,9 @@ def gpu_arm(args):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        graphs.clear()
+        torch.cuda.synchronize()
+        peers.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -292,6 +292,39 @@ B2_API int b2_swiglu(const b2_tensor *a, const b2_tensor *b, float alpha, b2_ten
                      void *stream);
 
 /*
+ * Multi-GPU support: device buffers shared between the processes of a group
+ * (one process per GPU) through CUDA IPC, for b2_allgather_cols.
+ *  b2_ipc_alloc: cudaMalloc of `bytes` (zero-filled) and its 64-byte IPC handle
+ *    (handle: caller buffer of 64 bytes).  Set-up only: this allocates.
+ *  b2_ipc_open / b2_ipc_close: map / unmap another process's buffer by handle.
+ *  b2_ipc_free: frees a b2_ipc_alloc buffer.
+ * No counterpart in onnx-light (its runtime is single-process, CPU-only).
+ */
+B2_API int b2_ipc_alloc(size_t bytes, void **ptr, void *handle);
+B2_API int b2_ipc_free(void *ptr);
+B2_API int b2_ipc_open(const void *handle, void **ptr);
+B2_API int b2_ipc_close(void *ptr);
+
+/*
+ * All-gather of column slices for column-sharded outputs (weights sharded
+ * along N, attention sharded by KV head): this rank's slice `local` [..., n]
+ * is stored into columns [rank n, (rank + 1) n) of every rank's full output
+ * peer_full[r] ([..., n_total], same dtype, rows contiguous), over NVLink; the
+ * call then waits (bounded, 5 s) until every rank's slice has arrived in its
+ * own full output.  peer_flags[r]: rank r's flag array (8 uint32, zeroed);
+ * counters: this rank's 2 uint32 (zeroed), kept by the kernel.  Every rank
+ * must issue the same sequence of gathers; a rank must not read its previous
+ * contents of a buffer after a later gather into that buffer has started.
+ * Stream-ordered and graph-capturable (no host synchronisation).  A peer that
+ * never arrives is reported by b2_kernel_status ("allgather_cols", code 1).
+ * Replaces the NCCL all-gather of output slices of the sharded configurations
+ * (no counterpart in onnx-light).
+ */
+B2_API int b2_allgather_cols(const b2_tensor *local, void *const *peer_full,
+                             uint32_t *const *peer_flags, uint32_t *counters, int world, int rank,
+                             int64_t n_total, void *stream);
+
+/*
  * Seeded synthetic inputs, identical to onnx-light's SplitMix64 generators
  * (onnx_light/onnx_core/runtime/kernels/random.cc:38-176), produced on the
  * device so that benchmark inputs never cross PCIe.  Not part of the hot path.

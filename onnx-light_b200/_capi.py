@@ -44,7 +44,8 @@ ONNX_TO_TORCH = {FLOAT: torch.float32, FLOAT16: torch.float16, BFLOAT16: torch.b
 EXPORTS = ("b2_version", "b2_last_error", "b2_dequantize_linear", "b2_dequantize_matmul",
            "b2_dequantize_matmul_noalloc", "b2_matmul_integer", "b2_qlinear_matmul", "b2_attention", "b2_attention_ex", "b2_synth_fill",
            "b2_convert", "b2_kernel_status", "b2_selftest_bounded_wait", "b2_selftest_gemm_timeout",
-           "b2_rms_normalization", "b2_rotary_embedding", "b2_swiglu")
+           "b2_rms_normalization", "b2_rotary_embedding", "b2_swiglu", "b2_ipc_alloc",
+           "b2_ipc_free", "b2_ipc_open", "b2_ipc_close", "b2_allgather_cols")
 
 
 class B2Tensor(C.Structure):
@@ -103,6 +104,12 @@ def lib() -> C.CDLL:
                 L.b2_rms_normalization.argtypes = [T, T, C.c_int64, C.c_float, T, P]
                 L.b2_rotary_embedding.argtypes = [T, T, T, T, C.c_int32, C.c_int64, C.c_int64, T, P]
                 L.b2_swiglu.argtypes = [T, T, C.c_float, T, P]
+                L.b2_ipc_alloc.argtypes = [C.c_size_t, C.POINTER(C.c_void_p), P]
+                L.b2_ipc_free.argtypes = [P]
+                L.b2_ipc_open.argtypes = [P, C.POINTER(C.c_void_p)]
+                L.b2_ipc_close.argtypes = [P]
+                L.b2_allgather_cols.argtypes = [T, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), P,
+                                                C.c_int, C.c_int, C.c_int64, P]
                 L.b2_synth_fill.argtypes = [C.c_int32, C.c_uint64, C.c_int64, C.c_double,
                                             C.c_double, P, P]
                 L.b2_convert.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int64, P]

@@ -24,6 +24,7 @@ int status_read_dq_gemm_tc(int reset);
 int status_read_imma_tc(int reset);
 int status_read_dq_gemv(int reset);
 int status_read_rotary(int reset);
+int status_read_allgather(int reset);
 
 __device__ int g_selftest_status;
 
@@ -58,6 +59,7 @@ extern "C" B2_API int b2_kernel_status(int reset) {
                       {"dq_gemm_tc", status_read_dq_gemm_tc, 0},
                       {"imma_tc", status_read_imma_tc, 0},
                       {"dq_gemv_i4h", status_read_dq_gemv, 0},
+                      {"allgather_cols", status_read_allgather, 0},
                       {"kernel::RotaryEmbedding", status_read_rotary, kOutOfRange}};
   int first = 0;
   for (const Src &s : srcs) {

@@ -9,13 +9,20 @@
   the KV cache of its heads and the matching query heads (GQA groups never
   straddle ranks), and the per-head outputs are all-gathered.
 
-The gather writes the rank-major buffer [world, M, N/world]; for M == 1 that is
-already the [M, N] layout, otherwise one transpose copy restores it.
+Two gathers:
+* `PeerGroup.gather` (GPUs): b2_allgather_cols stores each rank's slice straight
+  into the [M, N] output of every rank over NVLink (CUDA IPC peer buffers set
+  up once) and waits on per-rank arrival flags -- one kernel, no staging
+  buffer, graph-capturable;
+* `gather_columns` (any backend, gloo on CPU): a collective all-gather into the
+  rank-major buffer [world, M, N/world]; for M == 1 that is already the [M, N]
+  layout, otherwise one transpose copy restores it.
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
-from typing import Callable, Optional
+from typing import Callable, Dict, Optional
 
 import torch
 import torch.distributed as dist
@@ -91,3 +98,103 @@ def gather_heads(local_y: torch.Tensor, world: int, group=None) -> torch.Tensor:
     staging = torch.empty((world, B, h, S, D), dtype=local_y.dtype, device=local_y.device)
     dist.all_gather_into_tensor(staging.view(-1), local_y.contiguous().view(-1), group=group)
     return staging.permute(1, 0, 2, 3, 4).reshape(B, world * h, S, D)
+
+
+class _CudaArray:
+    """__cuda_array_interface__ view of a raw device allocation (for torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape),
+                                         "typestr": typestr, "version": 3, "strides": None}
+
+
+_TYPESTR = {torch.float16: "<f2", torch.bfloat16: "<u2", torch.float32: "<f4",
+            torch.int32: "<i4", torch.uint8: "|u1"}
+
+
+class PeerGroup:
+    """Peer-memory all-gather buffers of one process group (one rank per GPU).
+
+    `buffer(name, shape, dtype)` allocates a full output every rank can write
+    (CUDA IPC, exchanged once through the process group); `gather(name,
+    local)` runs b2_allgather_cols on the current stream: this rank's column
+    slice lands in every rank's `buffer(name)`, and the call returns once all
+    slices are in place here.  All ranks must create the same buffers and
+    issue the same gathers in the same order.  Set-up allocates and talks to
+    the process group; gathers do neither.
+    """
+
+    FLAGS = 8  # uint32 per flag array (b2_allgather_cols supports up to 8 ranks)
+
+    def __init__(self, group=None):
+        from . import _capi
+        self._capi = _capi
+        self.lib = _capi.lib()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > self.FLAGS:
+            raise ValueError(f"b2_allgather_cols supports up to {self.FLAGS} ranks")
+        self._own = []      # (ptr) allocations of this rank
+        self._opened = []   # peer mappings
+        self.bufs: Dict[str, tuple] = {}
+        # flags: one array per rank; counters: local only
+        flags_ptr, peers = self._shared(self.FLAGS * 4)
+        self.flag_ptrs = (C.c_void_p * self.world)(*peers)
+        ctr = C.c_void_p()
+        handle = C.create_string_buffer(64)
+        _capi.check(self.lib.b2_ipc_alloc(8, C.byref(ctr), handle))
+        self._own.append(ctr.value)
+        self.counters = ctr.value
+
+    def _shared(self, nbytes: int):
+        """Allocates nbytes here and maps every rank's allocation: (own, [per rank])."""
+        ptr = C.c_void_p()
+        handle = C.create_string_buffer(64)
+        self._capi.check(self.lib.b2_ipc_alloc(nbytes, C.byref(ptr), handle))
+        self._own.append(ptr.value)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=self.group)
+        peers = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                peers.append(ptr.value)
+                continue
+            p = C.c_void_p()
+            self._capi.check(self.lib.b2_ipc_open(C.create_string_buffer(h, 64), C.byref(p)))
+            self._opened.append(p.value)
+            peers.append(p.value)
+        return ptr.value, peers
+
+    def buffer(self, name: str, shape, dtype=torch.float16) -> torch.Tensor:
+        if name not in self.bufs:
+            nbytes = int(torch.tensor([], dtype=dtype).element_size())
+            for d in shape:
+                nbytes *= int(d)
+            own, peers = self._shared(nbytes)
+            t = torch.as_tensor(_CudaArray(own, shape, _TYPESTR[dtype]), device="cuda")
+            if dtype == torch.bfloat16:
+                t = t.view(torch.bfloat16)
+            self.bufs[name] = (t, (C.c_void_p * self.world)(*peers), int(shape[-1]))
+        return self.bufs[name][0]
+
+    def gather(self, name: str, local: torch.Tensor) -> torch.Tensor:
+        full, peers, n_total = self.bufs[name]
+        d = self._capi.Desc(local.data_ptr(), self._capi.TORCH_TO_ONNX[local.dtype],
+                            tuple(local.shape))
+        self._capi.check(self.lib.b2_allgather_cols(
+            d.ref, peers, self.flag_ptrs, C.c_void_p(self.counters), self.world, self.rank,
+            n_total, self._capi.stream_ptr(local.device)))
+        return full
+
+    def close(self):
+        torch.cuda.synchronize()
+        for p in self._opened:
+            self.lib.b2_ipc_close(C.c_void_p(p))
+        self._opened.clear()
+        dist.barrier(group=self.group)  # peers have unmapped before the memory goes
+        for p in self._own:
+            self.lib.b2_ipc_free(C.c_void_p(p))
+        self._own.clear()
+        self.bufs.clear()
+
