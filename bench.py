@@ -368,7 +368,6 @@ def gpu_arm(args):
                        "7 calls + D2H per step, captured in CUDA graphs"
                        + (" (+ b2_allgather_cols per call, max over ranks)" if world > 1 else "")}
         del ge
-        del ge
 
     # Sharded: the gathered full output of a step against the unsharded
     # projection computed on this rank (rel-L2, contract 1e-3).
@@ -393,6 +392,10 @@ def gpu_arm(args):
 
     # Secondary BASELINE metrics (same GPU, after the headline timing).
     secondary = None
+    if world > 1 and not args.no_secondary:
+        # the sharded configurations, every rank taking part
+        secondary = {"attention_config4_sharded":
+                     attention_config4_sharded(b2, synth, device, stream, peers, world, rank)}
     if rank == 0 and world == 1 and not args.no_secondary:
         want_cpu = not args.no_cpu_baseline
         secondary = {}
@@ -707,6 +710,79 @@ def attention_config4(b2, synth, device, stream, cpu):
     if cpu:
         out["cpu_baseline"] = _cpu_attention_sample()
     return out
+
+
+def attention_config4_sharded(b2, synth, device, stream, peers, world, rank):
+    """Config 4 sharded by KV head over `world` GPUs: rank r keeps the cache of
+    KV heads [r Hkv/world, (r+1) Hkv/world) and the matching query heads (GQA
+    groups never straddle ranks), runs the decode step on them and
+    b2_allgather_cols gathers the [B, Hq/world * D] head slices into every
+    rank's [B, Hq * D] output.  Fixed total work (strong scaling); tokens/s of
+    the whole group, step time max over ranks; the gathered output is checked
+    against an unsharded run on rank 0."""
+    import math
+    import torch
+    import torch.distributed as dist
+    B, Hq, Hkv, D, past = 32, 32, 8, 128, 4096
+    hk, hq = Hkv // world, Hq // world
+    n = B * Hkv * (past + 1) * D
+    kf = synth.convert(synth.randn(4001, (n,), 0.0, 0.5, device=device), FLOAT16, (B, Hkv, past + 1, D))
+    vf = synth.convert(synth.randn(4002, (n,), 0.0, 0.5, device=device), FLOAT16, (B, Hkv, past + 1, D))
+    qf = synth.convert(synth.randn(4003, (B * Hq * D,), 0.0, 0.5, device=device), FLOAT16, (B, Hq, 1, D))
+    knf = synth.convert(synth.randn(4004, (B * Hkv * D,), 0.0, 0.5, device=device), FLOAT16, (B, Hkv, 1, D))
+    vnf = synth.convert(synth.randn(4005, (B * Hkv * D,), 0.0, 0.5, device=device), FLOAT16, (B, Hkv, 1, D))
+    cache = b2.KVCache(B, hk, past + 1, D, device=device)
+    cache.k.copy_(kf[:, rank * hk:(rank + 1) * hk])
+    cache.v.copy_(vf[:, rank * hk:(rank + 1) * hk])
+    q = qf[:, rank * hq:(rank + 1) * hq].contiguous()
+    k = knf[:, rank * hk:(rank + 1) * hk].contiguous()
+    v = vnf[:, rank * hk:(rank + 1) * hk].contiguous()
+    y = torch.empty((B, hq, 1, D), dtype=torch.float16, device=device)
+    full = peers.buffer("attention4", (B, Hq * D), torch.float16)
+    att = b2.Attention()
+    attrs = b2.Attributes(has_scale=True, scale=1.0 / math.sqrt(D), is_causal=True)
+
+    def step():
+        cache.length = past
+        att(q, k, v, attrs, cache=cache, out=y)
+        peers.gather("attention4", y.view(B, hq * D))
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = _graph_time(stream, step, 512, chunk=32)
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # check: the gathered heads against one unsharded step (rank 0)
+    check = None
+    if rank == 0:
+        cache_f = b2.KVCache(B, Hkv, past + 1, D, device=device)
+        cache_f.k.copy_(kf)
+        cache_f.v.copy_(vf)
+        cache_f.length = past
+        yf = att(qf, knf, vnf, attrs, cache=cache_f).Y
+        torch.cuda.synchronize()
+        ref = yf.view(B, Hq * D).float()
+        check = float(((full.float() - ref).norm() / ref.norm()).item())
+        del cache_f, yf
+    dist.barrier()
+    nbytes = 537657344
+    peak, src = measured_peak()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    del kf, vf, cache
+    torch.cuda.empty_cache()
+    return {"metric": "GQA Attention decode tokens/s (config 4, sharded by KV head)",
+            "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+            "ms_per_step": round(ms, 5), "scaling": "strong",
+            "config": {"batch": B, "q_heads": Hq, "kv_heads": Hkv, "head": D, "past": past,
+                       "kv_heads_per_gpu": hk},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
+                         "peak": round(peak * world, 1), "unit": "GB/s",
+                         "frac": round(gbs / (peak * world), 4),
+                         "peak_source": f"{world} x {src}"},
+            "gather_check_rel_l2": check}
 
 
 def matmul_integer_config2(b2, synth, device, stream, cpu):
