@@ -68,15 +68,22 @@ __global__ void __launch_bounds__(AG_THREADS) allgather_cols_kernel(const AgArgs
   }
   __syncthreads();
   __shared__ bool last;
-  if (threadIdx.x == 0) {
-    asm volatile("fence.sc.sys;" ::: "memory"); // this CTA's peer stores, visible system-wide
-    const uint32_t prev = atomicAdd(&a.counters[0], 1u);
-    last = prev + 1 == gridDim.x;
+  if (gridDim.x == 1) {
+    // one CTA (a decode-sized slice): its stores are ordered before the flag
+    // stores below by the barrier and the release fence
+    if (threadIdx.x != 0) return;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+  } else {
+    if (threadIdx.x == 0) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory"); // this CTA's peer stores, system-wide
+      const uint32_t prev = atomicAdd(&a.counters[0], 1u);
+      last = prev + 1 == gridDim.x;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    a.counters[0] = 0u;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
   }
-  __syncthreads();
-  if (!last || threadIdx.x != 0) return;
-  a.counters[0] = 0u;
-  asm volatile("fence.sc.sys;" ::: "memory");
   const uint32_t gen = a.counters[1] + 1u;
   a.counters[1] = gen;
   for (int r = 0; r < a.world; ++r) st_release_sys(a.flags[r] + a.rank, gen);
@@ -91,7 +98,7 @@ __global__ void __launch_bounds__(AG_THREADS) allgather_cols_kernel(const AgArgs
         atomicExch(&g_allgather_status, tc::kTimeoutFull);
         return;
       }
-      __nanosleep(200);
+      __nanosleep(32);
     }
   }
 }
