@@ -247,6 +247,25 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
       prefetch_l2_2d(&map_w, (u / g.kunits) * (GM_TN / 2), (u % g.kunits) * GM_TK);
   }
   __syncthreads();
+  // The weights and scales are constants of the call, independent of the
+  // kernel launched ahead of this one: the first ring fill of each stage
+  // (weights + scales) is issued before waiting for that kernel, and only the
+  // activation boxes of those stages wait.  The stage's full barrier expects
+  // all three, so consumers see a stage only when its activations are in.
+  const uint32_t tx = GM_W_BYTES + L::kA + (uint32_t)g.srows * GM_TN * 2;
+  const int pre = nun < GM_STAGES ? nun : GM_STAGES;
+  auto load_weights = [&](int i) {
+    const int s = i % GM_STAGES;
+    const int u = u0 + i, tile = u / g.kunits, kb = u % g.kunits;
+    tc::mbar_expect_tx(&full[s], tx);
+    tc::tma_load_2d(sm + s * GM_W_BYTES, &map_w, &full[s], tile * (GM_TN / 2), kb * GM_TK);
+    if (g.srows) {
+      const int srow = g.block ? (kb * GM_TK) / g.block : 0;
+      tc::tma_load_2d(sm + L::kOffS + s * GM_SC_BYTES, &map_s, &full[s], tile * GM_TN, srow);
+    }
+  };
+  if (warp == GM_CONSUMERS && lane == 0)
+    for (int i = 0; i < pre; ++i) load_weights(i);
   // Everything below may read what the previous kernel on the stream wrote
   // (activations) or write what it reads (output, workspace).
   griddep_wait();
@@ -255,7 +274,6 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
   if (warp == GM_CONSUMERS) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
-      const uint32_t tx = GM_W_BYTES + L::kA + (uint32_t)g.srows * GM_TN * 2;
       for (int i = 0; i < nun; ++i) {
         const int s = i % GM_STAGES;
         if (i >= GM_STAGES && !tc::mbar_wait(&empty[s], ((i / GM_STAGES) - 1) & 1)) {
@@ -263,17 +281,11 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
           flags[0] = 1;
           break;
         }
-        const int u = u0 + i, tile = u / g.kunits, kb = u % g.kunits;
-        uint8_t *st = sm + s * GM_W_BYTES;
+        if (i >= pre) load_weights(i);
+        const int kb = (u0 + i) % g.kunits;
         uint8_t *sa = sm + L::kOffA + s * L::kA;
-        tc::mbar_expect_tx(&full[s], tx);
-        tc::tma_load_2d(st, &map_w, &full[s], tile * (GM_TN / 2), kb * GM_TK);
         tc::tma_load_2d(sa, &map_a, &full[s], kb * GM_TK, 0);
         tc::tma_load_2d(sa + L::kA / 2, &map_a, &full[s], kb * GM_TK + 64, 0);
-        if (g.srows) {
-          const int srow = g.block ? (kb * GM_TK) / g.block : 0;
-          tc::tma_load_2d(sm + L::kOffS + s * GM_SC_BYTES, &map_s, &full[s], tile * GM_TN, srow);
-        }
       }
     }
     return;
