@@ -44,3 +44,13 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.fail("GPU test run without a CUDA device")
     return torch.device("cuda:0")
+
+
+def pytest_sessionfinish(session, exitstatus):
+    path = os.environ.get("ONNXL_RELERR_LOG")
+    if not path:
+        return
+    import json
+    import util
+    with open(path, "w") as f:
+        json.dump(util.RELERR_LOG, f)

@@ -2,6 +2,8 @@
 generators, moving them to the device, and comparing results."""
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 import oracle as O
@@ -64,11 +66,18 @@ def to_dev(raw: np.ndarray, torch_dtype=None):
     return t.view(torch_dtype) if torch_dtype is not None else t
 
 
+# (test id, rel-L2) of every rel_l2 call; conftest writes them to the file named by
+# ONNXL_RELERR_LOG at the end of the session (the measured errors per dtype and kernel)
+RELERR_LOG = []
+
+
 def rel_l2(x: np.ndarray, ref: np.ndarray) -> float:
     x = np.asarray(x, np.float64)
     ref = np.asarray(ref, np.float64)
     den = np.linalg.norm(ref)
-    return float(np.linalg.norm(x - ref) / (den if den > 0 else 1.0))
+    v = float(np.linalg.norm(x - ref) / (den if den > 0 else 1.0))
+    RELERR_LOG.append((os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0], v))
+    return v
 
 
 def load_fixtures():
