@@ -404,6 +404,7 @@ def gpu_arm(args):
                                                                 want_cpu)
         secondary["dq_matmul_config1"] = dq_matmul_config1(b2, synth, device, stream, want_cpu)
         secondary["dequantize_linear"] = dequantize_standalone(b2, synth, device, stream, want_cpu)
+        secondary["decoder_ops"] = decoder_ops(b2, synth, device, stream, want_cpu)
         secondary["attention_config4"] = attention_config4(b2, synth, device, stream, want_cpu)
         secondary["matmul_integer_config2"] = matmul_integer_config2(b2, synth, device, stream,
                                                                      want_cpu)
@@ -636,6 +637,66 @@ def dequantize_standalone(b2, synth, device, stream, cpu):
     if cpu:
         out["cpu_baseline"] = _cpu_dq_sample()
     del w5, s5, y5
+    torch.cuda.empty_cache()
+    return out
+
+
+def decoder_ops(b2, synth, device, stream, cpu):
+    """The decoder-layer operators around the projections at the config-5
+    prefill shapes (bf16, B = 4, S = 8192, hidden 4096, 32 heads of 128,
+    intermediate 11008): RMSNormalization of the hidden state, RotaryEmbedding
+    of the queries (rank 3, cos/sin rows by position_ids) and SwiGLU of the
+    gate / up outputs.  All HBM-bound: bytes = inputs + outputs (every tensor
+    far above L2)."""
+    import torch
+    B, S, H, Dh, F = 4, 8192, 4096, 128, 11008
+    peak, src = measured_peak()
+    x = synth.convert(synth.randn(6001, (B * S * H,), 0.0, 1.0, device=device), BF16, (B, S, H))
+    sc = synth.convert(synth.uniform(6002, (H,), 0.5, 1.5, device=device), BF16, (H,))
+    y = torch.empty_like(x)
+    cos = synth.convert(synth.uniform(6003, (S * Dh // 2,), -1.0, 1.0, device=device), BF16,
+                        (S, Dh // 2))
+    sin = synth.convert(synth.uniform(6004, (S * Dh // 2,), -1.0, 1.0, device=device), BF16,
+                        (S, Dh // 2))
+    pos = torch.arange(S, dtype=torch.int64, device=device).repeat(B, 1)
+    ga = synth.convert(synth.randn(6005, (B * S * F,), 0.0, 1.0, device=device), BF16, (B * S, F))
+    ub = synth.convert(synth.randn(6006, (B * S * F,), 0.0, 1.0, device=device), BF16, (B * S, F))
+    gy = torch.empty_like(ga)
+    rms, rot, swi = b2.RMSNormalization(), b2.RotaryEmbedding(), b2.SwiGLU()
+    xb = x.numel() * 2
+    cases = [
+        ("rms_normalization", lambda: rms(x, sc, axis=-1, epsilon=1e-5, out=y),
+         2 * xb + H * 2, [x], y),
+        ("rotary_embedding", lambda: rot(x, cos, sin, pos, num_heads=H // Dh, out=y),
+         2 * xb + 2 * cos.numel() * 2 + pos.numel() * 8, [x], y),
+        ("swiglu", lambda: swi(ga, ub, 1.0, out=gy), 3 * ga.numel() * 2, [ga, ub], gy),
+    ]
+    out = {"metric": "decoder-layer ops HBM GB/s (config-5 shapes, bf16)", "unit": "GB/s",
+           "cases": {}}
+    for name, fn, nbytes, ins, yy in cases:
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        ms = _graph_time(stream, fn, 32, chunk=8)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        hosts = [(t, _pinned_like(t)) for t in ins]
+        for t, h in hosts:
+            h.copy_(t)
+        y_host = _pinned_like(yy)
+        e2e_ms, hb, db = _e2e(stream, fn, hosts, [(y_host, yy)], 4, 2)
+        out["cases"][name] = {
+            "value": round(gbs, 1), "ms_per_call": round(ms, 4),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_source": src,
+                         "algorithmic_bytes": nbytes},
+            "e2e": {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "ms_per_call": round(e2e_ms, 3), "h2d_bytes_per_step": hb,
+                    "d2h_bytes_per_step": db}}
+        del hosts, y_host
+    out["value"] = out["cases"]["rms_normalization"]["value"]
+    if cpu:
+        out["cpu_baseline"] = _cpu_decoder_sample()
+    del x, y, ga, ub, gy
     torch.cuda.empty_cache()
     return out
 
@@ -1138,6 +1199,36 @@ def _cpu_dq_sample():
         return {"value": None, "kind": "error", "sample": repr(e)[:200]}
 
 
+def _cpu_decoder_sample():
+    """Reference RMSNormalization, RotaryEmbedding and SwiGLU (bf16) on 1024 rows
+    of the config-5 shapes: bytes moved / time of the three calls."""
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import numpy as np
+        import oracle as O
+        if not O.ref_available():
+            return None
+        R, H, Dh, F, S = 1024, 4096, 128, 11008, 8192
+        x = O.f32_to_bf16_bits(O.randn(11, (1, R, H)))
+        sc = O.f32_to_bf16_bits(O.rand_uniform(12, (H,), 0.5, 1.5))
+        cs = O.f32_to_bf16_bits(O.rand_uniform(13, (S, Dh // 2), -1.0, 1.0))
+        sn = O.f32_to_bf16_bits(O.rand_uniform(14, (S, Dh // 2), -1.0, 1.0))
+        pos = np.arange(R, dtype=np.int64).reshape(1, R)
+        a = O.f32_to_bf16_bits(O.randn(15, (R, F)))
+        b = O.f32_to_bf16_bits(O.randn(16, (R, F)))
+        t0 = time.perf_counter()
+        O.ref_rms_normalization(x, sc, O.BFLOAT16, -1, 1e-5)
+        O.ref_rotary_embedding(x, cs, sn, O.BFLOAT16, pos, False, 0, H // Dh)
+        O.ref_swiglu(a, b, O.BFLOAT16, 1.0)
+        t = time.perf_counter() - t0
+        nbytes = 2 * x.nbytes + sc.nbytes + 2 * x.nbytes + 3 * a.nbytes
+        return {"value": round(nbytes / t / 1e9, 4), "unit": "GB/s", "cores": O.ref_thread_count(),
+                "kind": "reference",
+                "sample": f"1024 rows of each op's config-5 shape (bf16), {t * 1e3:.1f} ms for the three"}
+    except Exception as e:
+        return {"value": None, "kind": "error", "sample": repr(e)[:200]}
+
+
 def _cpu_mmi_sample():
     """Reference MatMulInteger (single-threaded in onnx-light) on N = 128
     columns of config 2, scaled to N = 11008."""
@@ -1253,7 +1344,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-4 attention and config-2 MatMulInteger measurements")
-    ap.add_argument("--only", choices=["attention4", "mmi2", "prefill5"],
+    ap.add_argument("--only", choices=["attention4", "mmi2", "prefill5", "decoder"],
                     help="run one secondary measurement alone on cuda:0 (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -1265,7 +1356,7 @@ def main():
         device = torch.device("cuda", 0)
         stream = torch.cuda.Stream(device)
         fn = {"attention4": attention_config4, "mmi2": matmul_integer_config2,
-              "prefill5": prefill_config5}[args.only]
+              "prefill5": prefill_config5, "decoder": decoder_ops}[args.only]
         print(json.dumps(fn(b2, synth, device, stream, False)), flush=True)
         return
     if args.impl == "reference":

@@ -703,11 +703,13 @@ static int wbits(int dt) {
   return 0;
 }
 
-// Kernel selection.  ONNXL_B200_DQ_KERNEL=tc|gemv|simt forces one family
-// (tests use it to exercise every kernel on the same shapes); the default
-// picks the decode GEMV for M <= 4, the tensor-core kernel for 16-bit
-// activations otherwise, and the CUDA-core GEMM for FLOAT activations.
-enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3, kPathMma = 4 };
+// Kernel selection.  ONNXL_B200_DQ_KERNEL=tc|gemv|simt|mma|f32 forces one
+// family (tests use it to exercise every kernel on the same shapes); the
+// default picks the register-MMA decode kernel for int4 / fp16 up to 16 rows,
+// the tensor-core kernel for other 16-bit activations, the CUDA-core GEMV for
+// one or two rows, dq_gemm_f32 for FLOAT activations with integer weights,
+// and the generic CUDA-core GEMM for the rest.
+enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3, kPathMma = 4, kPathF32 = 5 };
 
 static DqPath forced_path() {
   const char *e = getenv("ONNXL_B200_DQ_KERNEL");
@@ -716,6 +718,7 @@ static DqPath forced_path() {
   if (!strcmp(e, "gemv")) return kPathGemv;
   if (!strcmp(e, "simt")) return kPathSimt;
   if (!strcmp(e, "mma")) return kPathMma;
+  if (!strcmp(e, "f32")) return kPathF32;
   return kPathAuto;
 }
 
@@ -771,6 +774,11 @@ static Plan make_plan(const DqMmParams &p) {
       pl.smem = (size_t)pl.mt * pl.kchunk * 4 + red;
     }
     pl.ws = kCounterBytes + (pl.ksplit > 1 ? (size_t)pl.ksplit * p.M * p.N * 4 : 0);
+    return pl;
+  }
+  if ((forced == kPathAuto || forced == kPathF32) && dq_f32_eligible(p)) {
+    pl.kind = 4;
+    pl.ws = dq_f32_workspace(p);
     return pl;
   }
   pl.kind = 0;
@@ -872,10 +880,11 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
     B2_CUDA(cudaMemsetAsync(y->data, 0, (size_t)p.M * p.N * (p.ydt == kFloat ? 4 : 2), st));
     return B2_OK;
   }
-  if (pl.kind == 3) {
-    if (dq_mma_aligned(p)) return dq_mma_launch(p, workspace, st);
-    // TMA needs 16-byte aligned tensors: fall back to the unsplit CUDA-core
-    // kernel, which needs no workspace.
+  if (pl.kind == 3 || pl.kind == 4) {
+    if (pl.kind == 3 && dq_mma_aligned(p)) return dq_mma_launch(p, workspace, st);
+    if (pl.kind == 4 && dq_f32_aligned(p)) return dq_f32_launch(p, workspace, st);
+    // TMA / vector loads need aligned tensors: fall back to the unsplit
+    // CUDA-core kernel, which needs no workspace.
     Plan one;
     one.kchunk = p.K;
     one.ksplit = 1;
@@ -883,6 +892,7 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
                     (unsigned)((p.M + SIMT_BM - 1) / SIMT_BM), 1);
     p.kchunk = p.K;
     p.ksplit = 1;
+    if (pl.kind == 4) return launch_simt<float>(p, one, st);
     return launch_simt<__half>(p, one, st);
   }
   if (pl.kind == 2) return dq_tc_launch(p, workspace, st);

@@ -53,4 +53,11 @@ bool dq_mma_aligned(const DqMmParams &p);  // pointer alignment TMA needs
 size_t dq_mma_workspace(const DqMmParams &p);
 int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
 
+// FLOAT-activation path on CUDA cores (dq_gemm_f32.cu): INT4 / UINT4 / INT8 /
+// UINT8 weights, per-tensor, per-column or K-blocked scales, FLOAT output.
+bool dq_f32_eligible(const DqMmParams &p); // shape/type constraints
+bool dq_f32_aligned(const DqMmParams &p);  // pointer alignment of its vector loads
+size_t dq_f32_workspace(const DqMmParams &p);
+int dq_f32_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
+
 } // namespace b2

@@ -316,3 +316,49 @@ def test_workspace_is_per_stream(b2, cuda):
     w2 = kernels.workspace(torch.device("cuda", 0), 1 << 20, s2)
     assert w1.data_ptr() != w2.data_ptr()
     assert kernels.workspace(torch.device("cuda", 0), 1 << 20, s1).data_ptr() == w1.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# FLOAT activations with integer weights (dq_gemm_f32, the default for them
+# from 3 rows): every weight type, scale type and layout it takes, ragged
+# rows / columns / K, one and several row tiles and split-K.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("wdt,s_dt,cast,axis,block,zp", [
+    (O.INT4, O.FLOAT, 0, 0, 32, True),        # config 1's layout
+    (O.UINT4, O.FLOAT, 0, 0, 64, False),
+    (O.INT8, O.FLOAT, 0, 0, 96, True),        # blocks that straddle the warps' K slices
+    (O.UINT8, O.FLOAT, O.FLOAT, 1, None, True),  # per-column scales
+    (O.INT4, O.FLOAT16, O.FLOAT, 0, 32, True),   # FLOAT16 DequantizeLinear output + Cast
+    (O.UINT4, O.FLOAT16, O.FLOAT, 0, 0, True),   # per-tensor
+])
+@pytest.mark.parametrize("M,K,N", [(3, 1000, 196), (16, 512, 384), (33, 2048, 260), (70, 256, 4100)])
+def test_fp32_chain_kernel(b2, cuda, monkeypatch, wdt, s_dt, cast, axis, block, zp, M, K, N):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "f32")
+    if block and K % block:
+        K = (K // block + 1) * block
+    y, ref = run_case(b2, M, K, N, wdt, s_dt, O.FLOAT, axis, block, zp, cast, seed=M + K)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT], rel_l2(y, ref)
+
+
+def test_fp32_chain_config1_split_k_is_deterministic(b2, cuda):
+    # config 1 takes dq_gemm_f32 with split-K; repeated calls are bit-identical
+    # and agree with the generic CUDA-core GEMM within the contract
+    outs = [run_case(b2, 32, 4096, 4096, O.INT4, O.FLOAT, O.FLOAT, block=32, zp=True, seed=5,
+                     lead=(1, 32)) for _ in range(3)]
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[1][0], outs[2][0])
+    assert rel_l2(outs[0][0], outs[0][1]) <= TOL[O.FLOAT]
+
+
+def test_fp32_chain_unaligned_activations_fall_back(b2, cuda):
+    # activations one float past a 16-byte boundary: the generic kernel runs
+    K, N, M = 256, 192, 9
+    w = b2.QTensor(to_dev(random_q(3, (K, N), O.INT4)), O.INT4, (K, N))
+    s = to_dev(O.rand_uniform(4, (K // 32 * N,), 0.002, 0.02)).reshape(K // 32, N)
+    base = torch.from_numpy(O.randn(5, (M * K + 1,))).cuda()
+    a_off = base[1:].view(M, K)
+    a_al = a_off.clone()
+    y_off = b2.DequantizeMatMul()(a_off, w, s, axis=0)
+    y_al = b2.DequantizeMatMul()(a_al, w, s, axis=0)
+    torch.cuda.synchronize()
+    assert rel_l2(y_off.cpu().numpy(), y_al.cpu().numpy()) <= TOL[O.FLOAT]
