@@ -709,7 +709,8 @@ static int wbits(int dt) {
 // the tensor-core kernel for other 16-bit activations, the CUDA-core GEMV for
 // one or two rows, dq_gemm_f32 for FLOAT activations with integer weights,
 // and the generic CUDA-core GEMM for the rest.
-enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3, kPathMma = 4, kPathF32 = 5 };
+enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3, kPathMma = 4, kPathF32 = 5,
+              kPathX = 6, kPathN = 7, kPathC = 8 };
 
 static DqPath forced_path() {
   const char *e = getenv("ONNXL_B200_DQ_KERNEL");
@@ -719,6 +720,9 @@ static DqPath forced_path() {
   if (!strcmp(e, "simt")) return kPathSimt;
   if (!strcmp(e, "mma")) return kPathMma;
   if (!strcmp(e, "f32")) return kPathF32;
+  if (!strcmp(e, "x")) return kPathX;
+  if (!strcmp(e, "n")) return kPathN;
+  if (!strcmp(e, "c")) return kPathC;
   return kPathAuto;
 }
 
@@ -735,6 +739,21 @@ static Plan make_plan(const DqMmParams &p) {
                        (p.slayout != kScaleAxis0Block || p.block % 32 == 0) &&
                        ((p.N * bits / 8) % 16 == 0);
   const DqPath forced = forced_path();
+  if (forced == kPathC && dq_c_eligible(p)) {
+    pl.kind = 7;
+    pl.ws = 0;
+    return pl;
+  }
+  if (forced == kPathN && dq_n_eligible(p)) {
+    pl.kind = 6;
+    pl.ws = 0;
+    return pl;
+  }
+  if (forced == kPathX && dq_x_eligible(p)) {
+    pl.kind = 5;
+    pl.ws = dq_x_workspace(p);
+    return pl;
+  }
   if ((forced == kPathAuto || forced == kPathMma) && dq_mma_eligible(p)) {
     pl.kind = 3;
     pl.ws = dq_mma_workspace(p);
@@ -880,8 +899,11 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
     B2_CUDA(cudaMemsetAsync(y->data, 0, (size_t)p.M * p.N * (p.ydt == kFloat ? 4 : 2), st));
     return B2_OK;
   }
-  if (pl.kind == 3 || pl.kind == 4) {
+  if (pl.kind >= 3 && pl.kind <= 7) {
     if (pl.kind == 3 && dq_mma_aligned(p)) return dq_mma_launch(p, workspace, st);
+    if (pl.kind == 5 && dq_mma_aligned(p)) return dq_x_launch(p, workspace, st);
+    if (pl.kind == 6 && dq_mma_aligned(p)) return dq_n_launch(p, st);
+    if (pl.kind == 7 && dq_mma_aligned(p)) return dq_c_launch(p, st);
     if (pl.kind == 4 && dq_f32_aligned(p)) return dq_f32_launch(p, workspace, st);
     // TMA / vector loads need aligned tensors: fall back to the unsplit
     // CUDA-core kernel, which needs no workspace.

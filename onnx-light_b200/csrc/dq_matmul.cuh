@@ -53,6 +53,22 @@ bool dq_mma_aligned(const DqMmParams &p);  // pointer alignment TMA needs
 size_t dq_mma_workspace(const DqMmParams &p);
 int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
 
+// Decode path with the reference's exact fp16 weights (dq_gemv_x.cu): M <= 64,
+// INT4/UINT4 weights, FLOAT16 scales, activations and output.
+bool dq_x_eligible(const DqMmParams &p); // shape/type constraints (pointer alignment: dq_mma_aligned)
+size_t dq_x_workspace(const DqMmParams &p);
+int dq_x_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
+
+// Decode path on narrow column tiles without split-K (dq_gemv_n.cu): M <= 32,
+// INT4/UINT4 weights, FLOAT16 scales, activations and output; no workspace.
+bool dq_n_eligible(const DqMmParams &p); // shape/type constraints (pointer alignment: dq_mma_aligned)
+int dq_n_launch(const DqMmParams &p, cudaStream_t stream);
+
+// Decode path split along K inside thread-block clusters (dq_gemv_c.cu): M <=
+// 32, INT4/UINT4 weights, FLOAT16 scales, activations and output; no workspace.
+bool dq_c_eligible(const DqMmParams &p); // shape/type constraints (pointer alignment: dq_mma_aligned)
+int dq_c_launch(const DqMmParams &p, cudaStream_t stream);
+
 // FLOAT-activation path on CUDA cores (dq_gemm_f32.cu): INT4 / UINT4 / INT8 /
 // UINT8 weights, per-tensor, per-column or K-blocked scales, FLOAT output.
 bool dq_f32_eligible(const DqMmParams &p); // shape/type constraints

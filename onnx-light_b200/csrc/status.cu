@@ -25,6 +25,10 @@ int status_read_imma_tc(int reset);
 int status_read_dq_gemv(int reset);
 int status_read_rotary(int reset);
 int status_read_allgather(int reset);
+int status_read_dq_gemm_f32(int reset);
+int status_read_gemv_x(int reset);
+int status_read_gemv_n(int reset);
+int status_read_gemv_c(int reset);
 
 __device__ int g_selftest_status;
 
@@ -53,12 +57,16 @@ extern "C" B2_API int b2_kernel_status(int reset) {
   constexpr int kOutOfRange = 4;
   struct Src { const char *name; int (*read)(int); int code; };
   const Src srcs[] = {{"dq_gemv_mma", status_read_gemv_mma, 0},
+                      {"dq_gemv_x", status_read_gemv_x, 0},
+                      {"dq_gemv_n", status_read_gemv_n, 0},
+                      {"dq_gemv_c", status_read_gemv_c, 0},
                       {"attn_decode_mma", status_read_attn_decode, 0},
                       {"attn_prefill_mma", status_read_attn_prefill, 0},
                       {"attn_prefill_tc", status_read_attn_prefill_tc, 0},
                       {"dq_gemm_tc", status_read_dq_gemm_tc, 0},
                       {"imma_tc", status_read_imma_tc, 0},
                       {"dq_gemv_i4h", status_read_dq_gemv, 0},
+                      {"dq_gemm_f32", status_read_dq_gemm_f32, 0},
                       {"allgather_cols", status_read_allgather, 0},
                       {"kernel::RotaryEmbedding", status_read_rotary, kOutOfRange}};
   int first = 0;

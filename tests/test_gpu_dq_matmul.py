@@ -362,3 +362,172 @@ def test_fp32_chain_unaligned_activations_fall_back(b2, cuda):
     y_al = b2.DequantizeMatMul()(a_al, w, s, axis=0)
     torch.cuda.synchronize()
     assert rel_l2(y_off.cpu().numpy(), y_al.cpu().numpy()) <= TOL[O.FLOAT]
+
+
+# ---------------------------------------------------------------------------
+# Decode path with the reference's exact fp16 weights (dq_gemv_x, forced with
+# ONNXL_B200_DQ_KERNEL=x): one to eight activation tiles, two row passes,
+# stream-K splits, every scale layout it takes, ragged shapes.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M", [1, 2, 5, 8, 9, 16, 17, 32, 33, 64])
+def test_exact_decode_config3_batches(b2, cuda, monkeypatch, M):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "x")
+    y, ref = run_case(b2, M, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=60 + M)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16], rel_l2(y, ref)
+
+
+@pytest.mark.parametrize("K,N", [(11008, 4096), (4096, 11008), (1000, 4128), (200, 96)])
+def test_exact_decode_shapes(b2, cuda, monkeypatch, K, N):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "x")
+    for M in (1, 12, 40):
+        y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=None, axis=1, seed=K + M)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+@pytest.mark.parametrize("wdt,block,axis", [(O.INT4, 32, 0), (O.UINT4, 64, 0), (O.INT4, 256, 0),
+                                            (O.UINT4, 0, 0), (O.INT4, None, 1)])
+def test_exact_decode_scale_layouts(b2, cuda, monkeypatch, wdt, block, axis):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "x")
+    K = 512 if block != 256 else 768
+    for M in (3, 24):
+        y, ref = run_case(b2, M, K, 512, wdt, O.FLOAT16, O.FLOAT16, axis=axis, block=block, seed=M + 71)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+def test_exact_decode_weights_match_the_reference_rounding(b2, cuda, monkeypatch):
+    # a single activation row that is one-hot at k selects row k of the
+    # dequantized weight: the kernel's weights equal the reference's fp16
+    # DequantizeLinear output bit for bit (scales spanning normal and
+    # subnormal products)
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "x")
+    K, N = 256, 256
+    w = random_q(5, (K, N), O.INT4)
+    s = scale_raw(np.concatenate([O.rand_uniform(6, (N,), 1e-6, 1e-4),
+                                  O.rand_uniform(7, (N,), 0.002, 300.0)]), O.FLOAT16)
+    s_shape = (K // 128, N)
+    wq = O.dequantize_linear(w, O.INT4, (K, N), s, O.FLOAT16, s_shape, None, None, 0)
+    tw = b2.QTensor(to_dev(w), O.INT4, (K, N))
+    ts = to_dev(s, torch.float16).reshape(s_shape)
+    for k in (0, 77, 200):
+        a = torch.zeros((1, K), dtype=torch.float16, device="cuda")
+        a[0, k] = 1.0
+        y = b2.DequantizeMatMul()(a, tw, ts, None, axis=0)
+        torch.cuda.synchronize()
+        got = y.view(torch.int16).cpu().numpy().reshape(N).view(np.uint16)
+        assert np.array_equal(got, wq.reshape(K, N)[k]), k
+
+
+def test_exact_decode_repeated_calls_are_identical(b2, cuda, monkeypatch):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "x")
+    outs = [run_case(b2, 33, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=3)[0]
+            for _ in range(3)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
+# ---------------------------------------------------------------------------
+# Decode path on narrow column tiles (dq_gemv_n, forced with
+# ONNXL_B200_DQ_KERNEL=n): whole K per CTA, several tiles per CTA, chunks of
+# 256 / 128 / 64 rows, every scale layout it takes.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 17, 32])
+def test_narrow_decode_config3_batches(b2, cuda, monkeypatch, M):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "n")
+    y, ref = run_case(b2, M, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=80 + M)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16], rel_l2(y, ref)
+
+
+@pytest.mark.parametrize("K,N", [(11008, 4096), (4096, 11008), (1000, 4128), (200, 96), (4096, 32)])
+def test_narrow_decode_shapes(b2, cuda, monkeypatch, K, N):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "n")
+    for M in (1, 12, 30):
+        y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=None, axis=1, seed=K + M + 1)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+@pytest.mark.parametrize("wdt,block,axis", [(O.INT4, 16, 0), (O.UINT4, 64, 0), (O.INT4, 512, 0),
+                                            (O.UINT4, 0, 0), (O.INT4, None, 1)])
+def test_narrow_decode_scale_layouts(b2, cuda, monkeypatch, wdt, block, axis):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "n")
+    K = 1024
+    for M in (2, 20):
+        y, ref = run_case(b2, M, K, 512, wdt, O.FLOAT16, O.FLOAT16, axis=axis, block=block, seed=M + 91)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+def test_narrow_decode_weights_match_the_reference_rounding(b2, cuda, monkeypatch):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "n")
+    K, N = 512, 64
+    w = random_q(15, (K, N), O.INT4)
+    s = scale_raw(np.concatenate([O.rand_uniform(16, (2 * N,), 1e-6, 1e-4),
+                                  O.rand_uniform(17, (2 * N,), 0.002, 300.0)]), O.FLOAT16)
+    s_shape = (K // 128, N)
+    wq = O.dequantize_linear(w, O.INT4, (K, N), s, O.FLOAT16, s_shape, None, None, 0)
+    tw = b2.QTensor(to_dev(w), O.INT4, (K, N))
+    ts = to_dev(s, torch.float16).reshape(s_shape)
+    for k in (0, 130, 300, 511):
+        a = torch.zeros((1, K), dtype=torch.float16, device="cuda")
+        a[0, k] = 1.0
+        y = b2.DequantizeMatMul()(a, tw, ts, None, axis=0)
+        torch.cuda.synchronize()
+        got = y.view(torch.int16).cpu().numpy().reshape(N).view(np.uint16)
+        assert np.array_equal(got, wq.reshape(K, N)[k]), k
+
+
+# ---------------------------------------------------------------------------
+# Decode path split along K inside clusters (dq_gemv_c, forced with
+# ONNXL_B200_DQ_KERNEL=c): clusters of 8 / 4 / 2 / 1, more tiles than
+# clusters, ragged shapes, every scale layout it takes.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 17, 32])
+def test_cluster_decode_config3_batches(b2, cuda, monkeypatch, M):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+    y, ref = run_case(b2, M, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=100 + M)
+    assert rel_l2(y, ref) <= TOL[O.FLOAT16], rel_l2(y, ref)
+
+
+@pytest.mark.parametrize("K,N", [(11008, 4096), (4096, 11008), (1000, 4128), (200, 96), (384, 64),
+                                 (128, 8192)])
+def test_cluster_decode_shapes(b2, cuda, monkeypatch, K, N):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+    for M in (1, 12, 30):
+        y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=None, axis=1, seed=K + M + 2)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+@pytest.mark.parametrize("wdt,block,axis", [(O.INT4, 32, 0), (O.UINT4, 64, 0), (O.INT4, 256, 0),
+                                            (O.UINT4, 0, 0), (O.INT4, None, 1)])
+def test_cluster_decode_scale_layouts(b2, cuda, monkeypatch, wdt, block, axis):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+    K = 1024
+    for M in (2, 20):
+        y, ref = run_case(b2, M, K, 512, wdt, O.FLOAT16, O.FLOAT16, axis=axis, block=block, seed=M + 93)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+def test_cluster_decode_weights_match_the_reference_rounding(b2, cuda, monkeypatch):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+    K, N = 1024, 256
+    w = random_q(25, (K, N), O.INT4)
+    s = scale_raw(np.concatenate([O.rand_uniform(26, (4 * N,), 1e-6, 1e-4),
+                                  O.rand_uniform(27, (4 * N,), 0.002, 300.0)]), O.FLOAT16)
+    s_shape = (K // 128, N)
+    wq = O.dequantize_linear(w, O.INT4, (K, N), s, O.FLOAT16, s_shape, None, None, 0)
+    tw = b2.QTensor(to_dev(w), O.INT4, (K, N))
+    ts = to_dev(s, torch.float16).reshape(s_shape)
+    for k in (0, 130, 700, 1023):
+        a = torch.zeros((1, K), dtype=torch.float16, device="cuda")
+        a[0, k] = 1.0
+        y = b2.DequantizeMatMul()(a, tw, ts, None, axis=0)
+        torch.cuda.synchronize()
+        got = y.view(torch.int16).cpu().numpy().reshape(N).view(np.uint16)
+        assert np.array_equal(got, wq.reshape(K, N)[k]), k
+
+
+def test_cluster_decode_repeated_calls_are_identical(b2, cuda, monkeypatch):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+    outs = [run_case(b2, 5, 4096, 11008, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=4)[0]
+            for _ in range(3)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])

@@ -69,9 +69,11 @@ def test_noalloc_matches_oracle_twice_in_a_row(b2, cuda, M):
         assert rel_l2(got, ws) <= 1e-3
 
 
-def test_noalloc_rejects_plans_beyond_the_fixed_scratch(b2, cuda):
-    # FLOAT activations, 64 x 16384 outputs split in two along K: the split-K
-    # partials alone are 2 x 64 x 16384 x 4 bytes = 8 MiB, beyond the fixed scratch.
+def test_noalloc_rejects_plans_beyond_the_fixed_scratch(b2, cuda, monkeypatch):
+    # FLOAT activations on the generic CUDA-core GEMM, 64 x 16384 outputs split
+    # in two along K: the split-K partials alone are 2 x 64 x 16384 x 4 bytes =
+    # 8 MiB, beyond the fixed scratch.
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "simt")
     from onnx_light_b200 import _capi as capi
     K, N, M = 4096, 16384, 64
     w = torch.zeros((K * N // 2,), dtype=torch.uint8, device="cuda")
