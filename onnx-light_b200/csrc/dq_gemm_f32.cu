@@ -55,8 +55,7 @@ int status_read_dq_gemm_f32(int reset) {
 
 namespace {
 
-constexpr int F32_CONSUMERS = 8;                         // warps (all consume; lane 0 of warp 0 also loads)
-constexpr int F32_THREADS = F32_CONSUMERS * 32;
+constexpr int F32_KWARPS = 8;                            // warps splitting a stage's K rows (16 each)
 constexpr int F32_TN = 128;                              // columns per CTA (4 per lane)
 constexpr int F32_SK = 128;                              // K rows per stage (16 per warp)
 constexpr int F32_MAXST = 8;                             // ring stages at most
@@ -141,18 +140,26 @@ __device__ __forceinline__ void ffma2(float &c0, float &c1, float a, float b0, f
   asm("mov.b64 {%0, %1}, %2;" : "=f"(c0), "=f"(c1) : "l"(c));
 }
 
-// RG: K rows per activation load (4: one 128-bit load per activation row;
-// 2 for MR = 32, which keeps the 128 accumulators and the dequantized rows in
-// registers without spilling).
-template <int BITS, int MR, int RG = (MR >= 32 ? 2 : 4)>
-__global__ void __launch_bounds__(F32_THREADS, 1)
+// GROUPS groups of eight warps; group gr owns activation rows
+// [gr MRW, (gr + 1) MRW) of the CTA's MR = GROUPS * MRW, and its eight warps
+// split every stage's 128 K rows (16 each).  Two groups of 16 rows (512
+// threads, <= 128 registers each) rather than one group of 32 rows keep four
+// warps per scheduler to hide the shared-memory latency.
+// RG: K rows per activation load (a 128-bit load per activation row for 4,
+// 64-bit for 2: 16 rows per warp keep 64 accumulators and two dequantized
+// rows within 128 registers).
+template <int BITS, int MRW, int GROUPS, int RG = (MRW >= 16 ? 2 : 4)>
+__global__ void __launch_bounds__(GROUPS * F32_KWARPS * 32, 1)
     dq_gemm_f32(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                 const F32Args g) {
   extern __shared__ uint8_t dsm[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 127) & ~uintptr_t(127));
   const size_t ring = (size_t)g.stages * g.stage_bytes;
-  const size_t red_bytes = (size_t)F32_CONSUMERS * MR * F32_TN * 4;
+  constexpr int MR = MRW * GROUPS;
+  constexpr int NWARPS = GROUPS * F32_KWARPS;
+  constexpr int NTHREADS = NWARPS * 32;
+  const size_t red_bytes = (size_t)F32_KWARPS * MR * F32_TN * 4;
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + (ring > red_bytes ? ring : red_bytes));
   uint64_t *empty = full + F32_MAXST;
   volatile int *flags = reinterpret_cast<volatile int *>(empty + F32_MAXST); // [0] abort, [1] last
@@ -168,7 +175,7 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < g.stages; ++i) {
       tc::mbar_init(&full[i], 1);
-      tc::mbar_init(&empty[i], F32_CONSUMERS);
+      tc::mbar_init(&empty[i], NWARPS);
     }
     flags[0] = 0;
     flags[1] = 0;
@@ -205,9 +212,10 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
   const int n = n0 + lane * 4;
   const bool col_ok = n < g.N; // N % 4 == 0: all four columns or none
   const int mrows = min(MR, g.M - m0);
-  float acc[MR][4];
+  const int kw = warp % F32_KWARPS, grp = warp / F32_KWARPS;
+  float acc[MRW][4];
 #pragma unroll
-  for (int m = 0; m < MR; ++m)
+  for (int m = 0; m < MRW; ++m)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[m][i] = 0.0f;
   float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -232,7 +240,7 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
                    g.zp ? g.zp + (size_t)n * BITS / 8 : nullptr, g.s_f16, g.is_signed, s, mz);
     }
   }
-  const int r0 = warp * (F32_SK / F32_CONSUMERS); // this warp's 16 rows of every stage
+  const int r0 = kw * (F32_SK / F32_KWARPS); // this warp's 16 rows of every stage
   bool ok = true;
   for (int i = 0; i < nst; ++i) {
     const int sl = i % g.stages;
@@ -252,7 +260,7 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
                      g.has_zp ? st + g.off_z + (size_t)srow * F32_TN * BITS / 8 + lane * BITS / 2 : nullptr,
                      g.s_f16, g.is_signed, s, mz);
       }
-      const float *as = reinterpret_cast<const float *>(st);
+      const float *as = reinterpret_cast<const float *>(st) + grp * MRW * F32_SK; // this group's rows
       const uint8_t *ws = st + g.off_w + lane * (BITS / 2);
 #pragma unroll
       for (int rq = 0; rq < 16; rq += RG) {
@@ -271,11 +279,11 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
           }
         }
 #pragma unroll
-        for (int m = 0; m < MR; ++m) {
+        for (int m = 0; m < MRW; ++m) {
           float av[RG];
-          if (RG == 4) {
+          if constexpr (RG == 4) {
             const float4 a4 = *reinterpret_cast<const float4 *>(as + m * F32_SK + r0 + rq);
-            av[0] = a4.x, av[1] = a4.y, av[RG > 2 ? 2 : 0] = a4.z, av[RG > 3 ? 3 : 0] = a4.w;
+            av[0] = a4.x, av[1] = a4.y, av[2] = a4.z, av[3] = a4.w;
           } else {
             const float2 a2 = *reinterpret_cast<const float2 *>(as + m * F32_SK + r0 + rq);
             av[0] = a2.x, av[1] = a2.y;
@@ -311,19 +319,19 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
   __syncthreads();
   float4 *red = reinterpret_cast<float4 *>(sm); // [warp][m][32 lanes]
 #pragma unroll
-  for (int m = 0; m < MR; ++m)
-    red[(warp * MR + m) * 32 + lane] = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
+  for (int m = 0; m < MRW; ++m)
+    red[(kw * MR + grp * MRW + m) * 32 + lane] = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
   __syncthreads();
   const bool direct = g.ksplit == 1;
   const bool abort = flags[0] != 0;
   const float *redf = reinterpret_cast<const float *>(sm);
   float *part = g.partials + (int64_t)split * g.M * g.N;
-  for (int e = threadIdx.x; e < MR * F32_TN; e += F32_CONSUMERS * 32) {
+  for (int e = threadIdx.x; e < MR * F32_TN; e += NTHREADS) {
     const int m = e / F32_TN, c = e % F32_TN;
     if (abort || m >= mrows || n0 + c >= g.N) continue;
     float v = 0.0f;
 #pragma unroll
-    for (int w = 0; w < F32_CONSUMERS; ++w) v += redf[((w * MR + m) * 32) * 4 + c];
+    for (int w = 0; w < F32_KWARPS; ++w) v += redf[((w * MR + m) * 32) * 4 + c];
     const int64_t o = (int64_t)(m0 + m) * g.N + n0 + c;
     if (direct) g.y[o] = v;
     else part[o] = v;
@@ -342,7 +350,7 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
   }
   __syncthreads();
   if (!flags[1]) return;
-  for (int e = threadIdx.x; e < MR * F32_TN; e += F32_CONSUMERS * 32) {
+  for (int e = threadIdx.x; e < MR * F32_TN; e += NTHREADS) {
     const int m = e / F32_TN, c = e % F32_TN;
     if (m >= mrows || n0 + c >= g.N) continue;
     const int64_t o = (int64_t)(m0 + m) * g.N + n0 + c;
@@ -393,14 +401,15 @@ F32Plan f32_plan(const DqMmParams &p) {
   const int nst = (int)(kchunk / F32_SK);
   pl.stages = (int)std::min<size_t>(F32_RING_BUDGET / pl.stage_bytes, F32_MAXST);
   pl.stages = std::max(1, std::min(pl.stages, nst));
-  const size_t red = (size_t)F32_CONSUMERS * pl.mr * F32_TN * 4;
+  const size_t red = (size_t)F32_KWARPS * pl.mr * F32_TN * 4;
   const size_t ring = (size_t)pl.stages * pl.stage_bytes;
   pl.smem = std::max(ring, red) + 2 * F32_MAXST * 8 + 16 + 128;
   return pl;
 }
 
-template <int BITS, int MR>
+template <int BITS, int MRW, int GROUPS>
 int f32_launch_t(const DqMmParams &p, const F32Plan &pl, F32Args &g, cudaStream_t st) {
+  constexpr int MR = MRW * GROUPS;
   CUtensorMap map_a, map_w, map_s, map_z;
   {
     const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
@@ -439,9 +448,9 @@ int f32_launch_t(const DqMmParams &p, const F32Plan &pl, F32Args &g, cudaStream_
       if (rc) return rc;
     }
   }
-  auto kern = dq_gemm_f32<BITS, MR>;
+  auto kern = dq_gemm_f32<BITS, MRW, GROUPS>;
   B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
-  kern<<<pl.grid, F32_THREADS, pl.smem, st>>>(map_a, map_w, map_s, map_z, g);
+  kern<<<pl.grid, GROUPS * F32_KWARPS * 32, pl.smem, st>>>(map_a, map_w, map_s, map_z, g);
   B2_LAUNCH_CHECK();
   return B2_OK;
 }
@@ -505,13 +514,13 @@ int dq_f32_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
   g.wait_ns = kWaitNs;
   const bool four = p.wdt == kInt4 || p.wdt == kUint4;
   if (four) {
-    if (pl.mr == 8) return f32_launch_t<4, 8>(p, pl, g, st);
-    if (pl.mr == 16) return f32_launch_t<4, 16>(p, pl, g, st);
-    return f32_launch_t<4, 32>(p, pl, g, st);
+    if (pl.mr == 8) return f32_launch_t<4, 8, 1>(p, pl, g, st);
+    if (pl.mr == 16) return f32_launch_t<4, 8, 2>(p, pl, g, st);
+    return f32_launch_t<4, 16, 2>(p, pl, g, st);
   }
-  if (pl.mr == 8) return f32_launch_t<8, 8>(p, pl, g, st);
-  if (pl.mr == 16) return f32_launch_t<8, 16>(p, pl, g, st);
-  return f32_launch_t<8, 32>(p, pl, g, st);
+  if (pl.mr == 8) return f32_launch_t<8, 8, 1>(p, pl, g, st);
+  if (pl.mr == 16) return f32_launch_t<8, 8, 2>(p, pl, g, st);
+  return f32_launch_t<8, 16, 2>(p, pl, g, st);
 }
 
 } // namespace b2

@@ -147,7 +147,53 @@ __device__ __forceinline__ uint32_t dq2(uint32_t v, uint32_t magic, uint32_t s2)
 // lane row g + 8 holds the next column.
 __device__ __forceinline__ int mt_col(int mt, int g) { return (mt >> 1) * 32 + 4 * g + 2 * (mt & 1); }
 
-template <int NT, int CL>
+// One k16 step of the magic-number form (as dq_gemv_mma's k16_step): rows r0
+// .. r0 + 15 of the stage, the 128 columns of column half `wn`, activation
+// tile nt.  Nibbles 0 and 1 of each 16-bit half become the exact fp16
+// integers 1024 + code and 1024 + 16 code with one logic operation, nibbles 2
+// and 3 after a shift by 8; D accumulates sum a * magic, O sum a (ones row).
+template <int NT>
+__device__ __forceinline__ void k16_magic(const uint8_t *wst, const uint8_t *ast, int r0, int wn,
+                                          int lane, int g, int t, int nt, uint32_t mlo, uint32_t mhi,
+                                          float (&D)[8][4], float (&O)[4]) {
+  uint32_t B0, B1;
+  {
+    const int kb = ((r0 & 63) + 2 * t) * 2;
+    const uint8_t *box = ast + (r0 >= 64 ? 8 * NT * 128 : 0);
+    const int row = nt * 8 + g;
+    const uint8_t *rb = box + row * 128;
+    B0 = *reinterpret_cast<const uint32_t *>(rb + ((((kb >> 4) ^ (row & 7)) << 4) | (kb & 15)));
+    const int kb2 = kb + 16;
+    B1 = *reinterpret_cast<const uint32_t *>(rb + ((((kb2 >> 4) ^ (row & 7)) << 4) | (kb2 & 15)));
+  }
+  const int mi = lane >> 3;
+  const int row = r0 + (mi & 1) * 8 + (lane & 7);
+  const uint32_t rbase = tc::smem_u32(wst + row * 128);
+#pragma unroll
+  for (int pair = 0; pair < 2; ++pair) {
+    const int lch = wn * 4 + pair * 2 + (mi >> 1);
+    uint32_t r[4];
+    ldsm_t4(rbase + ((lch ^ (row & 7)) << 4), r);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint32_t x = r[2 * c], y = r[2 * c + 1];
+      const int mt = (pair * 2 + c) * 2;
+      mma16816(D[mt], (x & 0x000f000fu) ^ mlo, (x & 0x00f000f0u) ^ mhi, (y & 0x000f000fu) ^ mlo,
+               (y & 0x00f000f0u) ^ mhi, B0, B1);
+      const uint32_t xs = x >> 8, ys = y >> 8;
+      mma16816(D[mt + 1], (xs & 0x000f000fu) ^ mlo, (xs & 0x00f000f0u) ^ mhi,
+               (ys & 0x000f000fu) ^ mlo, (ys & 0x00f000f0u) ^ mhi, B0, B1);
+    }
+  }
+  constexpr uint32_t kOnes = 0x3c003c00u; // (1.0, 1.0) in fp16
+  mma16816(O, kOnes, kOnes, kOnes, kOnes, B0, B1);
+}
+
+// EXACT: weights formed as the reference's fp16 values (two fp16 operations
+// per pair of weights); otherwise the cheaper magic-number form of
+// dq_gemv_mma (one logic operation per pair, the scale applied to each
+// 32-row block sum in fp32, within 2^-11 relative of the reference's weights).
+template <int NT, int CL, bool EXACT>
 __global__ void __launch_bounds__(GC_THREADS, GcCfg<NT>::kCtasPerSm)
     dq_gemv_c(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
               const __grid_constant__ CUtensorMap map_s, const GcArgs g) {
@@ -218,10 +264,16 @@ __global__ void __launch_bounds__(GC_THREADS, GcCfg<NT>::kCtasPerSm)
   const int wn = warp & 1, quad = warp >> 1;
   const int gq = lane >> 2, t = lane & 3;
   const uint32_t magic = g.is_signed ? 0x64086408u : 0x64006400u; // fp16 (1032, 1032) / (1024, 1024)
+  const uint32_t mlo = magic;
+  const uint32_t mhi = g.is_signed ? 0x64806480u : 0x64006400u;
+  const float blo = g.is_signed ? 1032.0f : 1024.0f;
+  const float bhi = g.is_signed ? 1152.0f : 1024.0f;
   uint32_t scalar2 = 0;
+  float scalar = 0.0f;
   if (!g.srows) {
     const uint32_t h = __ldg(g.scalar_scale);
     scalar2 = h | (h << 16);
+    scalar = __half2float(__ushort_as_half((uint16_t)h));
   }
   float acc[8][NT][4];
 #pragma unroll
@@ -246,7 +298,44 @@ __global__ void __launch_bounds__(GC_THREADS, GcCfg<NT>::kCtasPerSm)
         flags[0] = 1;
         ok = false;
       }
-      if (ok) {
+      if (ok && !EXACT) {
+        const uint8_t *wst = sm + s * GC_W_BYTES;
+        const uint8_t *ast = sm + C::kOffA + s * C::kA;
+        const uint8_t *sst = sm + C::kOffS + s * GC_SC_BYTES;
+        const int srow = (g.block && g.block < GC_TK) ? slab_row0 / g.block : 0;
+        const uint8_t *srow_p = sst + srow * GC_TN * 2 + wn * 256;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float D[8][4], O[4];
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) D[mt][e] = 0.0f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) O[e] = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            k16_magic<NT>(wst, ast, slab_row0 + 16 * j, wn, lane, gq, t, nt, mlo, mhi, D, O);
+          // block done: acc += s_eff * (D - bias * sum a), the high nibbles'
+          // scale divided by 16
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            float se0 = scalar, se1 = scalar * 0.0625f;
+            if (g.srows) {
+              const uint32_t w2 = *reinterpret_cast<const uint32_t *>(srow_p + mt_col(mt, gq) * 2);
+              se0 = __half2float(__ushort_as_half((uint16_t)(w2 & 0xffffu)));
+              se1 = __half2float(__ushort_as_half((uint16_t)(w2 >> 16))) * 0.0625f;
+            }
+            const float c0 = fmaf(-blo, O[0], D[mt][0]), c1 = fmaf(-blo, O[1], D[mt][1]);
+            const float c2 = fmaf(-bhi, O[0], D[mt][2]), c3 = fmaf(-bhi, O[1], D[mt][3]);
+            acc[mt][nt][0] = fmaf(se0, c0, acc[mt][nt][0]);
+            acc[mt][nt][1] = fmaf(se0, c1, acc[mt][nt][1]);
+            acc[mt][nt][2] = fmaf(se1, c2, acc[mt][nt][2]);
+            acc[mt][nt][3] = fmaf(se1, c3, acc[mt][nt][3]);
+          }
+        }
+      }
+      if (ok && EXACT) {
         const uint8_t *wst = sm + s * GC_W_BYTES;
         const uint8_t *ast = sm + C::kOffA + s * C::kA;
         // (s_col, s_col) and (s_col+1, s_col+1) of this lane's 8 column pairs
@@ -401,14 +490,13 @@ struct GcPlan {
   int nt = 1, cl = 8, nclusters = 0, kunits = 0, ntiles = 0, kper = 0, srows = 0, block = 0;
 };
 
-template <int NT, int CL> size_t smem_c() { return GcCfg<NT>::kDynamic; }
 
 // Clusters of CL CTAs that can be resident at once for this kernel (host
 // query, cached per instance).
-template <int NT, int CL> int max_clusters() {
+template <int NT, int CL, bool EXACT> int max_clusters() {
   static int cached = -1;
   if (cached >= 0) return cached;
-  auto kern = dq_gemv_c<NT, CL>;
+  auto kern = dq_gemv_c<NT, CL, EXACT>;
   const size_t smem = GcCfg<NT>::kDynamic;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
       cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0) != cudaSuccess)
@@ -431,11 +519,12 @@ template <int NT, int CL> int max_clusters() {
 }
 
 template <int NT> int max_clusters_of(int cl) {
+  // both forms have the same shared memory and launch bounds
   switch (cl) {
-  case 1: return max_clusters<NT, 1>();
-  case 2: return max_clusters<NT, 2>();
-  case 4: return max_clusters<NT, 4>();
-  default: return max_clusters<NT, 8>();
+  case 1: return max_clusters<NT, 1, false>();
+  case 2: return max_clusters<NT, 2, false>();
+  case 4: return max_clusters<NT, 4, false>();
+  default: return max_clusters<NT, 8, false>();
   }
 }
 
@@ -461,7 +550,7 @@ GcPlan gc_plan(const DqMmParams &p) {
   return m;
 }
 
-template <int NT, int CL> int launch_c_t(const DqMmParams &p, const GcPlan &m, cudaStream_t st) {
+template <int NT, int CL, bool EXACT> int launch_c_t(const DqMmParams &p, const GcPlan &m, cudaStream_t st) {
   CUtensorMap map_w, map_a, map_s;
   {
     const uint64_t dims[2] = {(uint64_t)p.N / 2, (uint64_t)p.K};
@@ -502,7 +591,7 @@ template <int NT, int CL> int launch_c_t(const DqMmParams &p, const GcPlan &m, c
   a.is_signed = p.wdt == kInt4;
   a.scalar_scale = reinterpret_cast<const uint16_t *>(p.scale);
   a.wait_ns = kWaitNs;
-  auto kern = dq_gemv_c<NT, CL>;
+  auto kern = dq_gemv_c<NT, CL, EXACT>;
   const size_t smem = GcCfg<NT>::kDynamic;
   B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   cudaLaunchConfig_t cfg = {};
@@ -523,12 +612,12 @@ template <int NT, int CL> int launch_c_t(const DqMmParams &p, const GcPlan &m, c
   return B2_OK;
 }
 
-template <int NT> int launch_c(const DqMmParams &p, const GcPlan &m, cudaStream_t st) {
+template <int NT, bool EXACT> int launch_c(const DqMmParams &p, const GcPlan &m, cudaStream_t st) {
   switch (m.cl) {
-  case 1: return launch_c_t<NT, 1>(p, m, st);
-  case 2: return launch_c_t<NT, 2>(p, m, st);
-  case 4: return launch_c_t<NT, 4>(p, m, st);
-  default: return launch_c_t<NT, 8>(p, m, st);
+  case 1: return launch_c_t<NT, 1, EXACT>(p, m, st);
+  case 2: return launch_c_t<NT, 2, EXACT>(p, m, st);
+  case 4: return launch_c_t<NT, 4, EXACT>(p, m, st);
+  default: return launch_c_t<NT, 8, EXACT>(p, m, st);
   }
 }
 
@@ -552,11 +641,16 @@ bool dq_c_eligible(const DqMmParams &p) {
   }
 }
 
-int dq_c_launch(const DqMmParams &p, cudaStream_t st) {
+int dq_c_launch(const DqMmParams &p, cudaStream_t st, bool exact) {
   const GcPlan m = gc_plan(p);
-  if (m.nt == 1) return launch_c<1>(p, m, st);
-  if (m.nt == 2) return launch_c<2>(p, m, st);
-  return launch_c<4>(p, m, st);
+  if (exact) {
+    if (m.nt == 1) return launch_c<1, true>(p, m, st);
+    if (m.nt == 2) return launch_c<2, true>(p, m, st);
+    return launch_c<4, true>(p, m, st);
+  }
+  if (m.nt == 1) return launch_c<1, false>(p, m, st);
+  if (m.nt == 2) return launch_c<2, false>(p, m, st);
+  return launch_c<4, false>(p, m, st);
 }
 
 } // namespace b2

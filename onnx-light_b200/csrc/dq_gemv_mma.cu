@@ -51,6 +51,8 @@
 #include "dq_matmul.cuh"
 #include "tc_common.cuh"
 
+#include <cstdlib>
+
 namespace b2 {
 
 // Wait time-outs of the decode kernel (a TMA copy or a consumer that never
@@ -90,6 +92,10 @@ struct GmArgs {
   int srows;     // scale rows loaded per stage (0: per-tensor scale)
   const uint16_t *scalar_scale; // the per-tensor scale (srows == 0)
   int is_signed;
+  // Tile-aligned split (aligned != 0): tiles 0 .. cr-1 get cq + 1 CTAs, the
+  // others cq; each CTA one contiguous K slice of one tile.
+  int aligned, cq, cr;
+  uint64_t wait_ns;
 };
 
 template <int NT> struct GmSmem {
@@ -146,6 +152,32 @@ __device__ __forceinline__ int unit_begin(int c, int U, int G) {
 }
 __device__ __forceinline__ int cta_of(int u, int U, int G) {
   return (int)(((uint32_t)(u + 1) * (uint32_t)G - 1u) / (uint32_t)U);
+}
+// Tile-aligned split: CTA b -> (tile, K slice, slices of the tile, the tile's
+// first CTA).  Tiles 0 .. cr-1 have cq + 1 consecutive CTAs, the rest cq.
+__device__ __forceinline__ void tile_slice(int b, int cq, int cr, int &tile, int &slice, int &nsl,
+                                           int &first) {
+  const int big = cr * (cq + 1);
+  if (b < big) {
+    tile = b / (cq + 1);
+    slice = b % (cq + 1);
+    nsl = cq + 1;
+    first = tile * (cq + 1);
+  } else {
+    const int bb = b - big;
+    tile = cr + bb / cq;
+    slice = bb % cq;
+    nsl = cq;
+    first = big + (tile - cr) * cq;
+  }
+}
+__device__ __forceinline__ void red_release_add(uint32_t *p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Column (within the warp's 128-column half) of lane row g of m-tile mt;
@@ -226,8 +258,16 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
-  const int u0 = unit_begin(b, g.units, g.grid);
-  const int u1 = unit_begin(b + 1, g.units, g.grid);
+  int u0, u1;
+  int a_tile = 0, a_slice = 0, a_nsl = 1, a_first = 0; // tile-aligned split
+  if (g.aligned) {
+    tile_slice(b, g.cq, g.cr, a_tile, a_slice, a_nsl, a_first);
+    u0 = a_tile * g.kunits + a_slice * g.kunits / a_nsl;
+    u1 = a_tile * g.kunits + (a_slice + 1) * g.kunits / a_nsl;
+  } else {
+    u0 = unit_begin(b, g.units, g.grid);
+    u1 = unit_begin(b + 1, g.units, g.grid);
+  }
   const int nun = u1 - u0;
 
   if (threadIdx.x == 0) {
@@ -418,9 +458,104 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
       }
     }
     const int uf = tile * g.kunits, ul = uf + g.kunits - 1;
-    const int cf = cta_of(uf, g.units, g.grid), cl = cta_of(ul, g.units, g.grid);
+    const int cf = g.aligned ? a_first : cta_of(uf, g.units, g.grid);
+    const int cl = g.aligned ? a_first + a_nsl - 1 : cta_of(ul, g.units, g.grid);
     const int n0 = tile * GM_TN;
-    if (cf == cl) {
+    if (g.aligned && cf != cl) {
+      // ---- tile-aligned split: the tile's first CTA (slice 0) merges ----
+      float *part = g.partials + (size_t)(b * 2) * g.M * GM_TN;
+      uint32_t *ctr = g.counters + tile;
+      if (a_slice != 0) {
+        // Contributor: the partial to global memory, then a release add on
+        // the tile's counter (with kAbortMark when a wait gave up).
+        if (quad == 0) {
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            const int col = wn * 128 + mt_col(mt, gq);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const int m = nt * 8 + 2 * t;
+              if (m < g.M)
+                *reinterpret_cast<float2 *>(part + m * GM_TN + col) =
+                    make_float2(acc[mt][nt][0], acc[mt][nt][2]);
+              if (m + 1 < g.M)
+                *reinterpret_cast<float2 *>(part + (m + 1) * GM_TN + col) =
+                    make_float2(acc[mt][nt][1], acc[mt][nt][3]);
+            }
+          }
+        }
+        consumers_sync();
+        if (threadIdx.x == 0) {
+          __threadfence(); // every consumer's partial stores before the release
+          red_release_add(ctr, flags[0] ? kAbortMark + 1u : 1u);
+        }
+      } else {
+        // Merger: its own partial stays in shared memory; wait (bounded) for
+        // the other slices, reset the counter, sum the slices in order.
+        consumers_sync(); // the tree's last reads of `red` are done
+        if (quad == 0) {
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            const int col = wn * 128 + mt_col(mt, gq);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const int m = nt * 8 + 2 * t;
+              *reinterpret_cast<float2 *>(red + m * GM_TN + col) = make_float2(acc[mt][nt][0], acc[mt][nt][2]);
+              *reinterpret_cast<float2 *>(red + (m + 1) * GM_TN + col) =
+                  make_float2(acc[mt][nt][1], acc[mt][nt][3]);
+            }
+          }
+        }
+        if (threadIdx.x == 0) {
+          // Every contributor arrives exactly once, also after a give-up
+          // (each of its waits is bounded), so waiting for all of them and
+          // resetting leaves the counter at zero for the next call.
+          const uint64_t t0 = tc::globaltimer();
+          uint32_t v = ld_acquire_gpu(ctr);
+          bool arrived = true;
+          while ((v & (kAbortMark - 1u)) < (uint32_t)(a_nsl - 1)) {
+            if (tc::globaltimer() - t0 > 3 * g.wait_ns) {
+              atomicExch(&g_gemv_mma_status, tc::kTimeoutFull);
+              arrived = false;
+              break;
+            }
+            __nanosleep(32);
+            v = ld_acquire_gpu(ctr);
+          }
+          if (arrived) *ctr = 0u;
+          flags[1] = arrived && (v >> 16) == 0u && !flags[0] ? 1 : 0;
+        }
+        consumers_sync();
+        if (flags[1]) {
+          const int nc = a_nsl;
+          for (int e = threadIdx.x; e < g.M * (GM_TN / 4); e += GM_CONSUMERS * 32) {
+            float4 sum = reinterpret_cast<const float4 *>(red)[e];
+            for (int c0 = 1; c0 < nc; c0 += 16) {
+              float4 v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (c0 + j < nc)
+                  v[j] = __ldcg(reinterpret_cast<const float4 *>(
+                                    g.partials + (size_t)((b + c0 + j) * 2) * g.M * GM_TN) + e);
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                sum.x += v[j].x;
+                sum.y += v[j].y;
+                sum.z += v[j].z;
+                sum.w += v[j].w;
+              }
+            }
+            const int m = e / (GM_TN / 4), col = (e % (GM_TN / 4)) * 4;
+            if (n0 + col >= g.N) continue; // ragged last tile; N % 4 == 0
+            __half2 *dst = reinterpret_cast<__half2 *>(g.y + (int64_t)m * g.N + n0 + col);
+            dst[0] = __floats2half2_rn(sum.x, sum.y);
+            dst[1] = __floats2half2_rn(sum.z, sum.w);
+          }
+        }
+      }
+    } else if (cf == cl) {
       // The whole tile is this CTA's: write the output.
       if (quad == 0 && ok) {
 #pragma unroll
@@ -517,6 +652,7 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
 
 struct MmaPlan {
   int nt = 1, groups = 4, grid = 0, units = 0, kunits = 0, ntiles = 0, srows = 0, block = 0;
+  int aligned = 0, cq = 0, cr = 0;
   size_t ws = 0;
 };
 
@@ -527,9 +663,17 @@ MmaPlan mma_plan(const DqMmParams &p) {
   m.kunits = (int)((p.K + GM_TK - 1) / GM_TK);
   m.units = m.ntiles * m.kunits;
   m.grid = std::min(m.units, sm_count() * GM_CTAS_PER_SM);
+  // Up to one tile per CTA: split each tile's K range among whole CTAs (a
+  // CTA never straddles two tiles, and each tile's first CTA merges), which
+  // takes one merge per tile off the critical path of stream-K.
+  m.aligned = m.ntiles <= m.grid && getenv("ONNXL_B200_GEMV_STREAMK") == nullptr;
+  if (m.aligned) {
+    m.cq = m.grid / m.ntiles;
+    m.cr = m.grid % m.ntiles;
+  }
   // Stages per CTA below about 2 per stage group leave groups idle: put all
   // warps on every stage instead.
-  const int per_cta = (m.units + m.grid - 1) / m.grid;
+  const int per_cta = m.aligned ? (m.kunits + m.cq - 1) / m.cq : (m.units + m.grid - 1) / m.grid;
   m.groups = per_cta <= kGroupsThreshold ? 1 : 4;
   if (p.slayout == kScaleTensor) {
     m.srows = 0;
@@ -539,8 +683,8 @@ MmaPlan mma_plan(const DqMmParams &p) {
     m.block = (int)p.block;
     m.srows = p.block < GM_TK ? (int)(GM_TK / p.block) : 1;
   }
-  bool split = false;
-  for (int tile = 0; tile < m.ntiles && !split; ++tile) {
+  bool split = m.aligned && m.grid > m.ntiles;
+  for (int tile = 0; tile < m.ntiles && !split && !m.aligned; ++tile) {
     const int uf = tile * m.kunits, ul = uf + m.kunits - 1;
     const int cf = (int)(((int64_t)(uf + 1) * m.grid - 1) / m.units);
     const int cl = (int)(((int64_t)(ul + 1) * m.grid - 1) / m.units);
@@ -595,6 +739,10 @@ int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStrea
   a.srows = m.srows;
   a.is_signed = p.wdt == kInt4;
   a.scalar_scale = reinterpret_cast<const uint16_t *>(p.scale);
+  a.aligned = m.aligned;
+  a.cq = m.cq;
+  a.cr = m.cr;
+  a.wait_ns = kWaitNs;
   auto kern = dq_gemv_mma<NT, G, KS>;
   const size_t smem = GmSmem<NT>::kDynamic;
   B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -710,7 +710,7 @@ static int wbits(int dt) {
 // one or two rows, dq_gemm_f32 for FLOAT activations with integer weights,
 // and the generic CUDA-core GEMM for the rest.
 enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3, kPathMma = 4, kPathF32 = 5,
-              kPathX = 6, kPathN = 7, kPathC = 8 };
+              kPathX = 6, kPathN = 7, kPathC = 8, kPathCX = 9 };
 
 static DqPath forced_path() {
   const char *e = getenv("ONNXL_B200_DQ_KERNEL");
@@ -723,6 +723,7 @@ static DqPath forced_path() {
   if (!strcmp(e, "x")) return kPathX;
   if (!strcmp(e, "n")) return kPathN;
   if (!strcmp(e, "c")) return kPathC;
+  if (!strcmp(e, "cx")) return kPathCX;
   return kPathAuto;
 }
 
@@ -739,8 +740,8 @@ static Plan make_plan(const DqMmParams &p) {
                        (p.slayout != kScaleAxis0Block || p.block % 32 == 0) &&
                        ((p.N * bits / 8) % 16 == 0);
   const DqPath forced = forced_path();
-  if (forced == kPathC && dq_c_eligible(p)) {
-    pl.kind = 7;
+  if ((forced == kPathC || forced == kPathCX) && dq_c_eligible(p)) {
+    pl.kind = forced == kPathC ? 7 : 8;
     pl.ws = 0;
     return pl;
   }
@@ -899,11 +900,11 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
     B2_CUDA(cudaMemsetAsync(y->data, 0, (size_t)p.M * p.N * (p.ydt == kFloat ? 4 : 2), st));
     return B2_OK;
   }
-  if (pl.kind >= 3 && pl.kind <= 7) {
+  if (pl.kind >= 3 && pl.kind <= 8) {
     if (pl.kind == 3 && dq_mma_aligned(p)) return dq_mma_launch(p, workspace, st);
     if (pl.kind == 5 && dq_mma_aligned(p)) return dq_x_launch(p, workspace, st);
     if (pl.kind == 6 && dq_mma_aligned(p)) return dq_n_launch(p, st);
-    if (pl.kind == 7 && dq_mma_aligned(p)) return dq_c_launch(p, st);
+    if ((pl.kind == 7 || pl.kind == 8) && dq_mma_aligned(p)) return dq_c_launch(p, st, pl.kind == 8);
     if (pl.kind == 4 && dq_f32_aligned(p)) return dq_f32_launch(p, workspace, st);
     // TMA / vector loads need aligned tensors: fall back to the unsplit
     // CUDA-core kernel, which needs no workspace.

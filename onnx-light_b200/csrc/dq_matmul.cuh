@@ -67,7 +67,7 @@ int dq_n_launch(const DqMmParams &p, cudaStream_t stream);
 // Decode path split along K inside thread-block clusters (dq_gemv_c.cu): M <=
 // 32, INT4/UINT4 weights, FLOAT16 scales, activations and output; no workspace.
 bool dq_c_eligible(const DqMmParams &p); // shape/type constraints (pointer alignment: dq_mma_aligned)
-int dq_c_launch(const DqMmParams &p, cudaStream_t stream);
+int dq_c_launch(const DqMmParams &p, cudaStream_t stream, bool exact);
 
 // FLOAT-activation path on CUDA cores (dq_gemm_f32.cu): INT4 / UINT4 / INT8 /
 // UINT8 weights, per-tensor, per-column or K-blocked scales, FLOAT output.

@@ -477,30 +477,34 @@ def test_narrow_decode_weights_match_the_reference_rounding(b2, cuda, monkeypatc
 
 # ---------------------------------------------------------------------------
 # Decode path split along K inside clusters (dq_gemv_c, forced with
-# ONNXL_B200_DQ_KERNEL=c): clusters of 8 / 4 / 2 / 1, more tiles than
-# clusters, ragged shapes, every scale layout it takes.
+# ONNXL_B200_DQ_KERNEL=c for the magic-number form, cx for the exact fp16
+# weights): clusters of 8 / 4 / 2 / 1, more tiles than clusters, ragged
+# shapes, every scale layout it takes.
 # ---------------------------------------------------------------------------
 
+@pytest.mark.parametrize("form", ["c", "cx"])
 @pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 17, 32])
-def test_cluster_decode_config3_batches(b2, cuda, monkeypatch, M):
-    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+def test_cluster_decode_config3_batches(b2, cuda, monkeypatch, M, form):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", form)
     y, ref = run_case(b2, M, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=100 + M)
     assert rel_l2(y, ref) <= TOL[O.FLOAT16], rel_l2(y, ref)
 
 
+@pytest.mark.parametrize("form", ["c", "cx"])
 @pytest.mark.parametrize("K,N", [(11008, 4096), (4096, 11008), (1000, 4128), (200, 96), (384, 64),
                                  (128, 8192)])
-def test_cluster_decode_shapes(b2, cuda, monkeypatch, K, N):
-    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+def test_cluster_decode_shapes(b2, cuda, monkeypatch, K, N, form):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", form)
     for M in (1, 12, 30):
         y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=None, axis=1, seed=K + M + 2)
         assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
 
 
+@pytest.mark.parametrize("form", ["c", "cx"])
 @pytest.mark.parametrize("wdt,block,axis", [(O.INT4, 32, 0), (O.UINT4, 64, 0), (O.INT4, 256, 0),
                                             (O.UINT4, 0, 0), (O.INT4, None, 1)])
-def test_cluster_decode_scale_layouts(b2, cuda, monkeypatch, wdt, block, axis):
-    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+def test_cluster_decode_scale_layouts(b2, cuda, monkeypatch, wdt, block, axis, form):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", form)
     K = 1024
     for M in (2, 20):
         y, ref = run_case(b2, M, K, 512, wdt, O.FLOAT16, O.FLOAT16, axis=axis, block=block, seed=M + 93)
@@ -508,7 +512,7 @@ def test_cluster_decode_scale_layouts(b2, cuda, monkeypatch, wdt, block, axis):
 
 
 def test_cluster_decode_weights_match_the_reference_rounding(b2, cuda, monkeypatch):
-    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "cx")
     K, N = 1024, 256
     w = random_q(25, (K, N), O.INT4)
     s = scale_raw(np.concatenate([O.rand_uniform(26, (4 * N,), 1e-6, 1e-4),
@@ -526,8 +530,19 @@ def test_cluster_decode_weights_match_the_reference_rounding(b2, cuda, monkeypat
         assert np.array_equal(got, wq.reshape(K, N)[k]), k
 
 
-def test_cluster_decode_repeated_calls_are_identical(b2, cuda, monkeypatch):
-    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "c")
+@pytest.mark.parametrize("form", ["c", "cx"])
+def test_cluster_decode_repeated_calls_are_identical(b2, cuda, monkeypatch, form):
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", form)
     outs = [run_case(b2, 5, 4096, 11008, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=4)[0]
             for _ in range(3)]
     assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
+@pytest.mark.parametrize("K,N", [(4096, 4096), (11008, 4096), (4096, 11008)])
+def test_mma_decode_stream_k_partition(b2, cuda, monkeypatch, K, N):
+    # the stream-K unit partition (ONNXL_B200_GEMV_STREAMK) that shapes with
+    # more tiles than SMs take; the default splits each tile among whole CTAs
+    monkeypatch.setenv("ONNXL_B200_GEMV_STREAMK", "1")
+    for M in (1, 9):
+        y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=K + N + M)
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
