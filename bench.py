@@ -314,7 +314,7 @@ def gpu_arm(args):
             achieved = nbytes / (ms * 1e-3) / 1e9
         else:
             achieved = sum(p[1] for p in per) / (sum(p[2] for p in per) * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "dq_gemv_mma", "achieved": round(achieved, 1),
+        roof = {"bound": "hbm", "kernel": decode_kernel(B), "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_source": peak_src, "traffic": traffic_from_profile(B) if world == 1 else None,
                 "traffic_unit": "DRAM bytes per step (ncu capture of batch 1, profiles/traffic.json)",
@@ -488,11 +488,23 @@ def _e2e(stream, step_fn, h2d, d2h, reps, chunk):
     return max(wall, dev), hb, db
 
 
+def decode_kernel(B: int) -> str:
+    """The decode kernel(s) the planner picks for config 3 at batch B."""
+    if B <= 8:
+        return "dq_gemv_mma"
+    if B <= 16:
+        return "dq_gemv_n (4096 columns), dq_gemv_mma (11008 columns)"
+    if B <= 32:
+        return "dq_gemv_n"
+    if B <= 64:
+        return "dq_gemv_x"
+    return "dq_gemm_tc"
+
+
 def decode_config3(b2, layers, device, stream, B, cpu):
     """BASELINE config 3 at batch B (8, 32, 64): the same seven int4
     projections and weight copies as the headline, activations [B, 4096].
-    The planner takes the register-MMA decode kernel up to 16 rows and the
-    tcgen05 dequant GEMM above."""
+    The planner picks the decode kernel by batch (decode_kernel)."""
     import torch
     from onnx_light_b200 import synth
     mm = b2.DequantizeMatMul()
@@ -524,7 +536,7 @@ def decode_config3(b2, layers, device, stream, B, cpu):
                           NCOPIES * 8)
     out = {"metric": f"int4 dequant-MatMul HBM GB/s (config 3, batch {B})", "value": round(gbs, 1),
            "unit": "GB/s", "ms_per_step": round(ms, 5),
-           "kernel": "dq_gemv_mma" if B <= 16 else "dq_gemm_tc",
+           "kernel": decode_kernel(B),
            "tflops": round(step_flops(B) / (ms * 1e-3) / 1e12, 2),
            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(gbs / peak, 4), "peak_source": src,

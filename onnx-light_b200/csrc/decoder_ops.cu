@@ -125,58 +125,56 @@ struct RotaryArgs {
   int rank3, interleaved;
 };
 
-template <typename T> __global__ void rotary_kernel(const RotaryArgs a) {
-  const int64_t total = a.B * a.H * a.S * a.D;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t c = e % a.D;
-    int64_t t = e / a.D;
-    int64_t b, h, s;
-    if (a.rank3) { // storage [B, S, H, D]
-      h = t % a.H;
-      t /= a.H;
-      s = t % a.S;
-      b = t / a.S;
-    } else { // [B, H, S, D]
-      s = t % a.S;
-      t /= a.S;
-      h = t % a.H;
-      b = t / a.H;
+// One warp per row of D channels (a (batch, head, position) triple): the row
+// index is split into (b, s) once, and each lane computes both outputs of its
+// rotation pairs from one load of x1, x2, cos and sin; channels past the
+// rotary dimension are copied.
+template <typename T> __global__ void __launch_bounds__(256) rotary_kernel(const RotaryArgs a) {
+  const int64_t rows = a.B * a.H * a.S;
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < rows;
+       r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    int64_t b, s;
+    if (a.rank3) { // storage [B, S, H, D]: r = (b S + s) H + h
+      const int64_t bs = r / a.H;
+      b = bs / a.S;
+      s = bs - b * a.S;
+    } else { // [B, H, S, D]: r = (b H + h) S + s
+      const int64_t bh = r / a.S;
+      s = r - bh * a.S;
+      b = bh / a.H;
     }
-    (void)h;
-    const int64_t base = e - c;
-    if (c >= 2 * a.half) {
-      Act<T>::st(a.y, e, Act<T>::ld(a.x, e));
-      continue;
-    }
-    int64_t row = b * a.S + s;
+    const int64_t base = r * a.D;
+    int64_t crow = b * a.S + s;
+    bool valid = true;
     if (a.pos) {
-      row = a.pos[b * a.S + s];
-      if (row < 0 || row >= a.cache_rows) {
-        atomicExch(&g_rotary_status, 1);
-        Act<T>::st(a.y, e, 0.0f);
-        continue;
+      crow = a.pos[b * a.S + s];
+      if (crow < 0 || crow >= a.cache_rows) {
+        valid = false;
+        if (lane == 0) atomicExch(&g_rotary_status, 1);
       }
     }
-    int64_t i, i1, i2;
-    bool first;
-    if (a.interleaved) {
-      i = c >> 1;
-      i1 = base + 2 * i;
-      i2 = i1 + 1;
-      first = (c & 1) == 0;
-    } else {
-      first = c < a.half;
-      i = first ? c : c - a.half;
-      i1 = base + i;
-      i2 = base + a.half + i;
+    for (int64_t i = lane; i < a.half; i += 32) {
+      int64_t i1, i2;
+      if (a.interleaved) {
+        i1 = base + 2 * i;
+        i2 = i1 + 1;
+      } else {
+        i1 = base + i;
+        i2 = base + a.half + i;
+      }
+      if (!valid) {
+        Act<T>::st(a.y, i1, 0.0f);
+        Act<T>::st(a.y, i2, 0.0f);
+        continue;
+      }
+      const float cv = Act<T>::ld(a.cos, crow * a.half + i);
+      const float sv = Act<T>::ld(a.sin, crow * a.half + i);
+      const float x1 = Act<T>::ld(a.x, i1), x2 = Act<T>::ld(a.x, i2);
+      Act<T>::st(a.y, i1, __fsub_rn(__fmul_rn(cv, x1), __fmul_rn(sv, x2)));
+      Act<T>::st(a.y, i2, __fadd_rn(__fmul_rn(sv, x1), __fmul_rn(cv, x2)));
     }
-    const float cv = Act<T>::ld(a.cos, row * a.half + i);
-    const float sv = Act<T>::ld(a.sin, row * a.half + i);
-    const float x1 = Act<T>::ld(a.x, i1), x2 = Act<T>::ld(a.x, i2);
-    const float v = first ? __fsub_rn(__fmul_rn(cv, x1), __fmul_rn(sv, x2))
-                          : __fadd_rn(__fmul_rn(sv, x1), __fmul_rn(cv, x2));
-    Act<T>::st(a.y, e, v);
+    for (int64_t c = 2 * a.half + lane; c < a.D; c += 32) Act<T>::st(a.y, base + c, Act<T>::ld(a.x, base + c));
   }
 }
 
@@ -339,7 +337,8 @@ extern "C" int b2_rotary_embedding(const b2_tensor *x, const b2_tensor *cos_cach
   const int64_t total = a.B * a.H * a.S * a.D;
   if (total == 0) return B2_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned grid = grid_for(total, 256);
+  // one warp per (batch, head, position) row
+  const unsigned grid = grid_for(total / a.D * 32, 256);
   if (x->dtype == kFloat16) rotary_kernel<__half><<<grid, 256, 0, st>>>(a);
   else if (x->dtype == kBfloat16) rotary_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
   else rotary_kernel<float><<<grid, 256, 0, st>>>(a);

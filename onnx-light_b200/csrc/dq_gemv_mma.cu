@@ -78,7 +78,7 @@ constexpr int GM_SC_ROWS = 4;                      // scale rows per stage at mo
 constexpr uint32_t GM_SC_BYTES = GM_SC_ROWS * GM_TN * 2;
 constexpr uint32_t GM_ONES = 0x3c003c00u;          // (1.0, 1.0) in fp16
 #ifndef GM_GROUPS_THRESHOLD
-#define GM_GROUPS_THRESHOLD 8
+#define GM_GROUPS_THRESHOLD 2
 #endif
 constexpr int kGroupsThreshold = GM_GROUPS_THRESHOLD; // stages per CTA up to which G = 1
 

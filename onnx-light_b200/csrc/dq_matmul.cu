@@ -755,6 +755,24 @@ static Plan make_plan(const DqMmParams &p) {
     pl.ws = dq_x_workspace(p);
     return pl;
   }
+  // Default decode choice for the int4 / fp16 family, by batch (measured on
+  // config 3): up to 8 rows the magic-number split-K kernel; 9 to 32 rows the
+  // narrow-tile kernel (no split-K; its dequantization is shared by all
+  // activation tiles) unless, at 9 to 16 rows, the columns need more tiles
+  // than SMs; 33 to 64 rows the exact kernel with two row passes.
+  if (forced == kPathAuto && p.M > 8 && p.M <= 64) {
+    const bool narrow_fits = (p.N + 31) / 32 <= sm_count();
+    if (p.M <= 32 && dq_n_eligible(p) && (p.M > 16 || narrow_fits)) {
+      pl.kind = 6;
+      pl.ws = 0;
+      return pl;
+    }
+    if (p.M > 32 && dq_x_eligible(p)) {
+      pl.kind = 5;
+      pl.ws = dq_x_workspace(p);
+      return pl;
+    }
+  }
   if ((forced == kPathAuto || forced == kPathMma) && dq_mma_eligible(p)) {
     pl.kind = 3;
     pl.ws = dq_mma_workspace(p);

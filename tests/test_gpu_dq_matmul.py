@@ -266,11 +266,14 @@ def test_prefill_predequantized_gemm(b2, cuda, wdt, s_dt, act, block, zp, cast):
 # it, and leaves the caller's workspace valid for the next call.
 # ---------------------------------------------------------------------------
 
-def test_gemm_timeout_is_reported_and_workspace_stays_valid(b2, cuda):
+def test_gemm_timeout_is_reported_and_workspace_stays_valid(b2, cuda, monkeypatch):
     import ctypes as C
     from onnx_light_b200 import _capi as capi
     lib = capi.lib()
-    M, K, N = 32, 4096, 4096  # tensor-core plan, K split across CTAs
+    # the tensor-core plan (forced: the default for 32 rows is the narrow-tile
+    # GEMV), K split across CTAs
+    monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "tc")
+    M, K, N = 32, 4096, 4096
     w = random_q(41, (K, N), O.INT4)
     s = scale_raw(O.rand_uniform(42, (K // 128 * N,), 0.002, 0.02), O.FLOAT16)
     a = O.f32_to_f16_bits(O.randn(43, (M, K)))
