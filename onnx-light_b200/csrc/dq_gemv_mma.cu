@@ -103,8 +103,8 @@ template <int NT> struct GmSmem {
   static constexpr uint32_t kOffA = GM_STAGES * GM_W_BYTES;
   static constexpr uint32_t kOffS = kOffA + GM_STAGES * kA;
   static constexpr uint32_t kOffRed = kOffS + GM_STAGES * GM_SC_BYTES;
-  // GM_QUADS / 2 slots per column half for the tree reduction over its warps
-  static constexpr uint32_t kRedBytes = (GM_QUADS / 2) * 2u * 32 * NT * 32 * 4;
+  // GM_QUADS - 1 slots per column half for the sum over its warp groups
+  static constexpr uint32_t kRedBytes = (GM_QUADS - 1) * 2u * 32 * NT * 32 * 4;
   static constexpr uint32_t kOffBar = kOffRed + kRedBytes;
   static constexpr uint32_t kBytes = kOffBar + 2 * GM_STAGES * 8 + 16;
   static constexpr size_t kDynamic = kBytes + 1024; // alignment slack
@@ -432,23 +432,23 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     }
 
     // ------------------------ end of a tile segment ------------------------
-    // Sum the four groups of each column half (fixed-order tree); the warps of
-    // group 0 end with the column half's sums.
+    // Sum the four groups of each column half in group order, in one round:
+    // groups 1..3 leave their sums in shared memory, group 0 adds them.
+    consumers_sync();
+    if (quad > 0) {
+      float *r = red + (size_t)((quad - 1) * 2 + wn) * 32 * NT * 32;
 #pragma unroll
-    for (int half = GM_QUADS / 2; half >= 1; half >>= 1) {
-      consumers_sync();
-      if (quad >= half && quad < 2 * half) {
-        float *r = red + (size_t)((quad - half) * 2 + wn) * 32 * NT * 32;
+      for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt)
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
+          for (int e = 0; e < 4; ++e) r[((mt * NT + nt) * 4 + e) * 32 + lane] = acc[mt][nt][e];
+    }
+    consumers_sync();
+    if (quad == 0) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) r[((mt * NT + nt) * 4 + e) * 32 + lane] = acc[mt][nt][e];
-      }
-      consumers_sync();
-      if (quad < half) {
-        const float *r = red + (size_t)(quad * 2 + wn) * 32 * NT * 32;
+      for (int q = 0; q < GM_QUADS - 1; ++q) {
+        const float *r = red + (size_t)(q * 2 + wn) * 32 * NT * 32;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
@@ -484,15 +484,12 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
             }
           }
         }
-        consumers_sync();
-        if (threadIdx.x == 0) {
-          __threadfence(); // every consumer's partial stores before the release
-          red_release_add(ctr, flags[0] ? kAbortMark + 1u : 1u);
-        }
+        consumers_sync(); // every consumer's partial stores before the release below
+        if (threadIdx.x == 0) red_release_add(ctr, flags[0] ? kAbortMark + 1u : 1u);
       } else {
         // Merger: its own partial stays in shared memory; wait (bounded) for
         // the other slices, reset the counter, sum the slices in order.
-        consumers_sync(); // the tree's last reads of `red` are done
+        consumers_sync(); // the group sum's reads of `red` are done
         if (quad == 0) {
 #pragma unroll
           for (int mt = 0; mt < 8; ++mt) {
