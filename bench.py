@@ -206,14 +206,25 @@ def gpu_arm(args):
             acts[name] = peers.buffer(name, (B, N), torch.float16)
             loc[name] = torch.empty((B, N // world), dtype=torch.float16, device=device)
 
+    # Sharded decode (up to 16 rows): the fused kernel stores each rank's
+    # column slice into every rank's output itself (b2_dequantize_matmul_peer)
+    # and the next call waits for the previous one's slices; a step ends with
+    # a wait for its last projection.  Larger batches: each rank's slice, then
+    # b2_allgather_cols.
+    fused = world > 1 and B <= 16
+
     def run_step(layer):
         for name, K, N, src in PROJ:
             w, s = layer[name]
             if world == 1:
                 mm(acts[src], w, s, None, axis=0, out=acts[name])
+            elif fused:
+                peers.matmul(name, acts[src], w, s)
             else:
                 mm(acts[src], w, s, None, axis=0, out=loc[name])
                 peers.gather(name, loc[name])
+        if fused:
+            peers.wait()
 
     def run_steps(n, offset):
         for i in range(n):
@@ -366,7 +377,8 @@ def gpu_arm(args):
                "d2h_bytes_per_step": B * 4096 * 2,
                "path": "DequantizeMatMul python API -> b2_dequantize_matmul, pinned H2D + "
                        "7 calls + D2H per step, captured in CUDA graphs"
-                       + (" (+ b2_allgather_cols per call, max over ranks)" if world > 1 else "")}
+                       + ((" (fused peer stores, b2_dequantize_matmul_peer, max over ranks)" if fused
+                           else " (+ b2_allgather_cols per call, max over ranks)") if world > 1 else "")}
         del ge
 
     # Sharded: the gathered full output of a step against the unsharded
@@ -423,10 +435,13 @@ def gpu_arm(args):
             "timing": {"l2_policy": f"{NCOPIES} weight copies in rotation "
                                     f"({NCOPIES * step_bytes(B) / 1e6:.0f} MB > 126 MB L2)",
                        "launch": f"CUDA graphs of {chunk} steps"
-                                 + (" with a peer-store all-gather (b2_allgather_cols) per "
-                                    "projection" if world > 1 else "")},
+                                 + ((" with the column slices stored into every rank's output "
+                                     "by the decode kernel itself (b2_dequantize_matmul_peer) and "
+                                     "one completion wait per step" if fused else
+                                     " with a peer-store all-gather (b2_allgather_cols) per "
+                                     "projection") if world > 1 else "")},
             "tflops": round(step_flops(B) / (ms * 1e-3) / 1e12, 3),
-            "gpu_launches": (7 if world == 1 else 14) * args.steps,
+            "gpu_launches": (7 if world == 1 else (8 if fused else 14)) * args.steps,
             "gather_check": gather_check,
             "clocks": clocks,
             "roofline": roof,

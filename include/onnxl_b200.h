@@ -58,6 +58,24 @@ typedef struct b2_tensor {
   const int64_t *shape; /* ndim entries (may be NULL when ndim == 0) */
 } b2_tensor;
 
+/* A column-sharded output over a multi-GPU group (one process per GPU): every
+ * rank's full [M, n_full] output buffer and flag array (uint32[8], zeroed
+ * once), mapped into this process (b2_ipc_open), and this rank's two-word
+ * counter (zeroed once).  Rank r owns columns [r n_full / world, (r + 1)
+ * n_full / world). */
+typedef struct b2_peer_out {
+  void *full[8];
+  uint32_t *flags[8];
+  uint32_t *counters;
+  int32_t world, rank;
+  int64_t n_full;
+  /* b2_dequantize_matmul_peer: nonzero when the input `a` is (or may be) the
+   * output of a sharded call not yet waited for, so the kernel first waits
+   * for every rank to finish the group's previous call; zero skips the wait
+   * (an input no sharded call wrote since the last wait). */
+  int32_t wait_input;
+} b2_peer_out;
+
 /* Library identification, e.g. "onnxl_b200 0.1 sm_100a". */
 B2_API const char *b2_version(void);
 
@@ -323,6 +341,29 @@ B2_API int b2_ipc_close(void *ptr);
 B2_API int b2_allgather_cols(const b2_tensor *local, void *const *peer_full,
                              uint32_t *const *peer_flags, uint32_t *counters, int world, int rank,
                              int64_t n_total, void *stream);
+
+/* b2_dequantize_matmul with a column-sharded output, fused with its
+ * all-gather: this rank computes y[:, rank N_local : (rank + 1) N_local] (the
+ * weight w holds those N_local columns) and stores every output value
+ * straight into each rank's full buffer over NVLink (peer stores).  With
+ * out->wait_input set, before reading `a` the kernel waits (bounded) until
+ * every rank has finished the group's previous sharded call, so `a` may be
+ * such a call's full output; when it ends it publishes its own completion in
+ * every rank's flag array.  y_local
+ * describes the local slice [.., N_local] (its data is not used).  Every rank
+ * makes the same sequence of calls.  Int4 / uint4 weights with FLOAT16 scales
+ * and activations, up to 16 rows (the register-MMA decode kernel); other
+ * shapes return B2_ERR_UNSUPPORTED (use b2_dequantize_matmul on the slice and
+ * b2_allgather_cols). */
+B2_API int b2_dequantize_matmul_peer(const b2_tensor *a, const b2_tensor *w, const b2_tensor *w_scale,
+                                     const b2_tensor *w_zero_point, int64_t axis, int32_t cast_dtype,
+                                     const b2_tensor *y_local, const b2_peer_out *out,
+                                     void *workspace, size_t *workspace_bytes, void *stream);
+
+/* Waits (on the device, bounded) until every rank has finished the group's
+ * last sharded call or all-gather, so that this rank's full buffers may be
+ * read. */
+B2_API int b2_peer_wait(const b2_peer_out *out, void *stream);
 
 /*
  * Seeded synthetic inputs, identical to onnx-light's SplitMix64 generators

@@ -45,12 +45,20 @@ EXPORTS = ("b2_version", "b2_last_error", "b2_dequantize_linear", "b2_dequantize
            "b2_dequantize_matmul_noalloc", "b2_matmul_integer", "b2_qlinear_matmul", "b2_attention", "b2_attention_ex", "b2_synth_fill",
            "b2_convert", "b2_kernel_status", "b2_selftest_bounded_wait", "b2_selftest_gemm_timeout",
            "b2_rms_normalization", "b2_rotary_embedding", "b2_swiglu", "b2_ipc_alloc",
-           "b2_ipc_free", "b2_ipc_open", "b2_ipc_close", "b2_allgather_cols")
+           "b2_ipc_free", "b2_ipc_open", "b2_ipc_close", "b2_allgather_cols",
+           "b2_dequantize_matmul_peer", "b2_peer_wait")
 
 
 class B2Tensor(C.Structure):
     _fields_ = [("data", C.c_void_p), ("dtype", C.c_int32), ("ndim", C.c_int32),
                 ("shape", C.POINTER(C.c_int64))]
+
+
+class B2PeerOut(C.Structure):
+    """b2_peer_out: a column-sharded output over a multi-GPU group."""
+    _fields_ = [("full", C.c_void_p * 8), ("flags", C.c_void_p * 8), ("counters", C.c_void_p),
+                ("world", C.c_int32), ("rank", C.c_int32), ("n_full", C.c_int64),
+                ("wait_input", C.c_int32)]
 
 
 class B2AttentionAttrs(C.Structure):
@@ -110,6 +118,9 @@ def lib() -> C.CDLL:
                 L.b2_ipc_close.argtypes = [P]
                 L.b2_allgather_cols.argtypes = [T, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), P,
                                                 C.c_int, C.c_int, C.c_int64, P]
+                L.b2_dequantize_matmul_peer.argtypes = [T, T, T, T, C.c_int64, C.c_int32, T,
+                                                        C.POINTER(B2PeerOut), P, SZ, P]
+                L.b2_peer_wait.argtypes = [C.POINTER(B2PeerOut), P]
                 L.b2_synth_fill.argtypes = [C.c_int32, C.c_uint64, C.c_int64, C.c_double,
                                             C.c_double, P, P]
                 L.b2_convert.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int64, P]

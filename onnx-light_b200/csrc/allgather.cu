@@ -103,6 +103,22 @@ __global__ void __launch_bounds__(AG_THREADS) allgather_cols_kernel(const AgArgs
   }
 }
 
+// One thread: wait until every rank has published the generation this rank
+// last published (its last sharded call or all-gather).
+__global__ void peer_wait_kernel(const uint32_t *mine, const uint32_t *counters, int world,
+                                 uint64_t wait_ns) {
+  const uint32_t gen = *(volatile const uint32_t *)(counters + 1);
+  const uint64_t t0 = tc::globaltimer();
+  for (int r = 0; r < world; ++r)
+    while ((int32_t)(ld_acquire_sys(mine + r) - gen) < 0) {
+      if (tc::globaltimer() - t0 > wait_ns) {
+        atomicExch(&g_allgather_status, tc::kTimeoutFull);
+        return;
+      }
+      __nanosleep(32);
+    }
+}
+
 } // namespace
 
 int status_read_allgather(int reset) {
@@ -190,6 +206,17 @@ extern "C" int b2_allgather_cols(const b2_tensor *local, void *const *peer_full,
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   allgather_cols_kernel<<<(unsigned)blocks, AG_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  B2_LAUNCH_CHECK();
+  return B2_OK;
+}
+
+extern "C" int b2_peer_wait(const b2_peer_out *out, void *stream) {
+  if (!out || !out->counters) B2_FAIL(B2_ERR_INVALID_ARGUMENT, "b2_peer_wait: null argument");
+  B2_ENFORCE(out->world >= 1 && out->world <= AG_MAX_WORLD, "b2_peer_wait: world must be 1..%d", AG_MAX_WORLD);
+  B2_ENFORCE(out->rank >= 0 && out->rank < out->world && out->flags[out->rank],
+             "b2_peer_wait: rank out of range or null flags");
+  peer_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(out->flags[out->rank], out->counters,
+                                                                    out->world, 5000000000ull);
   B2_LAUNCH_CHECK();
   return B2_OK;
 }

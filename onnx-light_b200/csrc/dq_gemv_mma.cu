@@ -61,6 +61,7 @@ __device__ int g_gemv_mma_status;
 
 namespace {
 
+constexpr int kPeerMax = 8;
 constexpr int GM_TN = 256;                         // columns per tile (128 packed bytes / row)
 constexpr int GM_TK = 128;                         // weight rows per stage
 #ifndef GM_RING
@@ -96,6 +97,17 @@ struct GmArgs {
   // others cq; each CTA one contiguous K slice of one tile.
   int aligned, cq, cr;
   uint64_t wait_ns;
+  // Column-sharded output over a multi-GPU group (world > 1): every output
+  // value goes to each rank's full [M, ldy] buffer at column col_off + n, and
+  // the call first waits until every rank has finished the group's previous
+  // call, then publishes its own completion (a generation number) in every
+  // rank's flag array.
+  int world, rank;
+  int64_t ldy, col_off;
+  __half *peer_y[kPeerMax];
+  uint32_t *peer_flags[kPeerMax];
+  uint32_t *pctr; // this rank's [0] CTA arrivals, [1] generation
+  int wait_input; // wait for every rank's previous call before reading a
 };
 
 template <int NT> struct GmSmem {
@@ -173,6 +185,25 @@ __device__ __forceinline__ void tile_slice(int b, int cq, int cr, int &tile, int
 }
 __device__ __forceinline__ void red_release_add(uint32_t *p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Two output values (columns col, col + 1 of row m) to y, or to every rank's
+// full buffer when the output is column-sharded.
+__device__ __forceinline__ void store_h2(const GmArgs &g, int64_t m, int64_t col, __half2 v) {
+  if (g.world <= 1) {
+    *reinterpret_cast<__half2 *>(g.y + m * g.ldy + col) = v;
+    return;
+  }
+#pragma unroll
+  for (int r = 0; r < kPeerMax; ++r)
+    if (r < g.world) *reinterpret_cast<__half2 *>(g.peer_y[r] + m * g.ldy + g.col_off + col) = v;
 }
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
   uint32_t v;
@@ -253,7 +284,8 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + L::kOffBar);
   uint64_t *empty = full + GM_STAGES;
-  volatile int *flags = reinterpret_cast<volatile int *>(empty + GM_STAGES); // [0] abort, [1] last
+  // [0] abort, [1] last, [2] stored to peers
+  volatile int *flags = reinterpret_cast<volatile int *>(empty + GM_STAGES);
   float *red = reinterpret_cast<float *>(sm + L::kOffRed);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -277,6 +309,7 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     }
     flags[0] = 0;
     flags[1] = 0;
+    flags[2] = 0;
     tc::fence_barrier_init();
   }
   if (warp == GM_CONSUMERS && lane == 0) {
@@ -310,6 +343,27 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
   // (activations) or write what it reads (output, workspace).
   griddep_wait();
   griddep_launch();
+  if (g.world > 1 && g.wait_input) {
+    // Column-sharded: the activations are a previous sharded call's output,
+    // which other ranks store into this rank's buffer.  Wait (bounded) until
+    // every rank has published this rank's current generation.
+    if (threadIdx.x == 0) {
+      const uint32_t gen = *(volatile uint32_t *)(g.pctr + 1); // calls this rank completed
+      const uint32_t *mine = g.peer_flags[g.rank];
+      const uint64_t t0 = tc::globaltimer();
+      for (int r = 0; r < g.world && !flags[0]; ++r)
+        while ((int32_t)(ld_acquire_sys(mine + r) - gen) < 0) {
+          if (tc::globaltimer() - t0 > 5000000000ull) {
+            atomicExch(&g_gemv_mma_status, tc::kTimeoutFull);
+            flags[0] = 1;
+            break;
+          }
+          __nanosleep(32);
+        }
+      asm volatile("fence.proxy.async.global;" ::: "memory"); // before the TMA reads of them
+    }
+    __syncthreads();
+  }
 
   if (warp == GM_CONSUMERS) {
     // ------------------------------ producer ------------------------------
@@ -546,9 +600,9 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
             }
             const int m = e / (GM_TN / 4), col = (e % (GM_TN / 4)) * 4;
             if (n0 + col >= g.N) continue; // ragged last tile; N % 4 == 0
-            __half2 *dst = reinterpret_cast<__half2 *>(g.y + (int64_t)m * g.N + n0 + col);
-            dst[0] = __floats2half2_rn(sum.x, sum.y);
-            dst[1] = __floats2half2_rn(sum.z, sum.w);
+            store_h2(g, m, n0 + col, __floats2half2_rn(sum.x, sum.y));
+            store_h2(g, m, n0 + col + 2, __floats2half2_rn(sum.z, sum.w));
+            flags[2] = 1;
           }
         }
       }
@@ -562,12 +616,9 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             const int m = nt * 8 + 2 * t;
-            if (m < g.M)
-              *reinterpret_cast<__half2 *>(g.y + (int64_t)m * g.N + col) =
-                  __floats2half2_rn(acc[mt][nt][0], acc[mt][nt][2]);
-            if (m + 1 < g.M)
-              *reinterpret_cast<__half2 *>(g.y + (int64_t)(m + 1) * g.N + col) =
-                  __floats2half2_rn(acc[mt][nt][1], acc[mt][nt][3]);
+            if (m < g.M) store_h2(g, m, col, __floats2half2_rn(acc[mt][nt][0], acc[mt][nt][2]));
+            if (m + 1 < g.M) store_h2(g, m + 1, col, __floats2half2_rn(acc[mt][nt][1], acc[mt][nt][3]));
+            flags[2] = 1;
           }
         }
       }
@@ -631,9 +682,9 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
           }
           const int m = e / (GM_TN / 4), col = (e % (GM_TN / 4)) * 4;
           if (n0 + col >= g.N) continue; // ragged last tile; N % 4 == 0
-          __half2 *dst = reinterpret_cast<__half2 *>(g.y + (int64_t)m * g.N + n0 + col);
-          dst[0] = __floats2half2_rn(sum.x, sum.y);
-          dst[1] = __floats2half2_rn(sum.z, sum.w);
+          store_h2(g, m, n0 + col, __floats2half2_rn(sum.x, sum.y));
+          store_h2(g, m, n0 + col + 2, __floats2half2_rn(sum.z, sum.w));
+          flags[2] = 1;
         }
       }
     }
@@ -644,6 +695,27 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.0f;
     seg0 = seg1;
+  }
+  if (g.world > 1) {
+    // Publish completion: a CTA that stored output to peers makes those
+    // stores visible system-wide (fence.sc.sys, after the barrier that orders
+    // its threads' stores before thread 0), every CTA counts itself done, and
+    // the last one bumps the generation and stores it in every rank's flag
+    // array with a system-scope release.  Only the CTAs that wrote outputs
+    // (about one per tile) pay the system-scope fence.
+    consumers_sync();
+    if (threadIdx.x == 0) {
+      if (flags[2]) __threadfence_system();
+      const uint32_t prev = atom_add_acq_rel(g.pctr, 1u);
+      if (prev + 1 == gridDim.x) {
+        g.pctr[0] = 0u;
+        const uint32_t gen = g.pctr[1] + 1u;
+        g.pctr[1] = gen;
+#pragma unroll
+        for (int r = 0; r < kPeerMax; ++r)
+          if (r < g.world) st_release_sys(g.peer_flags[r] + g.rank, gen);
+      }
+    }
   }
 }
 
@@ -736,6 +808,16 @@ int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStrea
   a.srows = m.srows;
   a.is_signed = p.wdt == kInt4;
   a.scalar_scale = reinterpret_cast<const uint16_t *>(p.scale);
+  a.world = p.world > 1 ? p.world : 1;
+  a.rank = p.rank;
+  a.ldy = p.world > 1 ? p.n_full : p.N;
+  a.col_off = p.world > 1 ? p.col_off : 0;
+  for (int r = 0; r < kPeerMax; ++r) {
+    a.peer_y[r] = r < a.world ? static_cast<__half *>(p.peer_full[r]) : nullptr;
+    a.peer_flags[r] = r < a.world ? p.peer_flags[r] : nullptr;
+  }
+  a.pctr = p.pctr;
+  a.wait_input = p.wait_input;
   a.aligned = m.aligned;
   a.cq = m.cq;
   a.cr = m.cr;

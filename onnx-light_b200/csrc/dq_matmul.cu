@@ -943,6 +943,53 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
   return launch_simt<__nv_bfloat16>(p, pl, st);
 }
 
+extern "C" int b2_dequantize_matmul_peer(const b2_tensor *a, const b2_tensor *w,
+                                         const b2_tensor *w_scale, const b2_tensor *w_zero_point,
+                                         int64_t axis, int32_t cast_dtype, const b2_tensor *y_local,
+                                         const b2_peer_out *out, void *workspace,
+                                         size_t *workspace_bytes, void *stream) {
+  if (!out) B2_FAIL(B2_ERR_INVALID_ARGUMENT, "b2_dequantize_matmul_peer: null peer output");
+  DqMmParams p{};
+  int rc = dq_mm_validate(a, w, w_scale, w_zero_point, axis, cast_dtype, y_local, p);
+  if (rc) return rc;
+  B2_ENFORCE(out->world >= 2 && out->world <= 8, "b2_dequantize_matmul_peer: world must be 2..8");
+  B2_ENFORCE(out->rank >= 0 && out->rank < out->world, "b2_dequantize_matmul_peer: rank out of range");
+  B2_ENFORCE(out->n_full == p.N * out->world,
+             "b2_dequantize_matmul_peer: n_full must be world x the local slice's columns");
+  B2_ENFORCE(out->counters != nullptr, "b2_dequantize_matmul_peer: null counters");
+  for (int r = 0; r < out->world; ++r)
+    B2_ENFORCE(out->full[r] && out->flags[r] && reinterpret_cast<uintptr_t>(out->full[r]) % 16 == 0,
+               "b2_dequantize_matmul_peer: peer buffers must be non-null and 16-byte aligned");
+  // the fused peer stores live in the register-MMA decode kernel only
+  if (forced_path() != kPathAuto || !dq_mma_eligible(p))
+    B2_FAIL(B2_ERR_UNSUPPORTED,
+            "b2_dequantize_matmul_peer: only the int4 / fp16 decode kernel (M <= 16) stores to peers");
+  const size_t need = dq_mma_workspace(p);
+  rc = workspace_check(workspace, workspace_bytes, need);
+  if (rc < 0) return rc;
+  if (rc == 1) return B2_OK; // size query
+  p.a = a->data;
+  p.w = static_cast<const uint8_t *>(w->data);
+  p.scale = static_cast<const uint8_t *>(w_scale->data);
+  p.zp = nullptr;
+  p.y = out->full[out->rank];
+  p.world = out->world;
+  p.rank = out->rank;
+  p.n_full = out->n_full;
+  p.col_off = (int64_t)out->rank * p.N;
+  for (int r = 0; r < out->world; ++r) {
+    p.peer_full[r] = out->full[r];
+    p.peer_flags[r] = out->flags[r];
+  }
+  p.pctr = out->counters;
+  p.wait_input = out->wait_input;
+  if (!dq_mma_aligned(p) || (p.col_off * 2) % 4 != 0 || (p.n_full * 2) % 4 != 0)
+    B2_FAIL(B2_ERR_UNSUPPORTED, "b2_dequantize_matmul_peer: tensors must be 16-byte aligned");
+  if (p.M == 0 || p.N == 0 || p.K == 0)
+    B2_FAIL(B2_ERR_UNSUPPORTED, "b2_dequantize_matmul_peer: empty shapes are not sharded");
+  return dq_mma_launch(p, workspace, static_cast<cudaStream_t>(stream));
+}
+
 // Self-test of the tensor-core GEMM's time-out path (see the header): the
 // planned dq_gemm_tc launch runs with no TMA issued, so its first data wait
 // runs out after limit_ns; every CTA gives up, arrives on its split-K counter

@@ -33,6 +33,14 @@ struct DqMmParams {
   int gemv_nkb;       // scale rows staged per CTA (GEMV fast path)
   float *partials;    // split-K workspace
   uint32_t *counters; // split-K arrival counters (zero between calls)
+  // Column-sharded output over a multi-GPU group (b2_dequantize_matmul_peer):
+  // world > 1 sends every output value to each rank's full buffer.
+  int world, rank;
+  int64_t n_full, col_off;
+  void *peer_full[8];
+  uint32_t *peer_flags[8];
+  uint32_t *pctr;
+  int wait_input;
 };
 
 // Tensor-core path (dq_gemm_tc.cu).

@@ -9,7 +9,11 @@
   the KV cache of its heads and the matching query heads (GQA groups never
   straddle ranks), and the per-head outputs are all-gathered.
 
-Two gathers:
+Three ways to produce the gathered output:
+* `PeerGroup.matmul` (GPUs, int4 decode): the fused DequantizeLinear -> MatMul
+  kernel stores its column slice straight into every rank's full output
+  (b2_dequantize_matmul_peer) and publishes its completion; the next sharded
+  call waits for it before reading -- no gather kernel at all;
 * `PeerGroup.gather` (GPUs): b2_allgather_cols stores each rank's slice straight
   into the [M, N] output of every rank over NVLink (CUDA IPC peer buffers set
   up once) and waits on per-rank arrival flags -- one kernel, no staging
@@ -138,6 +142,7 @@ class PeerGroup:
         self._own = []      # (ptr) allocations of this rank
         self._opened = []   # peer mappings
         self.bufs: Dict[str, tuple] = {}
+        self._dirty = set()  # buffers a sharded call wrote since the last wait
         # flags: one array per rank; counters: local only
         flags_ptr, peers = self._shared(self.FLAGS * 4)
         self.flag_ptrs = (C.c_void_p * self.world)(*peers)
@@ -178,8 +183,57 @@ class PeerGroup:
             self.bufs[name] = (t, (C.c_void_p * self.world)(*peers), int(shape[-1]))
         return self.bufs[name][0]
 
+    def _peer_out(self, name: str):
+        full, peers, n_total = self.bufs[name]
+        po = self._capi.B2PeerOut()
+        for r in range(self.world):
+            po.full[r] = peers[r]
+            po.flags[r] = self.flag_ptrs[r]
+        po.counters = self.counters
+        po.world, po.rank, po.n_full = self.world, self.rank, n_total
+        return po
+
+    def matmul(self, name: str, a: torch.Tensor, w, scale: torch.Tensor, axis: int = 0,
+               workspace_fn=None) -> torch.Tensor:
+        """y = DequantizeLinear(w, scale) @ a on this rank's column slice, stored
+        into every rank's `buffer(name)` by the kernel itself
+        (b2_dequantize_matmul_peer); returns this rank's full buffer, complete
+        for the next sharded call (which waits for it) or after `wait()`."""
+        from . import kernels
+        full, peers, n_total = self.bufs[name]
+        n_loc = n_total // self.world
+        lead = tuple(a.shape[:-1])
+        po = self._peer_out(name)
+        # wait for the other ranks only when the input is a peer output
+        # written since the last wait (then every earlier call is complete)
+        src = next((n for n, b in self.bufs.items() if b[0].data_ptr() == a.data_ptr()), None)
+        po.wait_input = 1 if src in self._dirty else 0
+        if po.wait_input:
+            self._dirty.clear()
+        self._dirty.add(name)
+        ad = self._capi.Desc(a.data_ptr(), self._capi.TORCH_TO_ONNX[a.dtype], tuple(a.shape))
+        wd = kernels._desc(w)
+        sd = kernels._desc(scale)
+        yd = self._capi.Desc(0, self._capi.TORCH_TO_ONNX[a.dtype], lead + (n_loc,))
+        kernels._call_with_workspace(self.lib.b2_dequantize_matmul_peer,
+                                     (ad.ref, wd.ref, sd.ref, None, int(axis), 0, yd.ref,
+                                      C.byref(po)), (self._capi.stream_ptr(a.device),), a.device)
+        return full
+
+    def wait(self, device=None):
+        """Makes this rank's stream wait until every rank finished the group's
+        last sharded call or gather (so the full buffers may be read)."""
+        po = self._capi.B2PeerOut()
+        for r in range(self.world):
+            po.flags[r] = self.flag_ptrs[r]
+        po.counters = self.counters
+        po.world, po.rank, po.n_full = self.world, self.rank, 0
+        self._capi.check(self.lib.b2_peer_wait(C.byref(po), self._capi.stream_ptr(device)))
+        self._dirty.clear()
+
     def gather(self, name: str, local: torch.Tensor) -> torch.Tensor:
         full, peers, n_total = self.bufs[name]
+        self._dirty.clear()  # the gather waits for every rank's slice
         d = self._capi.Desc(local.data_ptr(), self._capi.TORCH_TO_ONNX[local.dtype],
                             tuple(local.shape))
         self._capi.check(self.lib.b2_allgather_cols(

@@ -22,6 +22,7 @@ def _free_port():
 def _worker(rank, world, port, mode, result):
     import sys
     sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.join(os.path.dirname(HERE), "oracle"))
     import torch.distributed as dist
     from conftest import load_package
     b2 = load_package()  # noqa: F841
@@ -56,6 +57,48 @@ def _worker(rank, world, port, mode, result):
         ok &= torch.equal(full, want + 1)
         ok &= lib.b2_kernel_status(1) == 0
         del g
+    elif mode == "fused_matmul":
+        # b2_dequantize_matmul_peer: each rank's int4 decode GEMV stores its
+        # column slice into both ranks' outputs; a chain of two sharded
+        # calls (the second reads the first's gathered output, waiting for
+        # the other rank's slice) matches the oracle's chain on the full
+        # weights within the fp16 contract.
+        import numpy as np
+        import oracle as O
+        from util import random_q, scale_raw, to_dev, rel_l2
+        K, N = 1024, 512
+        nl = N // world
+        w1 = random_q(71, (K, N), O.INT4)
+        s1 = scale_raw(O.rand_uniform(72, ((K // 128) * N,), 0.002, 0.02), O.FLOAT16).reshape(K // 128, N)
+        w2 = random_q(73, (N, K), O.INT4)
+        s2 = scale_raw(O.rand_uniform(74, ((N // 128) * K,), 0.002, 0.02), O.FLOAT16).reshape(N // 128, K)
+        x = O.f32_to_f16_bits(O.randn(75, (1, K)))
+        y1 = O.matmul(x, O.dequantize_linear(w1, O.INT4, (K, N), s1.ravel(), O.FLOAT16, (K // 128, N),
+                                              None, None, 0), O.FLOAT16)
+        y2 = O.matmul(y1, O.dequantize_linear(w2, O.INT4, (N, K), s2.ravel(), O.FLOAT16, (N // 128, K),
+                                              None, None, 0), O.FLOAT16)
+        # slice the packed int4 weight by columns on the host (two codes per byte)
+        def slice_int4(wq, kk, nn):
+            b = np.asarray(wq, np.uint8).reshape(kk, nn // 2)
+            return np.ascontiguousarray(b[:, rank * (nn // world) // 2:(rank + 1) * (nn // world) // 2])
+        tw1 = b2.QTensor(to_dev(slice_int4(w1, K, N)), O.INT4, (K, nl))
+        ts1 = to_dev(np.ascontiguousarray(s1.reshape(-1, N)[:, rank * nl:(rank + 1) * nl]), torch.float16)
+        tw2 = b2.QTensor(to_dev(slice_int4(w2, N, K)), O.INT4, (N, K // world))
+        ts2 = to_dev(np.ascontiguousarray(s2.reshape(-1, K)[:, rank * (K // world):(rank + 1) * (K // world)]),
+                     torch.float16)
+        full1 = peers.buffer("y1", (1, N), torch.float16)
+        full2 = peers.buffer("y2", (1, K), torch.float16)
+        tx = to_dev(x).view(torch.float16).reshape(1, K)
+        for _ in range(2):  # twice: the generations advance
+            peers.matmul("y1", tx, tw1, ts1)
+            peers.matmul("y2", full1, tw2, ts2)
+            peers.wait()
+            torch.cuda.synchronize()
+            got1 = full1.float().cpu().numpy()
+            got2 = full2.float().cpu().numpy()
+            ok &= rel_l2(got1, O.f16_bits_to_f32(y1)) <= 1e-3
+            ok &= rel_l2(got2, O.f16_bits_to_f32(y2)) <= 1e-3
+        ok &= lib.b2_kernel_status(1) == 0
     else:  # rank 1 never issues its gather: rank 0's wait runs out (5 s) and reports
         if rank == 0:
             peers.gather("y", local)
@@ -67,7 +110,7 @@ def _worker(rank, world, port, mode, result):
     result[rank] = bool(ok)
 
 
-@pytest.mark.parametrize("mode", ["gather", "absent_peer_times_out"])
+@pytest.mark.parametrize("mode", ["gather", "fused_matmul", "absent_peer_times_out"])
 def test_allgather_cols_two_gpus(cuda, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
