@@ -191,9 +191,6 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 // Two output values (columns col, col + 1 of row m) to y, or to every rank's
 // full buffer when the output is column-sharded.
 __device__ __forceinline__ void store_h2(const GmArgs &g, int64_t m, int64_t col, __half2 v) {
@@ -284,7 +281,7 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + L::kOffBar);
   uint64_t *empty = full + GM_STAGES;
-  // [0] abort, [1] last, [2] stored to peers
+  // [0] abort, [1] last
   volatile int *flags = reinterpret_cast<volatile int *>(empty + GM_STAGES);
   float *red = reinterpret_cast<float *>(sm + L::kOffRed);
 
@@ -309,7 +306,6 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     }
     flags[0] = 0;
     flags[1] = 0;
-    flags[2] = 0;
     tc::fence_barrier_init();
   }
   if (warp == GM_CONSUMERS && lane == 0) {
@@ -602,7 +598,6 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
             if (n0 + col >= g.N) continue; // ragged last tile; N % 4 == 0
             store_h2(g, m, n0 + col, __floats2half2_rn(sum.x, sum.y));
             store_h2(g, m, n0 + col + 2, __floats2half2_rn(sum.z, sum.w));
-            flags[2] = 1;
           }
         }
       }
@@ -618,7 +613,6 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
             const int m = nt * 8 + 2 * t;
             if (m < g.M) store_h2(g, m, col, __floats2half2_rn(acc[mt][nt][0], acc[mt][nt][2]));
             if (m + 1 < g.M) store_h2(g, m + 1, col, __floats2half2_rn(acc[mt][nt][1], acc[mt][nt][3]));
-            flags[2] = 1;
           }
         }
       }
@@ -684,7 +678,6 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
           if (n0 + col >= g.N) continue; // ragged last tile; N % 4 == 0
           store_h2(g, m, n0 + col, __floats2half2_rn(sum.x, sum.y));
           store_h2(g, m, n0 + col + 2, __floats2half2_rn(sum.z, sum.w));
-          flags[2] = 1;
         }
       }
     }
@@ -697,23 +690,26 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     seg0 = seg1;
   }
   if (g.world > 1) {
-    // Publish completion: a CTA that stored output to peers makes those
-    // stores visible system-wide (fence.sc.sys, after the barrier that orders
-    // its threads' stores before thread 0), every CTA counts itself done, and
-    // the last one bumps the generation and stores it in every rank's flag
-    // array with a system-scope release.  Only the CTAs that wrote outputs
-    // (about one per tile) pay the system-scope fence.
+    // Publish completion: every CTA counts itself done with a gpu-scope
+    // acquire/release add (the barrier orders its threads' peer stores before
+    // it); the last one, having acquired them all, issues one system-scope
+    // fence -- cumulative over every store it has observed -- and then stores
+    // the call's generation in every rank's flag array (a release pattern).
+    // One system-scope fence per call: it sits on the path to the next
+    // launch, so per-CTA fences would each add their NVLink round trip.
     consumers_sync();
     if (threadIdx.x == 0) {
-      if (flags[2]) __threadfence_system();
       const uint32_t prev = atom_add_acq_rel(g.pctr, 1u);
       if (prev + 1 == gridDim.x) {
         g.pctr[0] = 0u;
         const uint32_t gen = g.pctr[1] + 1u;
         g.pctr[1] = gen;
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
 #pragma unroll
         for (int r = 0; r < kPeerMax; ++r)
-          if (r < g.world) st_release_sys(g.peer_flags[r] + g.rank, gen);
+          if (r < g.world)
+            asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(g.peer_flags[r] + g.rank), "r"(gen)
+                         : "memory");
       }
     }
   }
