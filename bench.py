@@ -508,11 +508,9 @@ def decode_kernel(B: int) -> str:
     if B <= 8:
         return "dq_gemv_mma"
     if B <= 16:
-        return "dq_gemv_n (4096 columns), dq_gemv_mma (11008 columns)"
-    if B <= 32:
-        return "dq_gemv_n"
+        return "dq_gemv_n (4096 x 4096), dq_gemv_mma (11008-column and 11008-row shapes)"
     if B <= 64:
-        return "dq_gemv_x"
+        return "dq_gemv_n"
     return "dq_gemm_tc"
 
 
@@ -1371,7 +1369,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-4 attention and config-2 MatMulInteger measurements")
-    ap.add_argument("--only", choices=["attention4", "mmi2", "prefill5", "decoder"],
+    ap.add_argument("--only", choices=["attention4", "mmi2", "prefill5", "decoder",
+                                       "config1", "dequantize"],
                     help="run one secondary measurement alone on cuda:0 (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -1383,7 +1382,8 @@ def main():
         device = torch.device("cuda", 0)
         stream = torch.cuda.Stream(device)
         fn = {"attention4": attention_config4, "mmi2": matmul_integer_config2,
-              "prefill5": prefill_config5, "decoder": decoder_ops}[args.only]
+              "prefill5": prefill_config5, "decoder": decoder_ops,
+              "config1": dq_matmul_config1, "dequantize": dequantize_standalone}[args.only]
         print(json.dumps(fn(b2, synth, device, stream, False)), flush=True)
         return
     if args.impl == "reference":

@@ -1,6 +1,6 @@
 // Decode-shaped fused DequantizeLinear -> [Cast] -> MatMul on narrow column
 // tiles: INT4 / UINT4 weights, FLOAT16 scales (no zero point), FLOAT16
-// activations and output, M <= 32 rows.  The weight is dequantized exactly as
+// activations and output, M <= 64 rows.  The weight is dequantized exactly as
 // the reference does (fp16(q * s), see dq_gemv_x.cu for the argument) and
 // multiplied on mma.sync with fp32 accumulation.
 //
@@ -18,15 +18,18 @@
 // a DRAM sector; the neighbouring CTA reads the other half at the same time,
 // so L2 serves it and HBM traffic stays the packed weight once.
 //
-// Pipeline: the K range is cut into chunks of 256 rows (4 KB of packed
-// weights); chunk c belongs to warp c % 8, which owns two ring slots and loads
-// its own chunks by TMA (weights, the chunk's scale rows, the activation slice
-// in 128-byte swizzled 64-column boxes), so warps never wait for one another
-// before the final reduction.  The first two chunks' weights and scales of
-// every warp are requested before the programmatic-launch wait (they do not
-// depend on the kernel ahead), their activations after it.  Every mma.sync
-// accumulator chain alternates between two register sets, so consecutive
-// k16 steps do not wait on each other's results.
+// Pipeline: the K range is cut into chunks of 256 / NT rows (64 at least);
+// chunk c belongs to warp c % 8, which owns its own ring slots and loads its
+// own chunks by TMA (weights, the chunk's scale rows, the activation slice in
+// 128-byte swizzled 64-column boxes), so warps never wait for one another
+// before the final reduction.  The activation fragments of a k16 step come
+// from one non-transposing ldmatrix per pair of 8-row tiles.  The first
+// ring fill's weights and scales of every warp are requested before the
+// programmatic-launch wait (they do not depend on the kernel ahead), their
+// activations after it.  Up to four activation tiles every mma.sync
+// accumulator chain alternates between two register sets, so consecutive k16
+// steps do not wait on each other's results (eight tiles give the same
+// independence within a step).
 #include "dq_matmul.cuh"
 #include "tc_common.cuh"
 
@@ -51,9 +54,22 @@ namespace {
 constexpr int GN_TN = 32;                  // columns per tile (16 packed bytes per row)
 constexpr int GN_WARPS = 8;
 constexpr int GN_THREADS = GN_WARPS * 32;
-constexpr int GN_SLOTS_PER_WARP = 2;
-constexpr int GN_SLOTS = GN_WARPS * GN_SLOTS_PER_WARP;
-constexpr int GN_CH_MIN = 64;              // smallest chunk (four activation tiles)
+constexpr int GN_CH_MIN = 64;              // smallest chunk (one 64-column activation box)
+constexpr int GN_MAX_ROWS = 64;            // activation rows (eight 8-row tiles)
+
+// Ring slots per warp for each activation-tile count (shared memory bound).
+#ifndef GN_SPW1
+#define GN_SPW1 2
+#endif
+#ifndef GN_SPW2
+#define GN_SPW2 3
+#endif
+#ifndef GN_SPW4
+#define GN_SPW4 4
+#endif
+#ifndef GN_SPW8
+#define GN_SPW8 2
+#endif
 
 struct GnArgs {
   __half *y;
@@ -68,21 +84,27 @@ struct GnArgs {
 };
 
 // Chunk rows per activation-tile count: the activation slice of a chunk
-// (rows x 8 NT x 2 bytes) stays 4 KB, so 16 slots fit in shared memory.
+// (rows x 8 NT x 2 bytes) stays 4 KB up to four tiles (8 KB for eight), and
+// every warp owns kSpw ring slots.
 template <int NT> struct GnCfg {
-  static constexpr int kCh = 256 / NT;                        // weight rows per chunk
+  static constexpr int kCh = 256 / NT < GN_CH_MIN ? GN_CH_MIN : 256 / NT; // weight rows per chunk
+  static constexpr int kSpw = NT == 1 ? GN_SPW1 : NT == 2 ? GN_SPW2 : NT == 4 ? GN_SPW4 : GN_SPW8;
+  static constexpr int kSlots = GN_WARPS * kSpw;
+  static constexpr int kSets = NT >= 8 ? 1 : 2;               // accumulator sets (k16 parity)
   static constexpr uint32_t kW = kCh * GN_TN / 2;             // packed weights of a chunk
   static constexpr int kScRows = kCh / 16;                    // scale rows per chunk at most (block 16)
   static constexpr uint32_t kSc = kScRows * GN_TN * 2;
   static constexpr uint32_t kABox = 8u * NT * 128;            // one 64-column box, 8 NT rows
   static constexpr uint32_t kA = (kCh / 64) * kABox;          // a chunk's activations
-  static constexpr uint32_t kOffA = GN_SLOTS * kW;            // 1024-aligned (swizzled boxes)
-  static constexpr uint32_t kOffS = kOffA + GN_SLOTS * kA;
-  static constexpr uint32_t kOffRed = kOffS + GN_SLOTS * kSc;
+  static constexpr uint32_t kOffA = kSlots * kW;              // 1024-aligned (swizzled boxes)
+  static constexpr uint32_t kOffS = kOffA + kSlots * kA;
+  static constexpr uint32_t kOffRed = kOffS + kSlots * kSc;
   static constexpr uint32_t kRedBytes = GN_WARPS * 2 * NT * 4 * 32 * 4;
   static constexpr uint32_t kOffBar = kOffRed + kRedBytes;
-  static constexpr uint32_t kBytes = kOffBar + GN_SLOTS * 8 + 16;
+  static constexpr uint32_t kBytes = kOffBar + kSlots * 8 + 16;
   static constexpr size_t kDynamic = kBytes + 1024; // alignment slack
+  static_assert(kOffA % 1024 == 0 && kABox % 1024 == 0, "swizzled activation boxes");
+  static_assert(kDynamic <= 232448, "shared memory per CTA");
 };
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -101,6 +123,16 @@ __device__ __forceinline__ void ldsm_t4(uint32_t addr, uint32_t (&r)[4]) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm2(uint32_t addr, uint32_t (&r)[2]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
 // Two fp16 weights from two packed codes at bits 0..3 and 16..19 of `v`:
 // (1024 + code') - magic = q exactly, then q * s rounded to nearest even.
 __device__ __forceinline__ uint32_t dq2(uint32_t v, uint32_t magic, uint32_t s2) {
@@ -115,17 +147,19 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
     dq_gemv_n(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
               const __grid_constant__ CUtensorMap map_s, const GnArgs g) {
   using C = GnCfg<NT>;
+  constexpr int SPW = C::kSpw;
+  constexpr int NS = C::kSets;
   static_assert(C::kCh % 64 == 0 && C::kCh >= GN_CH_MIN, "whole 64-column activation boxes");
   extern __shared__ uint8_t dsm[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + C::kOffBar);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(full + GN_SLOTS);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(full + C::kSlots);
   float *red = reinterpret_cast<float *>(sm + C::kOffRed);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gq = lane >> 2, t = lane & 3;
+  const int gq = lane >> 2;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < GN_SLOTS; ++i) tc::mbar_init(&full[i], 1);
+    for (int i = 0; i < C::kSlots; ++i) tc::mbar_init(&full[i], 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
     tc::prefetch_tensormap(&map_w);
@@ -149,7 +183,7 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
   auto fill_w = [&](int seq) {
     int tile, k0;
     coords(seq, tile, k0);
-    const int sl = warp * GN_SLOTS_PER_WARP + (seq & 1);
+    const int sl = warp * SPW + seq % SPW;
     tc::mbar_expect_tx(&full[sl], tx);
     tc::tma_load_2d(sm + sl * C::kW, &map_w, &full[sl], tile * (GN_TN / 2), k0);
     if (g.srows) {
@@ -160,12 +194,12 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
   auto fill_a = [&](int seq) {
     int tile, k0;
     coords(seq, tile, k0);
-    const int sl = warp * GN_SLOTS_PER_WARP + (seq & 1);
+    const int sl = warp * SPW + seq % SPW;
     uint8_t *sa = sm + C::kOffA + sl * C::kA;
 #pragma unroll
     for (int q = 0; q < C::kCh / 64; ++q) tc::tma_load_2d(sa + q * C::kABox, &map_a, &full[sl], k0 + 64 * q, 0);
   };
-  const int pre = total < GN_SLOTS_PER_WARP ? total : GN_SLOTS_PER_WARP;
+  const int pre = total < SPW ? total : SPW;
   int nissued = pre; // fills this warp has requested (lane 0's count)
   if (lane == 0)
     for (int s = 0; s < pre; ++s) fill_w(s);
@@ -187,9 +221,9 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
   int seq = 0;
   for (int it = 0; it < ntile_mine; ++it) {
     const int tile = (int)blockIdx.x + g.grid * it;
-    float acc[2][2][NT][4]; // [set][m-tile][activation tile][fragment]
+    float acc[NS][2][NT][4]; // [set][m-tile][activation tile][fragment]
 #pragma unroll
-    for (int st = 0; st < 2; ++st)
+    for (int st = 0; st < NS; ++st)
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -197,9 +231,9 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[st][mt][nt][e] = 0.0f;
     for (int j = 0; j < nmy; ++j, ++seq) {
-      const int sl = warp * GN_SLOTS_PER_WARP + (seq & 1);
+      const int sl = warp * SPW + seq % SPW;
       if (ok && *abort_flag) ok = false;
-      if (ok && !tc::mbar_wait(&full[sl], (seq >> 1) & 1, g.wait_ns)) {
+      if (ok && !tc::mbar_wait(&full[sl], (seq / SPW) & 1, g.wait_ns)) {
         atomicExch(&g_gemv_n_status, tc::kTimeoutFull);
         *abort_flag = 1;
         ok = false;
@@ -230,17 +264,30 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
                 shi[1] = __byte_perm(w4.y, w4.y, 0x3232);
               }
             }
+            // activation fragments of the k16 step: non-transposing ldmatrix
+            // of the swizzled box, matrix i of lane group i = (tile 2p + (i >> 1),
+            // k half i & 1); lane (g, t) receives row g, k 2t and 2t + 1
             uint32_t B0[NT], B1[NT];
             {
-              const int kb = ((r0 & 63) + 2 * t) * 2; // byte within the 64-column box
               const uint8_t *box = ast + (r0 >> 6) * C::kABox;
+              const int ch0 = (r0 & 63) >> 3; // first 16-byte chunk of the step
 #pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                const int row = nt * 8 + gq;
-                const uint8_t *rb = box + row * 128;
-                B0[nt] = *reinterpret_cast<const uint32_t *>(rb + ((((kb >> 4) ^ (row & 7)) << 4) | (kb & 15)));
-                const int kb2 = kb + 16;
-                B1[nt] = *reinterpret_cast<const uint32_t *>(rb + ((((kb2 >> 4) ^ (row & 7)) << 4) | (kb2 & 15)));
+              for (int pr = 0; pr < (NT + 1) / 2; ++pr) {
+                const int row = (2 * pr + ((mi >> 1) & (NT > 1 ? 1 : 0))) * 8 + (lane & 7);
+                const uint32_t addr = tc::smem_u32(box + row * 128 + (((ch0 + (mi & 1)) ^ (row & 7)) << 4));
+                if constexpr (NT == 1) {
+                  uint32_t r2[2];
+                  ldsm2(addr, r2);
+                  B0[0] = r2[0];
+                  B1[0] = r2[1];
+                } else {
+                  uint32_t r4[4];
+                  ldsm4(addr, r4);
+                  B0[2 * pr] = r4[0];
+                  B1[2 * pr] = r4[1];
+                  B0[2 * pr + 1] = r4[2];
+                  B1[2 * pr + 1] = r4[3];
+                }
               }
             }
             const uint32_t x = r[2 * h], y = r[2 * h + 1]; // rows r0 + 2t.. and r0 + 8 + 2t..
@@ -248,13 +295,13 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
               const uint32_t a0 = dq2(x, magic, slo[0]), a1 = dq2(x >> 4, magic, shi[0]);
               const uint32_t a2 = dq2(y, magic, slo[0]), a3 = dq2(y >> 4, magic, shi[0]);
 #pragma unroll
-              for (int nt = 0; nt < NT; ++nt) mma16816(acc[h][0][nt], a0, a1, a2, a3, B0[nt], B1[nt]);
+              for (int nt = 0; nt < NT; ++nt) mma16816(acc[h % NS][0][nt], a0, a1, a2, a3, B0[nt], B1[nt]);
             }
             {
               const uint32_t a0 = dq2(x >> 8, magic, slo[1]), a1 = dq2(x >> 12, magic, shi[1]);
               const uint32_t a2 = dq2(y >> 8, magic, slo[1]), a3 = dq2(y >> 12, magic, shi[1]);
 #pragma unroll
-              for (int nt = 0; nt < NT; ++nt) mma16816(acc[h][1][nt], a0, a1, a2, a3, B0[nt], B1[nt]);
+              for (int nt = 0; nt < NT; ++nt) mma16816(acc[h % NS][1][nt], a0, a1, a2, a3, B0[nt], B1[nt]);
             }
           }
         }
@@ -263,11 +310,11 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
       // this warp alone reads the slot: once every lane is past it, refill it
       // with the warp's chunk two ahead
       __syncwarp();
-      if (lane == 0 && seq + GN_SLOTS_PER_WARP < total && !*abort_flag) {
+      if (lane == 0 && seq + SPW < total && !*abort_flag) {
         tc::fence_proxy_async();
-        fill_w(seq + GN_SLOTS_PER_WARP);
-        fill_a(seq + GN_SLOTS_PER_WARP);
-        nissued = seq + GN_SLOTS_PER_WARP + 1;
+        fill_w(seq + SPW);
+        fill_a(seq + SPW);
+        nissued = seq + SPW + 1;
       }
     }
     // ---- the eight warps' K slices summed in warp order ----
@@ -277,7 +324,7 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) rw[((mt * NT + nt) * 4 + e) * 32 + lane] = acc[0][mt][nt][e] + acc[1][mt][nt][e];
+        for (int e = 0; e < 4; ++e) rw[((mt * NT + nt) * 4 + e) * 32 + lane] = NS == 2 ? acc[0][mt][nt][e] + acc[NS - 1][mt][nt][e] : acc[0][mt][nt][e];
     __syncthreads();
     const bool abort_now = *abort_flag != 0;
     for (int idx = threadIdx.x; idx < 2 * NT * 4 * 32; idx += GN_THREADS) {
@@ -297,8 +344,8 @@ __global__ void __launch_bounds__(GN_THREADS, 1)
   // The CTA must not end with copies in flight into its shared memory: after
   // a give-up, wait (bounded) for the fills this warp issued.
   if (lane == 0 && *abort_flag)
-    for (int s = nissued > GN_SLOTS_PER_WARP ? nissued - GN_SLOTS_PER_WARP : 0; s < nissued; ++s)
-      tc::mbar_wait(&full[warp * GN_SLOTS_PER_WARP + (s & 1)], (s >> 1) & 1, g.wait_ns);
+    for (int s = nissued > SPW ? nissued - SPW : 0; s < nissued; ++s)
+      tc::mbar_wait(&full[warp * SPW + s % SPW], (s / SPW) & 1, g.wait_ns);
 }
 
 struct GnPlan {
@@ -307,9 +354,9 @@ struct GnPlan {
 
 GnPlan gn_plan(const DqMmParams &p) {
   GnPlan m;
-  m.nt = p.M <= 8 ? 1 : p.M <= 16 ? 2 : 4;
+  m.nt = p.M <= 8 ? 1 : p.M <= 16 ? 2 : p.M <= 32 ? 4 : 8;
   m.ntiles = (int)((p.N + GN_TN - 1) / GN_TN);
-  const int ch = 256 / m.nt;
+  const int ch = m.nt == 1 ? GnCfg<1>::kCh : m.nt == 2 ? GnCfg<2>::kCh : m.nt == 4 ? GnCfg<4>::kCh : GnCfg<8>::kCh;
   m.nchunks = (int)((p.K + ch - 1) / ch);
   m.grid = std::min(m.ntiles, sm_count());
   m.arows = (int)std::min<int64_t>(p.M, 8 * m.nt);
@@ -390,7 +437,7 @@ bool dq_n_eligible(const DqMmParams &p) {
   if (!p.s_f16 || p.zp != nullptr || p.ydt != kFloat16) return false;
   if (p.cast_dt != 0 && p.cast_dt != kFloat16) return false;
   // N % 32: whole 16-byte packed row pieces per tile (TMA box and strides)
-  if (p.M < 1 || p.M > 32 || p.N < 32 || p.N % 32 != 0 || p.K < 16 || p.K % 8 != 0) return false;
+  if (p.M < 1 || p.M > GN_MAX_ROWS || p.N < 32 || p.N % 32 != 0 || p.K < 16 || p.K % 8 != 0) return false;
   if (p.N > (int64_t)1 << 30 || p.K > (int64_t)1 << 30) return false;
   switch (p.slayout) {
   case kScaleTensor:
@@ -408,7 +455,8 @@ int dq_n_launch(const DqMmParams &p, cudaStream_t st) {
   const GnPlan m = gn_plan(p);
   if (m.nt == 1) return launch_n<1>(p, m, st);
   if (m.nt == 2) return launch_n<2>(p, m, st);
-  return launch_n<4>(p, m, st);
+  if (m.nt == 4) return launch_n<4>(p, m, st);
+  return launch_n<8>(p, m, st);
 }
 
 } // namespace b2

@@ -756,18 +756,22 @@ static Plan make_plan(const DqMmParams &p) {
     return pl;
   }
   // Default decode choice for the int4 / fp16 family, by batch (measured on
-  // config 3): up to 8 rows the magic-number split-K kernel; 9 to 32 rows the
-  // narrow-tile kernel (no split-K; its dequantization is shared by all
-  // activation tiles) unless, at 9 to 16 rows, the columns need more tiles
-  // than SMs; 33 to 64 rows the exact kernel with two row passes.
+  // the config-3 projection shapes): up to 8 rows the magic-number split-K
+  // kernel; 9 to 16 rows the narrow-tile kernel (no split-K; its
+  // dequantization is shared by all activation tiles) when its 32-column
+  // tiles fit one wave and K is short (4096 x 4096: 8.2 us against 11.8 us),
+  // else the split-K kernel (4096 x 11008: 18.2 against 23.5 us; 11008 x
+  // 4096: 17.7 against 20.4 us); 17 to 64 rows the narrow-tile kernel (at 64
+  // rows 12.3 / 35.8 / 29.6 us against 31.5 / 47.2 / 49.5 us for the exact
+  // kernel with two row passes, kept for M <= 64 outside its reach).
   if (forced == kPathAuto && p.M > 8 && p.M <= 64) {
-    const bool narrow_fits = (p.N + 31) / 32 <= sm_count();
-    if (p.M <= 32 && dq_n_eligible(p) && (p.M > 16 || narrow_fits)) {
+    const bool narrow_fits = (p.N + 31) / 32 <= sm_count() && p.K <= 8192;
+    if (dq_n_eligible(p) && (p.M > 16 || narrow_fits)) {
       pl.kind = 6;
       pl.ws = 0;
       return pl;
     }
-    if (p.M > 32 && dq_x_eligible(p)) {
+    if (p.M > 16 && dq_x_eligible(p)) {
       pl.kind = 5;
       pl.ws = dq_x_workspace(p);
       return pl;

@@ -431,10 +431,11 @@ def test_exact_decode_repeated_calls_are_identical(b2, cuda, monkeypatch):
 # ---------------------------------------------------------------------------
 # Decode path on narrow column tiles (dq_gemv_n, forced with
 # ONNXL_B200_DQ_KERNEL=n): whole K per CTA, several tiles per CTA, chunks of
-# 256 / 128 / 64 rows, every scale layout it takes.
+# 256 / 128 / 64 rows, one to eight activation tiles, every scale layout it
+# takes.
 # ---------------------------------------------------------------------------
 
-@pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 17, 32])
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 17, 32, 33, 40, 63, 64])
 def test_narrow_decode_config3_batches(b2, cuda, monkeypatch, M):
     monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "n")
     y, ref = run_case(b2, M, 4096, 4096, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=80 + M)
@@ -444,7 +445,7 @@ def test_narrow_decode_config3_batches(b2, cuda, monkeypatch, M):
 @pytest.mark.parametrize("K,N", [(11008, 4096), (4096, 11008), (1000, 4128), (200, 96), (4096, 32)])
 def test_narrow_decode_shapes(b2, cuda, monkeypatch, K, N):
     monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "n")
-    for M in (1, 12, 30):
+    for M in (1, 12, 30, 50):
         y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=None, axis=1, seed=K + M + 1)
         assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
 
@@ -454,7 +455,7 @@ def test_narrow_decode_shapes(b2, cuda, monkeypatch, K, N):
 def test_narrow_decode_scale_layouts(b2, cuda, monkeypatch, wdt, block, axis):
     monkeypatch.setenv("ONNXL_B200_DQ_KERNEL", "n")
     K = 1024
-    for M in (2, 20):
+    for M in (2, 20, 64):
         y, ref = run_case(b2, M, K, 512, wdt, O.FLOAT16, O.FLOAT16, axis=axis, block=block, seed=M + 91)
         assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
 
