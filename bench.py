@@ -5,8 +5,12 @@ one decode step of a Llama-7B-shaped layer's weight-only int4 projections,
 q/k/v/o [4096,4096], gate/up [4096,11008], down [11008,4096], int4 blocked
 along K (block 128), FLOAT16 scales, no zero points, FLOAT16 activations
 [B,1,4096] (B = --batch, default 1).  Each projection is one fused
-DequantizeLinear -> MatMul call (b2_dequantize_matmul).  Inputs are seeded
-synthetic data (onnx-light's SplitMix64 generators, produced on the device).
+DequantizeLinear -> MatMul; projections that read the same activations run as
+one call (q/k/v, gate/up: b2_dequantize_matmul_group, one launch whose CTAs
+split all their weight tiles), so a step is 4 launches; the line's `per_node`
+entry times the same step with one call per ONNX node (7 launches of
+b2_dequantize_matmul).  Inputs are seeded synthetic data (onnx-light's
+SplitMix64 generators, produced on the device).
 
 Timing: four copies of the layer's weights (417 MB > 126 MB L2) are used in
 rotation, so every step streams its weights from HBM; each step is a CUDA
@@ -15,13 +19,13 @@ steps, K timed steps, barrier + synchronize around the timed region, max over
 ranks.  `value` = algorithmic bytes (packed weights + scales + activations in
 and out) per step / device time.  `e2e` repeats the step through the public
 Python API with host-resident activations: pinned H2D copy of the step input,
-seven API calls, D2H of the result, all inside the timed region (weights stay
+four API calls, D2H of the result, all inside the timed region (weights stay
 resident, as onnx-light initializers do).
 
 --gpus N (torchrun): the weights are column-sharded; each rank computes its
-output slice and the slices are all-gathered over NCCL after every
-projection; `value` counts the whole layer's bytes once per step (strong
-scaling).
+output slice and the decode kernel stores it into every rank's output over
+NVLink (peer stores; b2_allgather_cols after each projection above 16 rows);
+`value` counts the whole layer's bytes once per step (strong scaling).
 
 --impl reference: onnx-light's own CPU kernels (oracle/_ref, compiled from the
 reference sources) run the same chain on the host cores: DequantizeLinear then
@@ -30,6 +34,7 @@ MatMul for every projection.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import importlib.util
 import json
 import os
@@ -45,6 +50,10 @@ PKG_DIR = os.path.join(ROOT, "onnx-light_b200")
 PROJ = [("q", 4096, 4096, "x"), ("k", 4096, 4096, "x"), ("v", 4096, 4096, "x"),
         ("o", 4096, 4096, "q"), ("gate", 4096, 11008, "o"), ("up", 4096, 11008, "o"),
         ("down", 11008, 4096, "gate")]
+# The step's projections that read the same activations run as one call
+# (DequantizeMatMulGroup -> b2_dequantize_matmul_group: one launch whose CTAs
+# split all the members' weight tiles): q / k / v, o, gate / up, down.
+GROUPS = [(("q", "k", "v"), "x"), (("o",), "q"), (("gate", "up"), "o"), (("down",), "gate")]
 BLOCK = 128
 NCOPIES = 4
 INT4, FLOAT16, BF16 = 22, 10, 16
@@ -187,6 +196,7 @@ def gpu_arm(args):
     layers = [make_layer(b2, synth, c, rank, world, device) for c in range(NCOPIES)]
     x0 = synth.convert(synth.randn(2000, (B * 4096,), 0.0, 1.0, device=device), FLOAT16, (B, 4096))
     mm = b2.DequantizeMatMul()
+    gm = b2.DequantizeMatMulGroup()
     stream = torch.cuda.Stream(device)
 
     # Buffers: the full activation of every projection output and, sharded,
@@ -207,33 +217,53 @@ def gpu_arm(args):
             loc[name] = torch.empty((B, N // world), dtype=torch.float16, device=device)
 
     # Sharded decode (up to 16 rows): the fused kernel stores each rank's
-    # column slice into every rank's output itself (b2_dequantize_matmul_peer)
-    # and the next call waits for the previous one's slices; a step ends with
-    # a wait for its last projection.  Larger batches: each rank's slice, then
-    # b2_allgather_cols.
+    # column slice into every rank's output itself (b2_dequantize_matmul_peer,
+    # b2_dequantize_matmul_group_peer) and a call whose input is such an
+    # output first waits for every rank's previous call.  That chain also
+    # orders every overwrite of a peer buffer after its readers on all ranks
+    # (each buffer's next writer waits, directly or through its stream, for
+    # a call that follows those readers on every rank), so a step needs no
+    # wait of its own; a host read of an output waits first (peers.wait).
+    # Larger batches: each rank's slice, then b2_allgather_cols.
     fused = world > 1 and B <= 16
 
-    def run_step(layer):
-        for name, K, N, src in PROJ:
-            w, s = layer[name]
-            if world == 1:
-                mm(acts[src], w, s, None, axis=0, out=acts[name])
-            elif fused:
-                peers.matmul(name, acts[src], w, s)
+    def run_step(layer, per_node=False):
+        if per_node:
+            # one call per ONNX node (b2_dequantize_matmul, _peer)
+            for name, K, N, src in PROJ:
+                w, s = layer[name]
+                if world == 1:
+                    mm(acts[src], w, s, None, axis=0, out=acts[name])
+                elif fused:
+                    peers.matmul(name, acts[src], w, s)
+                else:
+                    mm(acts[src], w, s, None, axis=0, out=loc[name])
+                    peers.gather(name, loc[name])
+            return
+        for names, src in GROUPS:
+            ws = [layer[n][0] for n in names]
+            ss = [layer[n][1] for n in names]
+            if fused:
+                peers.matmul_group(names, acts[src], ws, ss)
+            elif world == 1:
+                if len(names) == 1:
+                    mm(acts[src], ws[0], ss[0], None, axis=0, out=acts[names[0]])
+                else:
+                    gm(acts[src], ws, ss, axis=0, outs=[acts[n] for n in names])
             else:
-                mm(acts[src], w, s, None, axis=0, out=loc[name])
-                peers.gather(name, loc[name])
-        if fused:
-            peers.wait()
+                gm(acts[src], ws, ss, axis=0, outs=[loc[n] for n in names])
+                for n in names:
+                    peers.gather(n, loc[n])
 
-    def run_steps(n, offset):
+    def run_steps(n, offset, per_node=False):
         for i in range(n):
-            run_step(layers[(offset + i) % NCOPIES])
+            run_step(layers[(offset + i) % NCOPIES], per_node)
 
     # Warm the library (plans, function attributes, workspace, NCCL
     # communicators) outside capture.
     with torch.cuda.stream(stream):
         run_steps(NCOPIES, 0)
+        run_steps(NCOPIES, 0, per_node=True)
     torch.cuda.synchronize()
 
     # The steps run as CUDA graphs of up to CHUNK steps each (the peer gathers
@@ -243,61 +273,72 @@ def gpu_arm(args):
     chunk = max(NCOPIES, min(256, args.steps) // NCOPIES * NCOPIES)
     graphs = {}
 
-    def graph_of(n):
-        if n not in graphs:
+    def graph_of(n, per_node=False):
+        if (n, per_node) not in graphs:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                run_steps(n, 0)
-            graphs[n] = g
-        return graphs[n]
+                run_steps(n, 0, per_node)
+            graphs[(n, per_node)] = g
+        return graphs[(n, per_node)]
 
-    def play(n):
+    def play(n, per_node=False):
         with torch.cuda.stream(stream):
             for _ in range(n // chunk):
-                graph_of(chunk).replay()
+                graph_of(chunk, per_node).replay()
             if n % chunk:
-                graph_of(n % chunk).replay()
+                graph_of(n % chunk, per_node).replay()
 
-    graph_of(chunk)
-    if args.steps % chunk:
-        graph_of(args.steps % chunk)
-    if args.warmup % chunk:
-        graph_of(args.warmup % chunk)
-    # Replay every graph of the timed region once before it (untimed extra
-    # warm-up): the first replay of a graph uploads it to the device, which a
-    # short timed region would otherwise pay inside its first step.
-    with torch.cuda.stream(stream):
-        for n in sorted({chunk, args.steps % chunk} - {0}):
-            graph_of(n).replay()
-    play(args.warmup)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    def timed(per_node, clk=None):
+        """Device ms per step of args.steps steps after args.warmup, max over ranks."""
+        graph_of(chunk, per_node)
+        if args.steps % chunk:
+            graph_of(args.steps % chunk, per_node)
+        if args.warmup % chunk:
+            graph_of(args.warmup % chunk, per_node)
+        # Replay every graph of the timed region once before it (untimed extra
+        # warm-up): the first replay of a graph uploads it to the device, which
+        # a short timed region would otherwise pay inside its first step.
+        with torch.cuda.stream(stream):
+            for n in sorted({chunk, args.steps % chunk} - {0}):
+                graph_of(n, per_node).replay()
+        play(args.warmup, per_node)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        ev0.record(stream)
-        play(args.steps)
-        ev1.record(stream)
-        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with (clk if clk is not None else contextlib.nullcontext()):
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            ev0.record(stream)
+            play(args.steps, per_node)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+        t_ms = ev0.elapsed_time(ev1) / args.steps
         if world > 1:
-            dist.barrier()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+            t = torch.tensor([t_ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_ms = float(t.item())
+        return t_ms
+
+    clk = ClockSampler(local)
+    ms = timed(False, clk)
     nbytes = step_bytes(B)
     value = nbytes / (ms * 1e-3) / 1e9
+    # the same step with one call per ONNX node (7 launches), for comparison
+    ms_node = timed(True)
     graphs.clear()
+    if fused:
+        with torch.cuda.stream(stream):
+            peers.wait()
     torch.cuda.synchronize()
 
-    # Roofline.  The fused kernel is the only kernel of a single-GPU step, so
-    # its average launch duration is the timed region / (7 K): achieved =
-    # algorithmic bytes of the step / step time.  Each projection is also
-    # timed alone: a graph of REPS launches rotating the weight copies.
+    # Roofline.  The fused decode kernel is the only kernel of a single-GPU
+    # step (4 launches): achieved = algorithmic bytes of the step / step time.
+    # Each projection is also timed alone: a graph of REPS launches rotating
+    # the weight copies.
     roof = None
     if rank == 0:
         per = []
@@ -348,6 +389,8 @@ def gpu_arm(args):
             for i in range(n):
                 acts["x"].copy_(x_host, non_blocking=True)
                 run_step(layers[i % NCOPIES])
+                if fused:
+                    peers.wait()  # every rank's slice of the result is in
                 y_host.copy_(acts["down"], non_blocking=True)
 
         ge = torch.cuda.CUDAGraph()
@@ -375,10 +418,13 @@ def gpu_arm(args):
         e2e = {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": B * 4096 * 2,
                "d2h_bytes_per_step": B * 4096 * 2,
-               "path": "DequantizeMatMul python API -> b2_dequantize_matmul, pinned H2D + "
-                       "7 calls + D2H per step, captured in CUDA graphs"
-                       + ((" (fused peer stores, b2_dequantize_matmul_peer, max over ranks)" if fused
-                           else " (+ b2_allgather_cols per call, max over ranks)") if world > 1 else "")}
+               "path": "DequantizeMatMulGroup / DequantizeMatMul python API -> "
+                       "b2_dequantize_matmul_group / b2_dequantize_matmul, pinned H2D + "
+                       "4 calls + D2H per step, captured in CUDA graphs"
+                       + ((" (fused peer stores, b2_dequantize_matmul_group_peer / _peer, a "
+                           "completion wait before the D2H, max over ranks)" if fused
+                           else " (+ b2_allgather_cols per projection, max over ranks)")
+                          if world > 1 else "")}
         del ge
 
     # Sharded: the gathered full output of a step against the unsharded
@@ -387,6 +433,8 @@ def gpu_arm(args):
     if world > 1:
         with torch.cuda.stream(stream):
             run_step(layers[0])
+            if fused:
+                peers.wait()
         torch.cuda.synchronize()
         full = make_layer(b2, synth, 0, 0, 1, device)
         ref_q = mm(x0, full["q"][0], full["q"][1], None, axis=0)
@@ -434,14 +482,21 @@ def gpu_arm(args):
             "parallelism": f"column-sharded over {world} GPUs" if world > 1 else "single GPU",
             "timing": {"l2_policy": f"{NCOPIES} weight copies in rotation "
                                     f"({NCOPIES * step_bytes(B) / 1e6:.0f} MB > 126 MB L2)",
-                       "launch": f"CUDA graphs of {chunk} steps"
+                       "launch": f"CUDA graphs of {chunk} steps; projections sharing an input "
+                                 "in one call (q/k/v, gate/up): 4 launches per step"
                                  + ((" with the column slices stored into every rank's output "
-                                     "by the decode kernel itself (b2_dequantize_matmul_peer) and "
-                                     "one completion wait per step" if fused else
+                                     "by the decode kernel itself (b2_dequantize_matmul_group_peer"
+                                     " / _peer)" if fused else
                                      " with a peer-store all-gather (b2_allgather_cols) per "
                                      "projection") if world > 1 else "")},
+            "per_node": {"value": round(nbytes / (ms_node * 1e-3) / 1e9, 1), "unit": "GB/s",
+                         "ms_per_step": round(ms_node, 5),
+                         "launches_per_step": 7 if (world == 1 or fused) else 14,
+                         "note": "the same step with one call per ONNX node "
+                                 "(DequantizeMatMul -> b2_dequantize_matmul"
+                                 + (", _peer" if fused else "") + ")"},
             "tflops": round(step_flops(B) / (ms * 1e-3) / 1e12, 3),
-            "gpu_launches": (7 if world == 1 else (8 if fused else 14)) * args.steps,
+            "gpu_launches": (4 if (world == 1 or fused) else 11) * args.steps,
             "gather_check": gather_check,
             "clocks": clocks,
             "roofline": roof,
@@ -516,11 +571,13 @@ def decode_kernel(B: int) -> str:
 
 def decode_config3(b2, layers, device, stream, B, cpu):
     """BASELINE config 3 at batch B (8, 32, 64): the same seven int4
-    projections and weight copies as the headline, activations [B, 4096].
-    The planner picks the decode kernel by batch (decode_kernel)."""
+    projections, grouping and weight copies as the headline, activations
+    [B, 4096].  The planner picks the decode kernel by batch (decode_kernel);
+    above 16 rows a group runs one call per member."""
     import torch
     from onnx_light_b200 import synth
     mm = b2.DequantizeMatMul()
+    gm = b2.DequantizeMatMulGroup()
     x = synth.convert(synth.randn(2000 + B, (B * 4096,), 0.0, 1.0, device=device), FLOAT16, (B, 4096))
     acts = {"x": x}
     for name, K, N, _ in PROJ:
@@ -530,9 +587,13 @@ def decode_config3(b2, layers, device, stream, B, cpu):
     def step():
         layer = layers[state["i"] % NCOPIES]
         state["i"] += 1
-        for name, K, N, src in PROJ:
-            w, sc = layer[name]
-            mm(acts[src], w, sc, None, axis=0, out=acts[name])
+        for names, src in GROUPS:
+            if len(names) == 1:
+                w, sc = layer[names[0]]
+                mm(acts[src], w, sc, None, axis=0, out=acts[names[0]])
+            else:
+                gm(acts[src], [layer[n][0] for n in names], [layer[n][1] for n in names],
+                   axis=0, outs=[acts[n] for n in names])
 
     with torch.cuda.stream(stream):
         for _ in range(NCOPIES):
@@ -557,7 +618,8 @@ def decode_config3(b2, layers, device, stream, B, cpu):
            "e2e": {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                    "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": hb,
                    "d2h_bytes_per_step": db,
-                   "path": "DequantizeMatMul python API, pinned H2D + 7 calls + D2H per step"}}
+                   "path": "DequantizeMatMulGroup / DequantizeMatMul python API, pinned H2D + "
+                           "4 calls + D2H per step"}}
     if cpu:
         out["cpu_baseline"] = cpu_baseline_sample(B)
     return out

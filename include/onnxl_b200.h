@@ -360,6 +360,40 @@ B2_API int b2_dequantize_matmul_peer(const b2_tensor *a, const b2_tensor *w, con
                                      const b2_tensor *y_local, const b2_peer_out *out,
                                      void *workspace, size_t *workspace_bytes, void *stream);
 
+/*
+ * Several DequantizeLinear -> MatMul nodes that read the same activations `a`
+ * (the q / k / v projections of an attention block, the gate / up
+ * projections of an MLP) in one call: y[i] = a @ DequantizeLinear(w[i],
+ * w_scale[i]) for i < count (1..4).  w, w_scale and y point to arrays of
+ * `count` tensors; each member obeys b2_dequantize_matmul's contract with the
+ * same a and axis, no zero point and no cast (replaces `count` calls of
+ * DequantizeLinear::operator() + MatMul::operator(),
+ * onnx_light/onnx_extensions/kernels/kernels/quantization/kernel_dequantizelinear.cc:504-712
+ * and kernels/math/kernel_matmul.cc:60-267, on one shared input).  Members
+ * with the same K, weight type and scale layout that the int4 / fp16 decode
+ * kernel takes (up to 16 rows) run as ONE launch whose CTAs split all the
+ * members' weight tiles; otherwise each member runs as b2_dequantize_matmul
+ * would, in order.  Results equal b2_dequantize_matmul's for each member
+ * within its tolerance.  Workspace as b2_dequantize_matmul (workspace NULL
+ * with workspace_bytes non-NULL: size query).
+ */
+B2_API int b2_dequantize_matmul_group(int32_t count, const b2_tensor *a, const b2_tensor *w,
+                                      const b2_tensor *w_scale, int64_t axis, b2_tensor *y,
+                                      void *workspace, size_t *workspace_bytes, void *stream);
+
+/* b2_dequantize_matmul_group with column-sharded outputs, each fused with its
+ * all-gather as in b2_dequantize_matmul_peer: y_local[i] describes member i's
+ * local slice and out[i] its full buffers (out is an array of `count`; every
+ * member has the same world and rank).  The call waits for its input and
+ * publishes its completion once, through out[0]'s flags and counters
+ * (out[0].wait_input).  Members must fit one launch of the decode kernel
+ * (same K, weight type and scale layout, int4 / fp16, up to 16 rows);
+ * otherwise B2_ERR_UNSUPPORTED. */
+B2_API int b2_dequantize_matmul_group_peer(int32_t count, const b2_tensor *a, const b2_tensor *w,
+                                           const b2_tensor *w_scale, int64_t axis,
+                                           const b2_tensor *y_local, const b2_peer_out *out,
+                                           void *workspace, size_t *workspace_bytes, void *stream);
+
 /* Waits (on the device, bounded) until every rank has finished the group's
  * last sharded call or all-gather, so that this rank's full buffers may be
  * read. */

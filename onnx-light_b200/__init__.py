@@ -10,5 +10,5 @@ from ._capi import version  # noqa: F401
 from .dispatch import (KernelDispatchTable, RegisterB200KernelFunctions,  # noqa: F401
                        default_table)
 from .kernels import (Attention, Attributes, DequantizeLinear, DequantizeMatMul,  # noqa: F401
-                      KVCache, MatMulInteger, QLinearMatMul, QTensor, Result, RMSNormalization,
+                      DequantizeMatMulGroup, KVCache, MatMulInteger, QLinearMatMul, QTensor, Result, RMSNormalization,
                       RotaryEmbedding, SwiGLU)

@@ -46,7 +46,8 @@ EXPORTS = ("b2_version", "b2_last_error", "b2_dequantize_linear", "b2_dequantize
            "b2_convert", "b2_kernel_status", "b2_selftest_bounded_wait", "b2_selftest_gemm_timeout",
            "b2_rms_normalization", "b2_rotary_embedding", "b2_swiglu", "b2_ipc_alloc",
            "b2_ipc_free", "b2_ipc_open", "b2_ipc_close", "b2_allgather_cols",
-           "b2_dequantize_matmul_peer", "b2_peer_wait")
+           "b2_dequantize_matmul_peer", "b2_peer_wait", "b2_dequantize_matmul_group",
+           "b2_dequantize_matmul_group_peer")
 
 
 class B2Tensor(C.Structure):
@@ -121,6 +122,9 @@ def lib() -> C.CDLL:
                 L.b2_dequantize_matmul_peer.argtypes = [T, T, T, T, C.c_int64, C.c_int32, T,
                                                         C.POINTER(B2PeerOut), P, SZ, P]
                 L.b2_peer_wait.argtypes = [C.POINTER(B2PeerOut), P]
+                L.b2_dequantize_matmul_group.argtypes = [C.c_int32, T, T, T, C.c_int64, T, P, SZ, P]
+                L.b2_dequantize_matmul_group_peer.argtypes = [C.c_int32, T, T, T, C.c_int64, T,
+                                                              C.POINTER(B2PeerOut), P, SZ, P]
                 L.b2_synth_fill.argtypes = [C.c_int32, C.c_uint64, C.c_int64, C.c_double,
                                             C.c_double, P, P]
                 L.b2_convert.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int64, P]
@@ -162,6 +166,21 @@ class Desc:
     @property
     def ref(self):
         return C.byref(self.t)
+
+
+class DescArray:
+    """A contiguous array of B2Tensor (one per member of a group call), kept
+    alive with its shape arrays for the duration of the call."""
+
+    __slots__ = ("arr", "_descs")
+
+    def __init__(self, descs):
+        self._descs = list(descs)
+        self.arr = (B2Tensor * len(self._descs))(*[d.t for d in self._descs])
+
+    @property
+    def ref(self):
+        return C.cast(self.arr, C.POINTER(B2Tensor))
 
 
 def stream_ptr(device=None) -> C.c_void_p:

@@ -52,6 +52,7 @@
 #include "tc_common.cuh"
 
 #include <cstdlib>
+#include <cstring>
 
 namespace b2 {
 
@@ -62,6 +63,10 @@ __device__ int g_gemv_mma_status;
 namespace {
 
 constexpr int kPeerMax = 8;
+#ifndef GM_GROUP_MAX
+#define GM_GROUP_MAX 4
+#endif
+constexpr int kGroupMax = GM_GROUP_MAX; // projections of one launch that share the activations
 constexpr int GM_TN = 256;                         // columns per tile (128 packed bytes / row)
 constexpr int GM_TK = 128;                         // weight rows per stage
 #ifndef GM_RING
@@ -69,6 +74,9 @@ constexpr int GM_TK = 128;                         // weight rows per stage
 #endif
 #ifndef GM_CTAS_PER_SM
 #define GM_CTAS_PER_SM 1
+#endif
+#ifndef GM_GRID_PER_SM
+#define GM_GRID_PER_SM GM_CTAS_PER_SM
 #endif
 constexpr int GM_STAGES = GM_RING;                 // ring depth
 constexpr int GM_QUADS = 4;                        // consumer warps per column half
@@ -83,11 +91,24 @@ constexpr uint32_t GM_ONES = 0x3c003c00u;          // (1.0, 1.0) in fp16
 #endif
 constexpr int kGroupsThreshold = GM_GROUPS_THRESHOLD; // stages per CTA up to which G = 1
 
+// The weight and scale tensor maps of each projection of the launch.
+struct GmMaps {
+  CUtensorMap w[kGroupMax];
+  CUtensorMap s[kGroupMax];
+};
+
 struct GmArgs {
-  __half *y;
   float *partials;
   uint32_t *counters;
-  int M, N, K;
+  int M, K;
+  // Projections of the launch (nprob >= 1; all read the same activations, K,
+  // weight type and scale layout): projection p owns the 256-column tiles
+  // tile_end[p - 1] .. tile_end[p] - 1 of the launch's tile numbering, has
+  // Np[p] columns and writes y[p] (row stride ldy[p]).
+  int nprob;
+  int tile_end[kGroupMax];
+  int Np[kGroupMax];
+  __half *y[kGroupMax];
   int ntiles, kunits, units, grid;
   int block;     // scale block along K (0: one scale row for all K)
   int srows;     // scale rows loaded per stage (0: per-tensor scale)
@@ -103,8 +124,8 @@ struct GmArgs {
   // call, then publishes its own completion (a generation number) in every
   // rank's flag array.
   int world, rank;
-  int64_t ldy, col_off;
-  __half *peer_y[kPeerMax];
+  int64_t ldy[kGroupMax], col_off[kGroupMax];
+  __half *peer_y[kGroupMax][kPeerMax];
   uint32_t *peer_flags[kPeerMax];
   uint32_t *pctr; // this rank's [0] CTA arrivals, [1] generation
   int wait_input; // wait for every rank's previous call before reading a
@@ -191,16 +212,25 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Two output values (columns col, col + 1 of row m) to y, or to every rank's
-// full buffer when the output is column-sharded.
-__device__ __forceinline__ void store_h2(const GmArgs &g, int64_t m, int64_t col, __half2 v) {
+// Projection of a launch tile, and its first tile.
+__device__ __forceinline__ int prob_of(const GmArgs &g, int tile) {
+  int p = 0;
+#pragma unroll
+  for (int i = 0; i < kGroupMax - 1; ++i) p += (i < g.nprob - 1 && tile >= g.tile_end[i]) ? 1 : 0;
+  return p;
+}
+__device__ __forceinline__ int prob_first_tile(const GmArgs &g, int p) { return p ? g.tile_end[p - 1] : 0; }
+// Two output values (columns col, col + 1 of row m of projection p) to its y,
+// or to every rank's full buffer when the output is column-sharded.
+__device__ __forceinline__ void store_h2(const GmArgs &g, int p, int64_t m, int64_t col, __half2 v) {
   if (g.world <= 1) {
-    *reinterpret_cast<__half2 *>(g.y + m * g.ldy + col) = v;
+    *reinterpret_cast<__half2 *>(g.y[p] + m * g.ldy[p] + col) = v;
     return;
   }
 #pragma unroll
   for (int r = 0; r < kPeerMax; ++r)
-    if (r < g.world) *reinterpret_cast<__half2 *>(g.peer_y[r] + m * g.ldy + g.col_off + col) = v;
+    if (r < g.world)
+      *reinterpret_cast<__half2 *>(g.peer_y[p][r] + m * g.ldy[p] + g.col_off[p] + col) = v;
 }
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
   uint32_t v;
@@ -274,8 +304,8 @@ __device__ __forceinline__ void k16_step(const uint8_t *wst, const uint8_t *ast,
 // block is at least a slab), fixed at compile time so the steps unroll.
 template <int NT, int G, int KS>
 __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
-    dq_gemv_mma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
-                const __grid_constant__ CUtensorMap map_s, const GmArgs g) {
+    dq_gemv_mma(const __grid_constant__ GmMaps maps, const __grid_constant__ CUtensorMap map_a,
+                const __grid_constant__ GmArgs g) {
   using L = GmSmem<NT>;
   extern __shared__ uint8_t dsm[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
@@ -309,11 +339,15 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     tc::fence_barrier_init();
   }
   if (warp == GM_CONSUMERS && lane == 0) {
-    tc::prefetch_tensormap(&map_w);
+    for (int q = 0; q < g.nprob; ++q) {
+      tc::prefetch_tensormap(&maps.w[q]);
+      if (g.srows) tc::prefetch_tensormap(&maps.s[q]);
+    }
     tc::prefetch_tensormap(&map_a);
-    if (g.srows) tc::prefetch_tensormap(&map_s);
-    for (int u = u0; u < u1; ++u)
-      prefetch_l2_2d(&map_w, (u / g.kunits) * (GM_TN / 2), (u % g.kunits) * GM_TK);
+    for (int u = u0; u < u1; ++u) {
+      const int tile = u / g.kunits, q = prob_of(g, tile);
+      prefetch_l2_2d(&maps.w[q], (tile - prob_first_tile(g, q)) * (GM_TN / 2), (u % g.kunits) * GM_TK);
+    }
   }
   __syncthreads();
   // The weights and scales are constants of the call, independent of the
@@ -326,11 +360,12 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
   auto load_weights = [&](int i) {
     const int s = i % GM_STAGES;
     const int u = u0 + i, tile = u / g.kunits, kb = u % g.kunits;
+    const int q = prob_of(g, tile), lt = tile - prob_first_tile(g, q);
     tc::mbar_expect_tx(&full[s], tx);
-    tc::tma_load_2d(sm + s * GM_W_BYTES, &map_w, &full[s], tile * (GM_TN / 2), kb * GM_TK);
+    tc::tma_load_2d(sm + s * GM_W_BYTES, &maps.w[q], &full[s], lt * (GM_TN / 2), kb * GM_TK);
     if (g.srows) {
       const int srow = g.block ? (kb * GM_TK) / g.block : 0;
-      tc::tma_load_2d(sm + L::kOffS + s * GM_SC_BYTES, &map_s, &full[s], tile * GM_TN, srow);
+      tc::tma_load_2d(sm + L::kOffS + s * GM_SC_BYTES, &maps.s[q], &full[s], lt * GM_TN, srow);
     }
   };
   if (warp == GM_CONSUMERS && lane == 0)
@@ -416,7 +451,6 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     // this group's stages of the segment: i = seg0 .. seg1-1 with i % G == grp
     for (int i = seg0 + ((grp - seg0 % G + G) % G); i < seg1; i += G) {
       const int s = i % GM_STAGES;
-      const int kb = (u0 + i) % g.kunits;
       if (ok && flags[0]) ok = false;
       if (ok && !tc::mbar_wait(&full[s], (i / GM_STAGES) & 1)) {
         atomicExch(&g_gemv_mma_status, tc::kTimeoutFull);
@@ -510,7 +544,8 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     const int uf = tile * g.kunits, ul = uf + g.kunits - 1;
     const int cf = g.aligned ? a_first : cta_of(uf, g.units, g.grid);
     const int cl = g.aligned ? a_first + a_nsl - 1 : cta_of(ul, g.units, g.grid);
-    const int n0 = tile * GM_TN;
+    const int pj = prob_of(g, tile);               // this tile's projection
+    const int n0 = (tile - prob_first_tile(g, pj)) * GM_TN, Nj = g.Np[pj];
     if (g.aligned && cf != cl) {
       // ---- tile-aligned split: the tile's first CTA (slice 0) merges ----
       float *part = g.partials + (size_t)(b * 2) * g.M * GM_TN;
@@ -595,9 +630,9 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
               }
             }
             const int m = e / (GM_TN / 4), col = (e % (GM_TN / 4)) * 4;
-            if (n0 + col >= g.N) continue; // ragged last tile; N % 4 == 0
-            store_h2(g, m, n0 + col, __floats2half2_rn(sum.x, sum.y));
-            store_h2(g, m, n0 + col + 2, __floats2half2_rn(sum.z, sum.w));
+            if (n0 + col >= Nj) continue; // ragged last tile; N % 4 == 0
+            store_h2(g, pj, m, n0 + col, __floats2half2_rn(sum.x, sum.y));
+            store_h2(g, pj, m, n0 + col + 2, __floats2half2_rn(sum.z, sum.w));
           }
         }
       }
@@ -607,12 +642,13 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
           const int col = n0 + wn * 128 + mt_col(mt, gq);
-          if (col >= g.N) continue; // ragged last tile (N % 256 != 0); N is even
+          if (col >= Nj) continue; // ragged last tile (N % 256 != 0); N is even
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             const int m = nt * 8 + 2 * t;
-            if (m < g.M) store_h2(g, m, col, __floats2half2_rn(acc[mt][nt][0], acc[mt][nt][2]));
-            if (m + 1 < g.M) store_h2(g, m + 1, col, __floats2half2_rn(acc[mt][nt][1], acc[mt][nt][3]));
+            if (m < g.M) store_h2(g, pj, m, col, __floats2half2_rn(acc[mt][nt][0], acc[mt][nt][2]));
+            if (m + 1 < g.M)
+              store_h2(g, pj, m + 1, col, __floats2half2_rn(acc[mt][nt][1], acc[mt][nt][3]));
           }
         }
       }
@@ -675,9 +711,9 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
             }
           }
           const int m = e / (GM_TN / 4), col = (e % (GM_TN / 4)) * 4;
-          if (n0 + col >= g.N) continue; // ragged last tile; N % 4 == 0
-          store_h2(g, m, n0 + col, __floats2half2_rn(sum.x, sum.y));
-          store_h2(g, m, n0 + col + 2, __floats2half2_rn(sum.z, sum.w));
+          if (n0 + col >= Nj) continue; // ragged last tile; N % 4 == 0
+          store_h2(g, pj, m, n0 + col, __floats2half2_rn(sum.x, sum.y));
+          store_h2(g, pj, m, n0 + col + 2, __floats2half2_rn(sum.z, sum.w));
         }
       }
     }
@@ -718,23 +754,37 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
 struct MmaPlan {
   int nt = 1, groups = 4, grid = 0, units = 0, kunits = 0, ntiles = 0, srows = 0, block = 0;
   int aligned = 0, cq = 0, cr = 0;
+  int tile_end[kGroupMax] = {};
   size_t ws = 0;
 };
 
-MmaPlan mma_plan(const DqMmParams &p) {
+// One plan for the projections ps[0 .. count-1] (same activations, M, K,
+// weight type and scale layout): their 256-column tiles numbered one after
+// the other.
+MmaPlan mma_plan(const DqMmParams *ps, int count) {
+  const DqMmParams &p = ps[0];
   MmaPlan m;
   m.nt = p.M <= 8 ? 1 : 2;
-  m.ntiles = (int)((p.N + GM_TN - 1) / GM_TN); // the last tile may be ragged (TMA zero-fills)
+  m.ntiles = 0;
+  for (int i = 0; i < count; ++i) {
+    m.ntiles += (int)((ps[i].N + GM_TN - 1) / GM_TN); // a last tile may be ragged (TMA zero-fills)
+    m.tile_end[i] = m.ntiles;
+  }
   m.kunits = (int)((p.K + GM_TK - 1) / GM_TK);
   m.units = m.ntiles * m.kunits;
-  m.grid = std::min(m.units, sm_count() * GM_CTAS_PER_SM);
+  m.grid = std::min(m.units, sm_count() * GM_GRID_PER_SM);
   // Up to one tile per CTA: split each tile's K range among whole CTAs (a
   // CTA never straddles two tiles, and each tile's first CTA merges), which
-  // takes one merge per tile off the critical path of stream-K.
+  // takes one merge per tile off the critical path of stream-K.  Kept only
+  // while it balances the work: whole CTAs per tile leave some CTAs with
+  // ceil(kunits / cq) units against ceil(units / grid) for stream-K
+  // (4096 x 22016 in one launch: 32 against 19 units).
   m.aligned = m.ntiles <= m.grid && getenv("ONNXL_B200_GEMV_STREAMK") == nullptr;
   if (m.aligned) {
     m.cq = m.grid / m.ntiles;
     m.cr = m.grid % m.ntiles;
+    const int amax = (m.kunits + m.cq - 1) / m.cq, smax = (m.units + m.grid - 1) / m.grid;
+    if (4 * amax > 5 * smax) m.aligned = 0;
   }
   // Stages per CTA below about 2 per stage group leave groups idle: put all
   // warps on every stage instead.
@@ -761,15 +811,31 @@ MmaPlan mma_plan(const DqMmParams &p) {
 }
 
 template <int NT, int G, int KS>
-int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStream_t st) {
-  CUtensorMap map_w, map_a, map_s;
-  {
-    const uint64_t dims[2] = {(uint64_t)p.N / 2, (uint64_t)p.K};
-    const uint64_t strides[1] = {(uint64_t)p.N / 2};
-    const uint32_t box[2] = {GM_TN / 2, GM_TK};
-    int rc = make_tensor_map(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p.w, dims, strides, box,
-                             CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
+int launch_mma(const DqMmParams *ps, int count, const MmaPlan &m, void *workspace, cudaStream_t st) {
+  const DqMmParams &p = ps[0];
+  GmMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  CUtensorMap map_a;
+  for (int i = 0; i < count; ++i) {
+    const DqMmParams &q = ps[i];
+    {
+      const uint64_t dims[2] = {(uint64_t)q.N / 2, (uint64_t)q.K};
+      const uint64_t strides[1] = {(uint64_t)q.N / 2};
+      const uint32_t box[2] = {GM_TN / 2, GM_TK};
+      int rc = make_tensor_map(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q.w, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    }
+    maps.s[i] = maps.w[i];
+    if (m.srows) {
+      const uint64_t rows = q.slayout == kScaleAxis1 ? 1 : (uint64_t)q.s_alen;
+      const uint64_t dims[2] = {(uint64_t)q.N, rows};
+      const uint64_t strides[1] = {(uint64_t)q.N * 2};
+      const uint32_t box[2] = {GM_TN, (uint32_t)m.srows};
+      int rc = make_tensor_map(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.scale, dims, strides,
+                               box, CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+    }
   }
   {
     const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
@@ -779,23 +845,24 @@ int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStrea
                              CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  map_s = map_w;
-  if (m.srows) {
-    const uint64_t rows = p.slayout == kScaleAxis1 ? 1 : (uint64_t)p.s_alen;
-    const uint64_t dims[2] = {(uint64_t)p.N, rows};
-    const uint64_t strides[1] = {(uint64_t)p.N * 2};
-    const uint32_t box[2] = {GM_TN, (uint32_t)m.srows};
-    int rc = make_tensor_map(&map_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.scale, dims, strides,
-                             box, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-  }
   GmArgs a{};
-  a.y = static_cast<__half *>(p.y);
   a.counters = static_cast<uint32_t *>(workspace);
   a.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kCounterBytes);
   a.M = (int)p.M;
-  a.N = (int)p.N;
   a.K = (int)p.K;
+  a.nprob = count;
+  a.world = p.world > 1 ? p.world : 1;
+  a.rank = p.rank;
+  for (int i = 0; i < count; ++i) {
+    const DqMmParams &q = ps[i];
+    a.tile_end[i] = m.tile_end[i];
+    a.Np[i] = (int)q.N;
+    a.y[i] = static_cast<__half *>(q.y);
+    a.ldy[i] = p.world > 1 ? q.n_full : q.N;
+    a.col_off[i] = p.world > 1 ? q.col_off : 0;
+    for (int r = 0; r < kPeerMax; ++r)
+      a.peer_y[i][r] = r < a.world ? static_cast<__half *>(q.peer_full[r]) : nullptr;
+  }
   a.ntiles = m.ntiles;
   a.kunits = m.kunits;
   a.units = m.units;
@@ -804,14 +871,7 @@ int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStrea
   a.srows = m.srows;
   a.is_signed = p.wdt == kInt4;
   a.scalar_scale = reinterpret_cast<const uint16_t *>(p.scale);
-  a.world = p.world > 1 ? p.world : 1;
-  a.rank = p.rank;
-  a.ldy = p.world > 1 ? p.n_full : p.N;
-  a.col_off = p.world > 1 ? p.col_off : 0;
-  for (int r = 0; r < kPeerMax; ++r) {
-    a.peer_y[r] = r < a.world ? static_cast<__half *>(p.peer_full[r]) : nullptr;
-    a.peer_flags[r] = r < a.world ? p.peer_flags[r] : nullptr;
-  }
+  for (int r = 0; r < kPeerMax; ++r) a.peer_flags[r] = r < a.world ? p.peer_flags[r] : nullptr;
   a.pctr = p.pctr;
   a.wait_input = p.wait_input;
   a.aligned = m.aligned;
@@ -831,7 +891,7 @@ int launch_mma(const DqMmParams &p, const MmaPlan &m, void *workspace, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B2_CUDA(cudaLaunchKernelEx(&cfg, kern, map_w, map_a, map_s, a));
+  B2_CUDA(cudaLaunchKernelEx(&cfg, kern, maps, map_a, a));
   return B2_OK;
 }
 
@@ -867,24 +927,46 @@ bool dq_mma_aligned(const DqMmParams &p) {
          (p.slayout == kScaleTensor || al(p.scale, 16));
 }
 
-size_t dq_mma_workspace(const DqMmParams &p) { return mma_plan(p).ws; }
+size_t dq_mma_workspace(const DqMmParams &p) { return mma_plan(&p, 1).ws; }
 
-int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
-  const MmaPlan m = mma_plan(p);
+bool dq_mma_group_eligible(const DqMmParams *ps, int count) {
+  if (count < 1 || count > kGroupMax) return false;
+  int64_t ntiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const DqMmParams &q = ps[i];
+    if (!dq_mma_eligible(q) || !dq_mma_aligned(q)) return false;
+    if (q.a != ps[0].a || q.M != ps[0].M || q.K != ps[0].K || q.wdt != ps[0].wdt ||
+        q.slayout != ps[0].slayout || q.block != ps[0].block || q.s_alen != ps[0].s_alen)
+      return false;
+    ntiles += (q.N + GM_TN - 1) / GM_TN;
+  }
+  if (ntiles > (int64_t)kMaxCounters) return false;
+  const int64_t units = ntiles * ((ps[0].K + GM_TK - 1) / GM_TK);
+  return units * (int64_t)(sm_count() + 1) < ((int64_t)1 << 31);
+}
+
+size_t dq_mma_group_workspace(const DqMmParams *ps, int count) { return mma_plan(ps, count).ws; }
+
+int dq_mma_launch_group(const DqMmParams *ps, int count, void *workspace, cudaStream_t st) {
+  const MmaPlan m = mma_plan(ps, count);
   if (m.ws && workspace == nullptr) B2_FAIL(B2_ERR_WORKSPACE, "workspace of %zu bytes required", m.ws);
   if (m.groups == 1) // 32-row slabs: scale blocks are 32 rows or more
-    return m.nt == 1 ? launch_mma<1, 1, 2>(p, m, workspace, st)
-                     : launch_mma<2, 1, 2>(p, m, workspace, st);
+    return m.nt == 1 ? launch_mma<1, 1, 2>(ps, count, m, workspace, st)
+                     : launch_mma<2, 1, 2>(ps, count, m, workspace, st);
   // 128-row slabs: k16 steps per scale block
   const int ks = (m.block == 0 || m.block >= GM_TK) ? 8 : m.block / 16;
   if (m.nt == 1) {
-    if (ks == 2) return launch_mma<1, 4, 2>(p, m, workspace, st);
-    if (ks == 4) return launch_mma<1, 4, 4>(p, m, workspace, st);
-    return launch_mma<1, 4, 8>(p, m, workspace, st);
+    if (ks == 2) return launch_mma<1, 4, 2>(ps, count, m, workspace, st);
+    if (ks == 4) return launch_mma<1, 4, 4>(ps, count, m, workspace, st);
+    return launch_mma<1, 4, 8>(ps, count, m, workspace, st);
   }
-  if (ks == 2) return launch_mma<2, 4, 2>(p, m, workspace, st);
-  if (ks == 4) return launch_mma<2, 4, 4>(p, m, workspace, st);
-  return launch_mma<2, 4, 8>(p, m, workspace, st);
+  if (ks == 2) return launch_mma<2, 4, 2>(ps, count, m, workspace, st);
+  if (ks == 4) return launch_mma<2, 4, 4>(ps, count, m, workspace, st);
+  return launch_mma<2, 4, 8>(ps, count, m, workspace, st);
+}
+
+int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
+  return dq_mma_launch_group(&p, 1, workspace, st);
 }
 
 } // namespace b2

@@ -947,35 +947,17 @@ extern "C" int b2_dequantize_matmul(const b2_tensor *a, const b2_tensor *w,
   return launch_simt<__nv_bfloat16>(p, pl, st);
 }
 
-extern "C" int b2_dequantize_matmul_peer(const b2_tensor *a, const b2_tensor *w,
-                                         const b2_tensor *w_scale, const b2_tensor *w_zero_point,
-                                         int64_t axis, int32_t cast_dtype, const b2_tensor *y_local,
-                                         const b2_peer_out *out, void *workspace,
-                                         size_t *workspace_bytes, void *stream) {
-  if (!out) B2_FAIL(B2_ERR_INVALID_ARGUMENT, "b2_dequantize_matmul_peer: null peer output");
-  DqMmParams p{};
-  int rc = dq_mm_validate(a, w, w_scale, w_zero_point, axis, cast_dtype, y_local, p);
-  if (rc) return rc;
-  B2_ENFORCE(out->world >= 2 && out->world <= 8, "b2_dequantize_matmul_peer: world must be 2..8");
-  B2_ENFORCE(out->rank >= 0 && out->rank < out->world, "b2_dequantize_matmul_peer: rank out of range");
+// The sharded-output fields of p from one b2_peer_out (after p's validation).
+static int peer_fill(const b2_peer_out *out, DqMmParams &p, const char *fn) {
+  if (!out) B2_FAIL(B2_ERR_INVALID_ARGUMENT, "%s: null peer output", fn);
+  B2_ENFORCE(out->world >= 2 && out->world <= 8, "%s: world must be 2..8", fn);
+  B2_ENFORCE(out->rank >= 0 && out->rank < out->world, "%s: rank out of range", fn);
   B2_ENFORCE(out->n_full == p.N * out->world,
-             "b2_dequantize_matmul_peer: n_full must be world x the local slice's columns");
-  B2_ENFORCE(out->counters != nullptr, "b2_dequantize_matmul_peer: null counters");
+             "%s: n_full must be world x the local slice's columns", fn);
+  B2_ENFORCE(out->counters != nullptr, "%s: null counters", fn);
   for (int r = 0; r < out->world; ++r)
     B2_ENFORCE(out->full[r] && out->flags[r] && reinterpret_cast<uintptr_t>(out->full[r]) % 16 == 0,
-               "b2_dequantize_matmul_peer: peer buffers must be non-null and 16-byte aligned");
-  // the fused peer stores live in the register-MMA decode kernel only
-  if (forced_path() != kPathAuto || !dq_mma_eligible(p))
-    B2_FAIL(B2_ERR_UNSUPPORTED,
-            "b2_dequantize_matmul_peer: only the int4 / fp16 decode kernel (M <= 16) stores to peers");
-  const size_t need = dq_mma_workspace(p);
-  rc = workspace_check(workspace, workspace_bytes, need);
-  if (rc < 0) return rc;
-  if (rc == 1) return B2_OK; // size query
-  p.a = a->data;
-  p.w = static_cast<const uint8_t *>(w->data);
-  p.scale = static_cast<const uint8_t *>(w_scale->data);
-  p.zp = nullptr;
+               "%s: peer buffers must be non-null and 16-byte aligned", fn);
   p.y = out->full[out->rank];
   p.world = out->world;
   p.rank = out->rank;
@@ -988,10 +970,118 @@ extern "C" int b2_dequantize_matmul_peer(const b2_tensor *a, const b2_tensor *w,
   p.pctr = out->counters;
   p.wait_input = out->wait_input;
   if (!dq_mma_aligned(p) || (p.col_off * 2) % 4 != 0 || (p.n_full * 2) % 4 != 0)
-    B2_FAIL(B2_ERR_UNSUPPORTED, "b2_dequantize_matmul_peer: tensors must be 16-byte aligned");
+    B2_FAIL(B2_ERR_UNSUPPORTED, "%s: tensors must be 16-byte aligned", fn);
   if (p.M == 0 || p.N == 0 || p.K == 0)
-    B2_FAIL(B2_ERR_UNSUPPORTED, "b2_dequantize_matmul_peer: empty shapes are not sharded");
+    B2_FAIL(B2_ERR_UNSUPPORTED, "%s: empty shapes are not sharded", fn);
+  return B2_OK;
+}
+
+extern "C" int b2_dequantize_matmul_peer(const b2_tensor *a, const b2_tensor *w,
+                                         const b2_tensor *w_scale, const b2_tensor *w_zero_point,
+                                         int64_t axis, int32_t cast_dtype, const b2_tensor *y_local,
+                                         const b2_peer_out *out, void *workspace,
+                                         size_t *workspace_bytes, void *stream) {
+  if (!out) B2_FAIL(B2_ERR_INVALID_ARGUMENT, "b2_dequantize_matmul_peer: null peer output");
+  DqMmParams p{};
+  int rc = dq_mm_validate(a, w, w_scale, w_zero_point, axis, cast_dtype, y_local, p);
+  if (rc) return rc;
+  // the fused peer stores live in the register-MMA decode kernel only
+  if (forced_path() != kPathAuto || !dq_mma_eligible(p))
+    B2_FAIL(B2_ERR_UNSUPPORTED,
+            "b2_dequantize_matmul_peer: only the int4 / fp16 decode kernel (M <= 16) stores to peers");
+  p.a = a->data;
+  p.w = static_cast<const uint8_t *>(w->data);
+  p.scale = static_cast<const uint8_t *>(w_scale->data);
+  p.zp = nullptr;
+  rc = peer_fill(out, p, "b2_dequantize_matmul_peer");
+  if (rc) return rc;
+  const size_t need = dq_mma_workspace(p);
+  rc = workspace_check(workspace, workspace_bytes, need);
+  if (rc < 0) return rc;
+  if (rc == 1) return B2_OK; // size query
   return dq_mma_launch(p, workspace, static_cast<cudaStream_t>(stream));
+}
+
+// Validated parameters of the members of a group call (same a, axis, no
+// zero point, no cast).
+static int group_params(const char *fn, int32_t count, const b2_tensor *a, const b2_tensor *w,
+                        const b2_tensor *w_scale, int64_t axis, const b2_tensor *y, DqMmParams *ps) {
+  B2_ENFORCE(count >= 1 && count <= 4, "%s: count must be 1..4", fn);
+  B2_ENFORCE(a && w && w_scale && y, "%s: null tensor array", fn);
+  for (int i = 0; i < count; ++i) {
+    ps[i] = DqMmParams{};
+    int rc = dq_mm_validate(a, &w[i], &w_scale[i], nullptr, axis, 0, &y[i], ps[i]);
+    if (rc) return rc;
+    ps[i].a = a->data;
+    ps[i].w = static_cast<const uint8_t *>(w[i].data);
+    ps[i].scale = static_cast<const uint8_t *>(w_scale[i].data);
+    ps[i].zp = nullptr;
+    ps[i].y = y[i].data;
+  }
+  return B2_OK;
+}
+
+extern "C" int b2_dequantize_matmul_group(int32_t count, const b2_tensor *a, const b2_tensor *w,
+                                          const b2_tensor *w_scale, int64_t axis, b2_tensor *y,
+                                          void *workspace, size_t *workspace_bytes, void *stream) {
+  DqMmParams ps[4];
+  int rc = group_params("b2_dequantize_matmul_group", count, a, w, w_scale, axis, y, ps);
+  if (rc) return rc;
+  bool nonempty = true;
+  for (int i = 0; i < count; ++i) nonempty = nonempty && ps[i].M > 0 && ps[i].N > 0 && ps[i].K > 0;
+  if (forced_path() == kPathAuto && nonempty && dq_mma_group_eligible(ps, count)) {
+    rc = workspace_check(workspace, workspace_bytes, dq_mma_group_workspace(ps, count));
+    if (rc < 0) return rc;
+    if (rc == 1) return B2_OK; // size query
+    return dq_mma_launch_group(ps, count, workspace, static_cast<cudaStream_t>(stream));
+  }
+  // Not one launch: each member as its own call, in order, on one workspace
+  // of the largest member's size.
+  size_t need = 0;
+  for (int i = 0; i < count; ++i) need = std::max(need, make_plan(ps[i]).ws);
+  rc = workspace_check(workspace, workspace_bytes, need);
+  if (rc < 0) return rc;
+  if (rc == 1) return B2_OK; // size query
+  for (int i = 0; i < count; ++i) {
+    size_t wsb = workspace_bytes ? *workspace_bytes : 0;
+    rc = b2_dequantize_matmul(a, &w[i], &w_scale[i], nullptr, axis, 0, &y[i], workspace,
+                              workspace ? &wsb : nullptr, stream);
+    if (rc) return rc;
+  }
+  return B2_OK;
+}
+
+extern "C" int b2_dequantize_matmul_group_peer(int32_t count, const b2_tensor *a, const b2_tensor *w,
+                                               const b2_tensor *w_scale, int64_t axis,
+                                               const b2_tensor *y_local, const b2_peer_out *out,
+                                               void *workspace, size_t *workspace_bytes,
+                                               void *stream) {
+  const char *fn = "b2_dequantize_matmul_group_peer";
+  if (!out) B2_FAIL(B2_ERR_INVALID_ARGUMENT, "%s: null peer outputs", fn);
+  DqMmParams ps[4];
+  int rc = group_params(fn, count, a, w, w_scale, axis, y_local, ps);
+  if (rc) return rc;
+  for (int i = 0; i < count; ++i) {
+    rc = peer_fill(&out[i], ps[i], fn);
+    if (rc) return rc;
+    B2_ENFORCE(out[i].world == out[0].world && out[i].rank == out[0].rank,
+               "%s: every member must have the same world and rank", fn);
+  }
+  // the call's completion is published once, through the first member's
+  // flags and counters
+  for (int i = 1; i < count; ++i) {
+    for (int r = 0; r < out[0].world; ++r) ps[i].peer_flags[r] = ps[0].peer_flags[r];
+    ps[i].pctr = ps[0].pctr;
+    ps[i].wait_input = ps[0].wait_input;
+  }
+  if (forced_path() != kPathAuto || !dq_mma_group_eligible(ps, count))
+    B2_FAIL(B2_ERR_UNSUPPORTED,
+            "%s: the members must share K, the weight type and the scale layout and fit the int4 / "
+            "fp16 decode kernel (M <= 16)", fn);
+  rc = workspace_check(workspace, workspace_bytes, dq_mma_group_workspace(ps, count));
+  if (rc < 0) return rc;
+  if (rc == 1) return B2_OK; // size query
+  return dq_mma_launch_group(ps, count, workspace, static_cast<cudaStream_t>(stream));
 }
 
 // Self-test of the tensor-core GEMM's time-out path (see the header): the

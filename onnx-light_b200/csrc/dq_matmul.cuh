@@ -60,6 +60,11 @@ bool dq_mma_eligible(const DqMmParams &p); // shape/type constraints
 bool dq_mma_aligned(const DqMmParams &p);  // pointer alignment TMA needs
 size_t dq_mma_workspace(const DqMmParams &p);
 int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
+// Several projections of the same activations in one launch (1..4 of them,
+// same M, K, weight type and scale layout, each eligible and aligned).
+bool dq_mma_group_eligible(const DqMmParams *ps, int count);
+size_t dq_mma_group_workspace(const DqMmParams *ps, int count);
+int dq_mma_launch_group(const DqMmParams *ps, int count, void *workspace, cudaStream_t stream);
 
 // Decode path with the reference's exact fp16 weights (dq_gemv_x.cu): M <= 64,
 // INT4/UINT4 weights, FLOAT16 scales, activations and output.

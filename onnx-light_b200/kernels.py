@@ -148,6 +148,34 @@ class DequantizeMatMul:
         return out
 
 
+class DequantizeMatMulGroup:
+    """Several DequantizeLinear -> MatMul nodes on the same activations (q / k / v,
+    gate / up) as one call: ``[a @ DequantizeLinear(w_i, s_i) for i]``.
+
+    Each member is the two-node pattern of DequantizeMatMul (kernel_dequantizelinear.cc
+    :522-693 then kernel_matmul.cc:181-223) with the same ``a`` and ``axis``, no zero
+    point and no cast; members with one K, weight type and scale layout that the
+    int4 / fp16 decode kernel takes run as one launch (b2_dequantize_matmul_group).
+    """
+
+    name = "onnx_kernels:GPU:b200:DequantizeMatMulGroup"
+
+    def __call__(self, a: torch.Tensor, ws, scales, axis: int = 0, outs=None):
+        if len(ws) != len(scales) or not 1 <= len(ws) <= 4:
+            raise ValueError("DequantizeMatMulGroup: 1 to 4 weights, one scale each")
+        if outs is None:
+            outs = [torch.empty(tuple(a.shape[:-1]) + (int(w.shape[-1]),), dtype=a.dtype,
+                                device=a.device) for w in ws]
+        ad = _desc(a)
+        wd = capi.DescArray([_desc(w) for w in ws])
+        sd = capi.DescArray([_desc(s) for s in scales])
+        yd = capi.DescArray([_desc(y) for y in outs])
+        _call_with_workspace(lib().b2_dequantize_matmul_group,
+                             (len(ws), ad.ref, wd.ref, sd.ref, int(axis), yd.ref),
+                             (stream_ptr(a.device),), a.device)
+        return outs
+
+
 def _matmul_shape(a_shape, b_shape):
     a2 = list(a_shape) if len(a_shape) > 1 else [1, a_shape[0]]
     b2 = list(b_shape) if len(b_shape) > 1 else [b_shape[0], 1]

@@ -220,6 +220,35 @@ class PeerGroup:
                                       C.byref(po)), (self._capi.stream_ptr(a.device),), a.device)
         return full
 
+    def matmul_group(self, names, a: torch.Tensor, ws, scales, axis: int = 0):
+        """matmul for projections that read the same `a` (q / k / v, gate /
+        up), as one launch (b2_dequantize_matmul_group_peer); returns this
+        rank's full buffers."""
+        from . import kernels
+        names = list(names)
+        if len(names) == 1:
+            return [self.matmul(names[0], a, ws[0], scales[0], axis)]
+        lead = tuple(a.shape[:-1])
+        pos = (self._capi.B2PeerOut * len(names))()
+        for i, name in enumerate(names):
+            pos[i] = self._peer_out(name)
+        src = next((n for n, b in self.bufs.items() if b[0].data_ptr() == a.data_ptr()), None)
+        pos[0].wait_input = 1 if src in self._dirty else 0
+        if pos[0].wait_input:
+            self._dirty.clear()
+        self._dirty.update(names)
+        ad = self._capi.Desc(a.data_ptr(), self._capi.TORCH_TO_ONNX[a.dtype], tuple(a.shape))
+        wd = self._capi.DescArray([kernels._desc(w) for w in ws])
+        sd = self._capi.DescArray([kernels._desc(sc) for sc in scales])
+        yd = self._capi.DescArray([self._capi.Desc(0, self._capi.TORCH_TO_ONNX[a.dtype],
+                                                   lead + (self.bufs[n][2] // self.world,))
+                                   for n in names])
+        kernels._call_with_workspace(self.lib.b2_dequantize_matmul_group_peer,
+                                     (len(names), ad.ref, wd.ref, sd.ref, int(axis), yd.ref,
+                                      C.cast(pos, C.POINTER(self._capi.B2PeerOut))),
+                                     (self._capi.stream_ptr(a.device),), a.device)
+        return [self.bufs[n][0] for n in names]
+
     def wait(self, device=None):
         """Makes this rank's stream wait until every rank finished the group's
         last sharded call or gather (so the full buffers may be read)."""

@@ -99,6 +99,45 @@ def _worker(rank, world, port, mode, result):
             ok &= rel_l2(got1, O.f16_bits_to_f32(y1)) <= 1e-3
             ok &= rel_l2(got2, O.f16_bits_to_f32(y2)) <= 1e-3
         ok &= lib.b2_kernel_status(1) == 0
+    elif mode == "fused_group":
+        # b2_dequantize_matmul_group_peer: two projections of the same input in
+        # one launch, each stored into both ranks' outputs, then a sharded call
+        # on the first one's output; three steps back to back with no wait of
+        # their own (the chain orders every overwrite), checked after a wait.
+        import numpy as np
+        import oracle as O
+        from util import random_q, scale_raw, to_dev, rel_l2
+        K, N = 1024, 768
+
+        def sliced(seed, kk, nn):
+            wq = random_q(seed, (kk, nn), O.INT4)
+            sc = scale_raw(O.rand_uniform(seed + 1, ((kk // 128) * nn,), 0.002, 0.02),
+                           O.FLOAT16).reshape(kk // 128, nn)
+            nl = nn // world
+            b = np.asarray(wq, np.uint8).reshape(kk, nn // 2)
+            wl = np.ascontiguousarray(b[:, rank * nl // 2:(rank + 1) * nl // 2])
+            sl = np.ascontiguousarray(sc[:, rank * nl:(rank + 1) * nl])
+            deq = O.dequantize_linear(wq, O.INT4, (kk, nn), sc.ravel(), O.FLOAT16, (kk // 128, nn),
+                                      None, None, 0)
+            return (b2.QTensor(to_dev(wl), O.INT4, (kk, nl)), to_dev(sl, torch.float16), deq)
+
+        wa, wb, w2 = sliced(81, K, N), sliced(83, K, N), sliced(85, N, K)
+        fa = peers.buffer("ya", (2, N), torch.float16)
+        fb = peers.buffer("yb", (2, N), torch.float16)
+        f2 = peers.buffer("y2", (2, K), torch.float16)
+        for step in range(3):
+            x = O.f32_to_f16_bits(O.randn(90 + step, (2, K)))
+            tx = to_dev(x).view(torch.float16).reshape(2, K)
+            peers.matmul_group(["ya", "yb"], tx, [wa[0], wb[0]], [wa[1], wb[1]])
+            peers.matmul("y2", fa, w2[0], w2[1])
+        peers.wait()
+        torch.cuda.synchronize()
+        ya = O.matmul(x, wa[2], O.FLOAT16)
+        yb = O.matmul(x, wb[2], O.FLOAT16)
+        y2 = O.matmul(ya, w2[2], O.FLOAT16)
+        for got, want in ((fa, ya), (fb, yb), (f2, y2)):
+            ok &= rel_l2(got.float().cpu().numpy(), O.f16_bits_to_f32(want)) <= 1e-3
+        ok &= lib.b2_kernel_status(1) == 0
     else:  # rank 1 never issues its gather: rank 0's wait runs out (5 s) and reports
         if rank == 0:
             peers.gather("y", local)
@@ -110,7 +149,7 @@ def _worker(rank, world, port, mode, result):
     result[rank] = bool(ok)
 
 
-@pytest.mark.parametrize("mode", ["gather", "fused_matmul", "absent_peer_times_out"])
+@pytest.mark.parametrize("mode", ["gather", "fused_matmul", "fused_group", "absent_peer_times_out"])
 def test_allgather_cols_two_gpus(cuda, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")

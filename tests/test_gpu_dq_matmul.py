@@ -550,3 +550,66 @@ def test_mma_decode_stream_k_partition(b2, cuda, monkeypatch, K, N):
     for M in (1, 9):
         y, ref = run_case(b2, M, K, N, O.INT4, O.FLOAT16, O.FLOAT16, block=128, seed=K + N + M)
         assert rel_l2(y, ref) <= TOL[O.FLOAT16], (M, rel_l2(y, ref))
+
+
+# ---------------------------------------------------------------------------
+# Projections that share their activations in one call (b2_dequantize_matmul_group):
+# the members' weight tiles split among the CTAs of one decode launch, or one
+# call per member when they do not fit it.
+# ---------------------------------------------------------------------------
+
+def group_case(b2, M, K, Ns, block, seed, axis=0):
+    """Runs DequantizeMatMulGroup on len(Ns) int4 members; returns (gpu, oracle) lists."""
+    a32 = O.randn(seed, (M, K))
+    a_raw = O.f32_to_f16_bits(a32)
+    ta = to_dev(a_raw).view(torch.float16).reshape(M, K)
+    ws, ss, refs = [], [], []
+    for j, N in enumerate(Ns):
+        w = finite_q(seed + 10 * j + 1, (K, N), O.INT4)
+        s_shape = (K // block, N) if block else ((K,) if axis == 0 else (N,))
+        s = scale_raw(O.rand_uniform(seed + 10 * j + 2, (int(np.prod(s_shape)),), 0.002, 0.02), O.FLOAT16)
+        wq = O.dequantize_linear(w, O.INT4, (K, N), s, O.FLOAT16, s_shape, None, None, axis)
+        refs.append(O.f16_bits_to_f32(O.matmul(a_raw, wq, O.FLOAT16)))
+        ws.append(b2.QTensor(to_dev(w), O.INT4, (K, N)))
+        ss.append(to_dev(s, torch.float16).reshape(s_shape))
+    ys = b2.DequantizeMatMulGroup()(ta, ws, ss, axis=axis)
+    torch.cuda.synchronize()
+    return [y.float().cpu().numpy().reshape(M, N) for y, N in zip(ys, Ns)], refs, (ta, ws, ss)
+
+
+@pytest.mark.parametrize("M,K,Ns,block,axis", [(1, 4096, (4096, 4096, 4096), 128, 0),
+                                               (8, 4096, (11008, 11008), 128, 0),
+                                               (16, 4096, (4096, 1024, 1024), 128, 0),
+                                               (5, 11008, (4096, 256, 512, 768), 64, 0),
+                                               (3, 1000, (4128, 96), None, 1),
+                                               (2, 512, (64, 4096), None, 0)])
+def test_group_projections_match_the_oracle(b2, cuda, M, K, Ns, block, axis):
+    # the last case (per-row scales) is not the decode kernel's: one call per member
+    ys, refs, _ = group_case(b2, M, K, Ns, block, seed=500 + M + len(Ns), axis=axis)
+    for y, ref in zip(ys, refs):
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], rel_l2(y, ref)
+
+
+def test_group_of_one_is_the_single_call(b2, cuda):
+    # one member: the same decode plan and launch as DequantizeMatMul, bit for bit
+    ys, refs, (ta, ws, ss) = group_case(b2, 1, 4096, (11008,), 128, seed=611)
+    y1 = b2.DequantizeMatMul()(ta, ws[0], ss[0], None, axis=0)
+    torch.cuda.synchronize()
+    assert np.array_equal(ys[0], y1.float().cpu().numpy().reshape(1, 11008))
+
+
+@pytest.mark.parametrize("M", [24, 64])
+def test_group_beyond_the_decode_kernel_runs_each_member(b2, cuda, M):
+    ys, refs, _ = group_case(b2, M, 4096, (4096, 1024), 128, seed=700 + M)
+    for y, ref in zip(ys, refs):
+        assert rel_l2(y, ref) <= TOL[O.FLOAT16], rel_l2(y, ref)
+
+
+def test_group_rejects_a_bad_member_count(b2, cuda):
+    from onnx_light_b200 import _capi as capi
+    a = torch.zeros((1, 64), dtype=torch.float16, device="cuda")
+    ad = capi.Desc(a.data_ptr(), O.FLOAT16, (1, 64))
+    for count in (0, 5):
+        rc = capi.lib().b2_dequantize_matmul_group(count, ad.ref, ad.ref, ad.ref, 0, ad.ref, None,
+                                                   None, capi.stream_ptr())
+        assert rc == capi.B2_ERR_INVALID_ARGUMENT
