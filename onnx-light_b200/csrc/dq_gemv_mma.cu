@@ -63,10 +63,12 @@ __device__ int g_gemv_mma_status;
 namespace {
 
 constexpr int kPeerMax = 8;
-#ifndef GM_GROUP_MAX
-#define GM_GROUP_MAX 4
-#endif
-constexpr int kGroupMax = GM_GROUP_MAX; // projections of one launch that share the activations
+// Projections of one launch that share the activations.  The kernel is
+// instantiated per count NP so that its parameters (NP weight and scale
+// tensor maps, NP output descriptions) stay as small as the call needs: the
+// launch of a 4096 x 4096 decode projection measured 6.9 us with one slot
+// and 7.4 us with four (about 0.15 us per 400 bytes of parameters).
+constexpr int kGroupMax = 4;
 constexpr int GM_TN = 256;                         // columns per tile (128 packed bytes / row)
 constexpr int GM_TK = 128;                         // weight rows per stage
 #ifndef GM_RING
@@ -92,23 +94,22 @@ constexpr uint32_t GM_ONES = 0x3c003c00u;          // (1.0, 1.0) in fp16
 constexpr int kGroupsThreshold = GM_GROUPS_THRESHOLD; // stages per CTA up to which G = 1
 
 // The weight and scale tensor maps of each projection of the launch.
-struct GmMaps {
-  CUtensorMap w[kGroupMax];
-  CUtensorMap s[kGroupMax];
+template <int NP> struct GmMaps {
+  CUtensorMap w[NP];
+  CUtensorMap s[NP];
 };
 
-struct GmArgs {
+template <int NP> struct GmArgs {
   float *partials;
   uint32_t *counters;
   int M, K;
-  // Projections of the launch (nprob >= 1; all read the same activations, K,
+  // Projections of the launch (NP >= 1; all read the same activations, K,
   // weight type and scale layout): projection p owns the 256-column tiles
   // tile_end[p - 1] .. tile_end[p] - 1 of the launch's tile numbering, has
   // Np[p] columns and writes y[p] (row stride ldy[p]).
-  int nprob;
-  int tile_end[kGroupMax];
-  int Np[kGroupMax];
-  __half *y[kGroupMax];
+  int tile_end[NP];
+  int Np[NP];
+  __half *y[NP];
   int ntiles, kunits, units, grid;
   int block;     // scale block along K (0: one scale row for all K)
   int srows;     // scale rows loaded per stage (0: per-tensor scale)
@@ -124,8 +125,8 @@ struct GmArgs {
   // call, then publishes its own completion (a generation number) in every
   // rank's flag array.
   int world, rank;
-  int64_t ldy[kGroupMax], col_off[kGroupMax];
-  __half *peer_y[kGroupMax][kPeerMax];
+  int64_t ldy[NP], col_off[NP];
+  __half *peer_y[NP][kPeerMax];
   uint32_t *peer_flags[kPeerMax];
   uint32_t *pctr; // this rank's [0] CTA arrivals, [1] generation
   int wait_input; // wait for every rank's previous call before reading a
@@ -213,16 +214,19 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   return v;
 }
 // Projection of a launch tile, and its first tile.
-__device__ __forceinline__ int prob_of(const GmArgs &g, int tile) {
+template <int NP> __device__ __forceinline__ int prob_of(const GmArgs<NP> &g, int tile) {
   int p = 0;
 #pragma unroll
-  for (int i = 0; i < kGroupMax - 1; ++i) p += (i < g.nprob - 1 && tile >= g.tile_end[i]) ? 1 : 0;
+  for (int i = 0; i < NP - 1; ++i) p += tile >= g.tile_end[i] ? 1 : 0;
   return p;
 }
-__device__ __forceinline__ int prob_first_tile(const GmArgs &g, int p) { return p ? g.tile_end[p - 1] : 0; }
+template <int NP> __device__ __forceinline__ int prob_first_tile(const GmArgs<NP> &g, int p) {
+  return p ? g.tile_end[p - 1] : 0;
+}
 // Two output values (columns col, col + 1 of row m of projection p) to its y,
 // or to every rank's full buffer when the output is column-sharded.
-__device__ __forceinline__ void store_h2(const GmArgs &g, int p, int64_t m, int64_t col, __half2 v) {
+template <int NP>
+__device__ __forceinline__ void store_h2(const GmArgs<NP> &g, int p, int64_t m, int64_t col, __half2 v) {
   if (g.world <= 1) {
     *reinterpret_cast<__half2 *>(g.y[p] + m * g.ldy[p] + col) = v;
     return;
@@ -302,10 +306,10 @@ __device__ __forceinline__ void k16_step(const uint8_t *wst, const uint8_t *ast,
 // stage; G = 4: one warp pair per stage, 128 rows -- fewest epilogues).
 // KS = k16 steps per scale block inside a slab (the slab's rows / 16 when the
 // block is at least a slab), fixed at compile time so the steps unroll.
-template <int NT, int G, int KS>
+template <int NT, int G, int KS, int NP>
 __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
-    dq_gemv_mma(const __grid_constant__ GmMaps maps, const __grid_constant__ CUtensorMap map_a,
-                const __grid_constant__ GmArgs g) {
+    dq_gemv_mma(const __grid_constant__ GmMaps<NP> maps, const __grid_constant__ CUtensorMap map_a,
+                const __grid_constant__ GmArgs<NP> g) {
   using L = GmSmem<NT>;
   extern __shared__ uint8_t dsm[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
@@ -339,7 +343,7 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     tc::fence_barrier_init();
   }
   if (warp == GM_CONSUMERS && lane == 0) {
-    for (int q = 0; q < g.nprob; ++q) {
+    for (int q = 0; q < NP; ++q) {
       tc::prefetch_tensormap(&maps.w[q]);
       if (g.srows) tc::prefetch_tensormap(&maps.s[q]);
     }
@@ -810,10 +814,11 @@ MmaPlan mma_plan(const DqMmParams *ps, int count) {
   return m;
 }
 
-template <int NT, int G, int KS>
-int launch_mma(const DqMmParams *ps, int count, const MmaPlan &m, void *workspace, cudaStream_t st) {
+template <int NT, int G, int KS, int NP>
+int launch_mma(const DqMmParams *ps, const MmaPlan &m, void *workspace, cudaStream_t st) {
+  constexpr int count = NP;
   const DqMmParams &p = ps[0];
-  GmMaps maps;
+  GmMaps<NP> maps;
   memset(&maps, 0, sizeof(maps));
   CUtensorMap map_a;
   for (int i = 0; i < count; ++i) {
@@ -845,12 +850,11 @@ int launch_mma(const DqMmParams *ps, int count, const MmaPlan &m, void *workspac
                              CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  GmArgs a{};
+  GmArgs<NP> a{};
   a.counters = static_cast<uint32_t *>(workspace);
   a.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kCounterBytes);
   a.M = (int)p.M;
   a.K = (int)p.K;
-  a.nprob = count;
   a.world = p.world > 1 ? p.world : 1;
   a.rank = p.rank;
   for (int i = 0; i < count; ++i) {
@@ -878,7 +882,7 @@ int launch_mma(const DqMmParams *ps, int count, const MmaPlan &m, void *workspac
   a.cq = m.cq;
   a.cr = m.cr;
   a.wait_ns = kWaitNs;
-  auto kern = dq_gemv_mma<NT, G, KS>;
+  auto kern = dq_gemv_mma<NT, G, KS, NP>;
   const size_t smem = GmSmem<NT>::kDynamic;
   B2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   cudaLaunchConfig_t cfg = {};
@@ -947,22 +951,34 @@ bool dq_mma_group_eligible(const DqMmParams *ps, int count) {
 
 size_t dq_mma_group_workspace(const DqMmParams *ps, int count) { return mma_plan(ps, count).ws; }
 
+// One instance per (activation tiles, stage groups, k16 steps per scale
+// block) of the plan and member count.
+template <int NT, int G, int KS>
+int launch_np(const DqMmParams *ps, int count, const MmaPlan &m, void *workspace, cudaStream_t st) {
+  switch (count) {
+  case 1: return launch_mma<NT, G, KS, 1>(ps, m, workspace, st);
+  case 2: return launch_mma<NT, G, KS, 2>(ps, m, workspace, st);
+  case 3: return launch_mma<NT, G, KS, 3>(ps, m, workspace, st);
+  default: return launch_mma<NT, G, KS, 4>(ps, m, workspace, st);
+  }
+}
+
 int dq_mma_launch_group(const DqMmParams *ps, int count, void *workspace, cudaStream_t st) {
   const MmaPlan m = mma_plan(ps, count);
   if (m.ws && workspace == nullptr) B2_FAIL(B2_ERR_WORKSPACE, "workspace of %zu bytes required", m.ws);
   if (m.groups == 1) // 32-row slabs: scale blocks are 32 rows or more
-    return m.nt == 1 ? launch_mma<1, 1, 2>(ps, count, m, workspace, st)
-                     : launch_mma<2, 1, 2>(ps, count, m, workspace, st);
+    return m.nt == 1 ? launch_np<1, 1, 2>(ps, count, m, workspace, st)
+                     : launch_np<2, 1, 2>(ps, count, m, workspace, st);
   // 128-row slabs: k16 steps per scale block
   const int ks = (m.block == 0 || m.block >= GM_TK) ? 8 : m.block / 16;
   if (m.nt == 1) {
-    if (ks == 2) return launch_mma<1, 4, 2>(ps, count, m, workspace, st);
-    if (ks == 4) return launch_mma<1, 4, 4>(ps, count, m, workspace, st);
-    return launch_mma<1, 4, 8>(ps, count, m, workspace, st);
+    if (ks == 2) return launch_np<1, 4, 2>(ps, count, m, workspace, st);
+    if (ks == 4) return launch_np<1, 4, 4>(ps, count, m, workspace, st);
+    return launch_np<1, 4, 8>(ps, count, m, workspace, st);
   }
-  if (ks == 2) return launch_mma<2, 4, 2>(ps, count, m, workspace, st);
-  if (ks == 4) return launch_mma<2, 4, 4>(ps, count, m, workspace, st);
-  return launch_mma<2, 4, 8>(ps, count, m, workspace, st);
+  if (ks == 2) return launch_np<2, 4, 2>(ps, count, m, workspace, st);
+  if (ks == 4) return launch_np<2, 4, 4>(ps, count, m, workspace, st);
+  return launch_np<2, 4, 8>(ps, count, m, workspace, st);
 }
 
 int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
