@@ -32,17 +32,25 @@
 //
 // Work split ("stream-K"): the weight is cut into units of 128 rows x 256
 // columns (16 KB packed, one pipeline stage), numbered tile-major (tile = 256
-// columns); the grid's CTAs (one per SM) take equal contiguous ranges of units,
+// columns); the grid's CTAs take equal contiguous ranges of units,
 // so every SM streams the same number of bytes whatever the shape.  A tile
 // covered by one CTA is written directly; a tile shared by several CTAs is
 // finished by the last one to arrive, which sums the fp32 partials in CTA
 // order (deterministic).
 //
-// Pipeline: one producer warp fills an 8-stage ring with TMA (packed weights
+// Pipeline: one producer warp fills a 4-stage ring with TMA (packed weights
 // 128 x 128 bytes with the 128-byte swizzle, the activation slice 128 x M in
-// two swizzled boxes, the stage's scale rows).  Eight consumer warps form four
-// groups of two (one per 128-column half); group j consumes stages j, j + 4,
-// ..., so four stages are being multiplied while four are in flight.  Before
+// two swizzled boxes, the stage's scale rows).  Four consumer warps, two per
+// 128-column half, take every stage together (64 rows each) or, with more
+// stages per CTA, form two groups of two that take alternate whole stages.
+// A CTA holds about 90 KB of shared memory and 160 threads, so two fit on an
+// SM: a launch of few units per CTA runs one CTA per SM and leaves the second
+// slot to the next launch on the stream, whose CTAs start (programmatic
+// dependent launch) and load their first weights while this one finishes
+// (4096 x 4096: 6.8 -> 5.8 us per launch against one CTA of eight consumer
+// warps and an 8-stage ring per SM); a launch of many units (8 or more per
+// SM, tiles enough for at most 8 CTAs per tile) runs two CTAs per SM, whose
+// rings together keep 8 stages per SM in flight.  Before
 // waiting on the kernel launched ahead of it (programmatic dependent launch),
 // each CTA asks the TMA unit to prefetch its whole weight range into L2: the
 // prefetch changes no value (L2 is the point of coherence), so it is safe
@@ -72,16 +80,16 @@ constexpr int kGroupMax = 4;
 constexpr int GM_TN = 256;                         // columns per tile (128 packed bytes / row)
 constexpr int GM_TK = 128;                         // weight rows per stage
 #ifndef GM_RING
-#define GM_RING 8
+#define GM_RING 4
 #endif
 #ifndef GM_CTAS_PER_SM
-#define GM_CTAS_PER_SM 1
-#endif
-#ifndef GM_GRID_PER_SM
-#define GM_GRID_PER_SM GM_CTAS_PER_SM
+#define GM_CTAS_PER_SM 2
 #endif
 constexpr int GM_STAGES = GM_RING;                 // ring depth
-constexpr int GM_QUADS = 4;                        // consumer warps per column half
+#ifndef GM_QUADS_N
+#define GM_QUADS_N 2
+#endif
+constexpr int GM_QUADS = GM_QUADS_N;               // consumer warps per column half
 constexpr int GM_CONSUMERS = 2 * GM_QUADS;         // consumer warps
 constexpr int GM_THREADS = (GM_CONSUMERS + 1) * 32;
 constexpr uint32_t GM_W_BYTES = GM_TK * GM_TN / 2; // 16 KB
@@ -520,8 +528,8 @@ __global__ void __launch_bounds__(GM_THREADS, GM_CTAS_PER_SM)
     }
 
     // ------------------------ end of a tile segment ------------------------
-    // Sum the four groups of each column half in group order, in one round:
-    // groups 1..3 leave their sums in shared memory, group 0 adds them.
+    // Sum the warp groups of each column half in group order, in one round:
+    // groups 1.. leave their sums in shared memory, group 0 adds them.
     consumers_sync();
     if (quad > 0) {
       float *r = red + (size_t)((quad - 1) * 2 + wn) * 32 * NT * 32;
@@ -776,7 +784,17 @@ MmaPlan mma_plan(const DqMmParams *ps, int count) {
   }
   m.kunits = (int)((p.K + GM_TK - 1) / GM_TK);
   m.units = m.ntiles * m.kunits;
-  m.grid = std::min(m.units, sm_count() * GM_GRID_PER_SM);
+  // One CTA per SM (the second slot is the next launch's), or two for a
+  // long launch whose tiles are wide enough that no tile merges more than 8
+  // slices (the merge reads every slice's partial).
+  const int sms = sm_count();
+#ifndef GM_GRID_RULE
+#define GM_GRID_RULE 0
+#endif
+  bool two = m.units >= 8 * sms && 4 * m.ntiles >= sms;
+  if (GM_GRID_RULE == 1) two = m.units >= 2 * sms;
+  if (GM_GRID_RULE == 2 && p.M <= 4) two = m.units >= 2 * sms;
+  m.grid = std::min(m.units, sms * (two ? GM_CTAS_PER_SM : 1));
   // Up to one tile per CTA: split each tile's K range among whole CTAs (a
   // CTA never straddles two tiles, and each tile's first CTA merges), which
   // takes one merge per tile off the critical path of stream-K.  Kept only
@@ -793,7 +811,7 @@ MmaPlan mma_plan(const DqMmParams *ps, int count) {
   // Stages per CTA below about 2 per stage group leave groups idle: put all
   // warps on every stage instead.
   const int per_cta = m.aligned ? (m.kunits + m.cq - 1) / m.cq : (m.units + m.grid - 1) / m.grid;
-  m.groups = per_cta <= kGroupsThreshold ? 1 : 4;
+  m.groups = per_cta <= kGroupsThreshold ? 1 : GM_QUADS;
   if (p.slayout == kScaleTensor) {
     m.srows = 0;
   } else if (p.slayout == kScaleAxis1) {
@@ -972,13 +990,13 @@ int dq_mma_launch_group(const DqMmParams *ps, int count, void *workspace, cudaSt
   // 128-row slabs: k16 steps per scale block
   const int ks = (m.block == 0 || m.block >= GM_TK) ? 8 : m.block / 16;
   if (m.nt == 1) {
-    if (ks == 2) return launch_np<1, 4, 2>(ps, count, m, workspace, st);
-    if (ks == 4) return launch_np<1, 4, 4>(ps, count, m, workspace, st);
-    return launch_np<1, 4, 8>(ps, count, m, workspace, st);
+    if (ks == 2) return launch_np<1, GM_QUADS, 2>(ps, count, m, workspace, st);
+    if (ks == 4) return launch_np<1, GM_QUADS, 4>(ps, count, m, workspace, st);
+    return launch_np<1, GM_QUADS, 8>(ps, count, m, workspace, st);
   }
-  if (ks == 2) return launch_np<2, 4, 2>(ps, count, m, workspace, st);
-  if (ks == 4) return launch_np<2, 4, 4>(ps, count, m, workspace, st);
-  return launch_np<2, 4, 8>(ps, count, m, workspace, st);
+  if (ks == 2) return launch_np<2, GM_QUADS, 2>(ps, count, m, workspace, st);
+  if (ks == 4) return launch_np<2, GM_QUADS, 4>(ps, count, m, workspace, st);
+  return launch_np<2, GM_QUADS, 8>(ps, count, m, workspace, st);
 }
 
 int dq_mma_launch(const DqMmParams &p, void *workspace, cudaStream_t st) {
