@@ -44,13 +44,10 @@
 // 128-column half, take every stage together (64 rows each) or, with more
 // stages per CTA, form two groups of two that take alternate whole stages.
 // A CTA holds about 90 KB of shared memory and 160 threads, so two fit on an
-// SM: a launch of few units per CTA runs one CTA per SM and leaves the second
-// slot to the next launch on the stream, whose CTAs start (programmatic
-// dependent launch) and load their first weights while this one finishes
-// (4096 x 4096: 6.8 -> 5.8 us per launch against one CTA of eight consumer
-// warps and an 8-stage ring per SM); a launch of many units (8 or more per
-// SM, tiles enough for at most 8 CTAs per tile) runs two CTAs per SM, whose
-// rings together keep 8 stages per SM in flight.  Before
+// SM, and a launch of two or more units per SM runs two per SM: their rings
+// keep 8 stages per SM in flight, and as CTAs finish, the CTAs of the next
+// launch on the stream take their slots (programmatic dependent launch) and
+// load their first weights while this launch ends.  Before
 // waiting on the kernel launched ahead of it (programmatic dependent launch),
 // each CTA asks the TMA unit to prefetch its whole weight range into L2: the
 // prefetch changes no value (L2 is the point of coherence), so it is safe
@@ -784,16 +781,13 @@ MmaPlan mma_plan(const DqMmParams *ps, int count) {
   }
   m.kunits = (int)((p.K + GM_TK - 1) / GM_TK);
   m.units = m.ntiles * m.kunits;
-  // One CTA per SM (the second slot is the next launch's), or two for a
-  // long launch whose tiles are wide enough that no tile merges more than 8
-  // slices (the merge reads every slice's partial).
+  // Two CTAs per SM once there are two units per CTA: in a chain of decode
+  // launches the CTAs of the next launch take the slots that this launch's
+  // CTAs free as they finish (config 3, grouped step: 45.7 us at B = 1 and
+  // 55.7 us at B = 8 against 48.6 / 56.6 us with two CTAs per SM only for
+  // launches of 8 units per SM or more).
   const int sms = sm_count();
-#ifndef GM_GRID_RULE
-#define GM_GRID_RULE 0
-#endif
-  bool two = m.units >= 8 * sms && 4 * m.ntiles >= sms;
-  if (GM_GRID_RULE == 1) two = m.units >= 2 * sms;
-  if (GM_GRID_RULE == 2 && p.M <= 4) two = m.units >= 2 * sms;
+  const bool two = m.units >= 2 * sms;
   m.grid = std::min(m.units, sms * (two ? GM_CTAS_PER_SM : 1));
   // Up to one tile per CTA: split each tile's K range among whole CTAs (a
   // CTA never straddles two tiles, and each tile's first CTA merges), which
