@@ -129,6 +129,40 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Three-way maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// Element-wise a * b + c, a + b and a - b on two fp32 lanes (one packed
+// instruction each on sm_100; the same IEEE operation per element).
+__device__ __forceinline__ uint64_t f2pack(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ float2 f2unpack(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(PT_THREADS, 1)
     attn_prefill_tc(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -326,7 +360,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
         load_scores(r0, v, 0, g, need_mask, key0 + half * 64, pos);
         load_scores(r1, v, 32, g, need_mask, key0 + half * 64 + 32, pos);
 #pragma unroll
-        for (int e = 0; e < 64; ++e) mx = fmaxf(mx, v[e]);
+        for (int e = 0; e < 64; e += 2) mx = max3f(mx, v[e], v[e + 1]);
         mx *= vk; // vk > 0: the maximum of the scaled scores
       }
       float *rm = red + (j & 1) * 2 * PT_M;
@@ -364,8 +398,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       // pass 2: P for this half (keys half * 64 .. + 63) over the S buffer
       // the scores came from (every thread of the row has read its S half
       // before the barrier above); masked scores are -inf and give 0
-      const float nm = -m_ref;
-      float ls = 0.0f;
+      // pairs of keys on the packed fp32x2 pipe: the exponent's argument, the
+      // running sums (two lanes, added at the end) and the bf16 low parts
+      const uint64_t nm2 = f2pack(-m_ref, -m_ref), vk2 = f2pack(vk, vk);
+      uint64_t ls2 = f2pack(0.0f, 0.0f);
       const uint32_t p_col = tmem + lane_off + (j & 1) * PT_N + half * 32;
 #pragma unroll
       for (int c = 0; c < 2; ++c) { // 32 keys (16 packed columns) at a time
@@ -373,20 +409,25 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
         uint32_t pl[std::is_same<T, __half>::value ? 1 : 16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          const float p0 = ex2(fmaf(v[c * 32 + 2 * u], vk, nm));
-          const float p1 = ex2(fmaf(v[c * 32 + 2 * u + 1], vk, nm));
-          ls += p0 + p1;
+          const float2 t = f2unpack(ffma2(f2pack(v[c * 32 + 2 * u], v[c * 32 + 2 * u + 1]), vk2, nm2));
+          const float p0 = ex2(t.x), p1 = ex2(t.y);
+          const uint64_t pp = f2pack(p0, p1);
+          ls2 = fadd2(ls2, pp);
           ph[u] = pack2<T>(p0, p1);
           if constexpr (!std::is_same<T, __half>::value) {
-            const float h0 = __uint_as_float(ph[u] << 16), h1 = __uint_as_float(ph[u] & 0xffff0000u);
-            pl[u] = pack2<T>(p0 - h0, p1 - h1);
+            const float2 lo = f2unpack(fsub2(pp, f2pack(__uint_as_float(ph[u] << 16),
+                                                        __uint_as_float(ph[u] & 0xffff0000u))));
+            pl[u] = pack2<T>(lo.x, lo.y);
           }
         }
         tc::tmem_st16(p_col + c * 16, ph);
         if constexpr (!std::is_same<T, __half>::value) tc::tmem_st16(p_col + 64 + c * 16, pl);
       }
       tc::tmem_st_wait();
-      l_part += ls;
+      {
+        const float2 l2 = f2unpack(ls2);
+        l_part += l2.x + l2.y;
+      }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[j & 1]);
