@@ -785,9 +785,11 @@ MmaPlan mma_plan(const DqMmParams *ps, int count) {
   // launches the CTAs of the next launch take the slots that this launch's
   // CTAs free as they finish (config 3, grouped step: 45.7 us at B = 1 and
   // 55.7 us at B = 8 against 48.6 / 56.6 us with two CTAs per SM only for
-  // launches of 8 units per SM or more).
+  // launches of 8 units per SM or more) -- unless that would split a tile
+  // among more than 20 CTAs, whose merge reads every slice's partial (the
+  // narrow column shards of a multi-GPU layer).
   const int sms = sm_count();
-  const bool two = m.units >= 2 * sms;
+  const bool two = m.units >= 2 * sms && 2 * sms <= 20 * m.ntiles;
   m.grid = std::min(m.units, sms * (two ? GM_CTAS_PER_SM : 1));
   // Up to one tile per CTA: split each tile's K range among whole CTAs (a
   // CTA never straddles two tiles, and each tile's first CTA merges), which
