@@ -703,12 +703,13 @@ static int wbits(int dt) {
   return 0;
 }
 
-// Kernel selection.  ONNXL_B200_DQ_KERNEL=tc|gemv|simt|mma|f32 forces one
-// family (tests use it to exercise every kernel on the same shapes); the
-// default picks the register-MMA decode kernel for int4 / fp16 up to 16 rows,
-// the tensor-core kernel for other 16-bit activations, the CUDA-core GEMV for
-// one or two rows, dq_gemm_f32 for FLOAT activations with integer weights,
-// and the generic CUDA-core GEMM for the rest.
+// Kernel selection.  ONNXL_B200_DQ_KERNEL=tc|gemv|simt|mma|f32|x|n|c|cx
+// forces one family (tests use it to exercise every kernel on the same
+// shapes); the default picks, for int4 / fp16, the register-MMA decode
+// kernels up to 64 rows (split-K magic-number kernel, or narrow tiles, by the
+// rule below), the tensor-core kernel for other 16-bit activations, the
+// CUDA-core GEMV for one or two rows, dq_gemm_f32 for FLOAT activations with
+// integer weights, and the generic CUDA-core GEMM for the rest.
 enum DqPath { kPathAuto = 0, kPathTc = 1, kPathGemv = 2, kPathSimt = 3, kPathMma = 4, kPathF32 = 5,
               kPathX = 6, kPathN = 7, kPathC = 8, kPathCX = 9 };
 

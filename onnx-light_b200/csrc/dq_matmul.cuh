@@ -72,7 +72,7 @@ bool dq_x_eligible(const DqMmParams &p); // shape/type constraints (pointer alig
 size_t dq_x_workspace(const DqMmParams &p);
 int dq_x_launch(const DqMmParams &p, void *workspace, cudaStream_t stream);
 
-// Decode path on narrow column tiles without split-K (dq_gemv_n.cu): M <= 32,
+// Decode path on narrow column tiles without split-K (dq_gemv_n.cu): M <= 64,
 // INT4/UINT4 weights, FLOAT16 scales, activations and output; no workspace.
 bool dq_n_eligible(const DqMmParams &p); // shape/type constraints (pointer alignment: dq_mma_aligned)
 int dq_n_launch(const DqMmParams &p, cudaStream_t stream);
