@@ -77,6 +77,29 @@ def test_workspace_query_protocol(b2):
     assert rc in (_capi.B2_OK, _capi.B2_ERR_CUDA)
 
 
+def test_group_call_validates_on_host(b2):
+    """The group entry points check the member count, the arrays and each
+    member's types before touching the device."""
+    from onnx_light_b200 import _capi
+    lib = _capi.lib()
+    a = _capi.Desc(0, _capi.FLOAT16, (1, 256))
+    ws = _capi.DescArray([_capi.Desc(0, _capi.INT4, (256, 64)) for _ in range(2)])
+    ss = _capi.DescArray([_capi.Desc(0, _capi.FLOAT16, (2, 64)) for _ in range(2)])
+    ys = _capi.DescArray([_capi.Desc(0, _capi.FLOAT16, (1, 64)) for _ in range(2)])
+    for count in (0, 5):
+        assert lib.b2_dequantize_matmul_group(count, a.ref, ws.ref, ss.ref, 0, ys.ref, None, None,
+                                              None) == _capi.B2_ERR_INVALID_ARGUMENT
+    assert lib.b2_dequantize_matmul_group(2, a.ref, None, ss.ref, 0, ys.ref, None, None,
+                                          None) == _capi.B2_ERR_INVALID_ARGUMENT
+    # a member whose scale is not FLOAT / FLOAT16 fails like b2_dequantize_matmul
+    bad = _capi.DescArray([_capi.Desc(0, _capi.FLOAT16, (2, 64)), _capi.Desc(0, _capi.INT32, (2, 64))])
+    with pytest.raises(ValueError):
+        _capi.check(lib.b2_dequantize_matmul_group(2, a.ref, ws.ref, bad.ref, 0, ys.ref, None, None,
+                                                   None))
+    assert lib.b2_dequantize_matmul_group_peer(2, a.ref, ws.ref, ss.ref, 0, ys.ref, None, None, None,
+                                               None) == _capi.B2_ERR_INVALID_ARGUMENT
+
+
 def test_dispatch_table_rules(b2):
     t = b2.KernelDispatchTable()
     from onnx_light_b200 import dispatch as d
